@@ -1,0 +1,299 @@
+"""Benchmark: batch-1 decode of the Llama-2-7B-shape Q4_0 model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload llama7b_q4_0|llama7b_q8_0|stories_f32]
+
+One step = one decode token: every layer's rmsnorm + quantize + qkv matvec +
+RoPE, attention over the KV cache, wo, w1/w3 + SwiGLU, w2, then the classifier
+and the greedy argmax (cats_llama2_transformer, llm/catseye_llm.h:1625-1772).
+Synthetic weights N(0, 0.02) quantized per 32-block (generated on the device);
+the 3.7 GB of weights exceed the 126 MB L2, so every step streams them from
+HBM (no L2 flush needed).
+
+value : tokens/s with the step replayed as a CUDA graph, the argmax fed back on
+        the device (inputs resident in HBM), CUDA events on the model's stream.
+e2e   : tokens/s through the public C API cats_gpu_llama2_transformer(token,
+        pos, m, logits) — token/pos copied in, the logits copied out, every step.
+roofline : the dominant kernel (the fused w1/w3 Q4_0 matvec) timed alone with
+        CUDA events: reference-layout weight bytes + x + out per launch / time.
+cpu_baseline : the reference's own CPU step (oracle/_ref, all cores) on a
+        bounded sample (1- and 2-layer models of the same shapes, extrapolated).
+
+--impl reference times only that CPU reference on the same workload.
+With torchrun (N > 1) every rank decodes its own replica (no collective on
+the data path yet): value = sum over ranks, time = max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "llama7b_q4_0": ("LLAMA2_7B", 2),
+    "llama7b_q8_0": ("LLAMA2_7B", 8),
+    "stories_f32": ("STORIES_F32", 0),
+}
+PROMPT = 8
+SEED = 20241201
+
+
+def cfg_for(workload):
+    from catseye_b200 import llm
+    name, t = WORKLOADS[workload]
+    return getattr(llm, name).with_type(t)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.device = device
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        try:
+            for line in open(self.f.name):
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        finally:
+            os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if ws == 1:
+        return None, 0, 1, int(os.environ.get("LOCAL_RANK", "0"))
+    import datetime
+    import torch
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist, rank, ws, local
+
+
+# ------------------------------------------------------------- CPU reference
+def cpu_reference(cfg, kind="reference", samples=3):
+    """Time the reference's own decode step on the host cores on a bounded sample.
+
+    Two models with the workload's shapes but 1 and 2 layers (classifier
+    included) are timed; per-token time = t1 + (L - 1) * (t2 - t1)."""
+    from dataclasses import replace
+    from oracle.cpu import Oracle, Reference, ref_available
+    from oracle.models import ModelWeights
+    orc = Oracle()
+    use_ref = kind == "reference" and ref_available("llm_allcores") and cfg.wtype in (0, 2)
+    times = {}
+    for L in (1, 2):
+        c = replace(cfg, n_layers=L, seq_len=64)
+        mw = ModelWeights(c, SEED, orc)
+        m = Reference("llm_allcores").llm(mw) if use_ref else orc.llm(mw)
+        m.step(1, 0)
+        ts = []
+        for pos in range(1, 1 + samples):
+            t0 = time.perf_counter()
+            m.step(pos, pos)
+            ts.append(time.perf_counter() - t0)
+        times[L] = min(ts)
+        del m, mw
+    t_layer = max(times[2] - times[1], 1e-9)
+    t_tok = times[1] + (cfg.n_layers - 1) * t_layer
+    cores = os.cpu_count()
+    return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": cores,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"1- and 2-layer models of the same shapes (+classifier), best of {samples} steps each at "
+                      f"pos 1-{samples}; per token = t1 + {cfg.n_layers - 1} x (t2 - t1) = {t_tok * 1e3:.1f} ms"}
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, dist, rank, ws, local):
+    import torch
+    from catseye_b200 import _lib, llm
+    _lib.init(local)
+    torch.cuda.set_device(local)
+    cfg = cfg_for(args.workload)
+    m = llm.GpuLLM(cfg)
+    m.init_random(SEED)
+    stream = torch.cuda.ExternalStream(m.stream)
+    rng = np.random.default_rng(SEED + 1)
+    prompt = rng.integers(0, cfg.vocab, PROMPT)
+    for pos, tok in enumerate(prompt):            # prompt forcing (untimed)
+        m.step(int(tok), pos)
+    pos0 = PROMPT
+    assert pos0 + args.warmup + args.steps + args.e2e_steps <= cfg.seq_len
+    m.set_position(int(np.argmax(m.logits())), pos0)
+    m.enqueue(args.warmup)
+    m.synchronize()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        m.enqueue(args.steps)
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = clk.summary()
+    pos = pos0 + args.warmup + args.steps
+
+    # e2e through the public API: host token in, host logits out, every step
+    tok = m.next_token()
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        lg = m.step(tok, pos + i)
+        tok = int(np.argmax(lg))
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    # dominant kernel: the fused w1/w3 matvec (largest bytes per launch)
+    kms, kbytes = m.time_matvec(2, reps=3)
+    kinds = {}
+    for k, name in enumerate(("qkv", "wo", "w13", "w2", "cls")):
+        a, b = m.time_matvec(k, reps=2)
+        kinds[name] = {"us_per_launch": round(a * 1e3, 2), "gbs": round(b / (a * 1e-3) / 1e9, 1)}
+    wbytes = m.weight_bytes()
+    m.close()
+    return ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="llama7b_q4_0", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        cfg = cfg_for(args.workload)
+        for _ in range(args.warmup and 0):
+            pass
+        cb = cpu_reference(cfg, "reference", samples=max(3, min(args.steps, 5)))
+        line = {"impl": "reference", "metric": "decode tok/s (batch 1)", "value": round(cb["value"], 3),
+                "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(1e3 / cb["value"], 3), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)",
+                                               8: "q8_0 x q8"}[cfg.wtype],
+                "data": "synthetic", "config": {"workload": args.workload, "batch": 1, "prompt": PROMPT},
+                "cpu_baseline": cb,
+                "e2e": {"value": round(cb["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    dist, rank, ws, local = dist_init()
+    ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg = run_ours(args, dist, rank, ws, local)
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = peaks()
+    tok_s = ws * args.steps / (ms * 1e-3)
+    achieved = kbytes / (kms * 1e-3) / 1e9
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "matvec_q4_0_w13_traffic.json")
+    if os.path.exists(tf):
+        traffic = json.load(open(tf)).get("dram_bytes_per_launch")
+    step_bytes = wbytes + cfg.n_layers * 2 * cfg.kv_dim * 4 * (PROMPT + args.warmup + args.steps / 2)
+    line = {
+        "metric": "decode tok/s (batch 1)", "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)", 8: "q8_0 x q8"}[cfg.wtype],
+        "data": "synthetic",
+        "config": {"workload": args.workload, "batch": 1, "prompt": PROMPT, "dim": cfg.dim, "layers": cfg.n_layers,
+                   "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                   "l2": "weights 3.7 GB > 126 MB L2; no flush" if cfg.wtype else "weights 37 MB; L2-resident"},
+        "step_hbm_gbs": round(step_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
+        "step_hbm_frac_of_measured": round(step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4),
+        "roofline": {"bound": "hbm", "kernel": "k_matvec<Q4_0> fused w1/w3 (4096 -> 2x11008)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "bytes_per_launch": int(kbytes), "us_per_launch": round(kms * 1e3, 2)},
+        "kernels": kinds,
+        "e2e": {"value": round(ws * args.e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": cfg.vocab * 4},
+        "gpu_launches": args.steps * (5 * cfg.n_layers + 2),
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference(cfg, "reference")
+    print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,574 @@
+// capi.cu — the C ABI of libcatsgpu.so (include/catsgpu.h).
+//
+// Owns the device, one CUDA stream, the weight registry (host pointer of the
+// caller's cats_tensor.data -> re-laid-out device copy), grow-only staging
+// buffers for the host-pointer drop-ins, and the sticky error status that the
+// void drop-in signatures cannot return.
+#include "../../include/catsgpu.h"
+#include "llm.cuh"
+#include "sgemm.cuh"
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+using namespace cats;
+
+namespace {
+
+struct Reg {
+    int type = 0, n = 0, d = 0;
+    DevWeight W;
+};
+
+struct Ctx {
+    bool init = false;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int last_err = 0;
+    bool strict = false;
+    unsigned printed = 0;
+    int *d_err = nullptr;
+    std::unordered_map<const void *, Reg> weights;
+    void *d_x = nullptr;
+    size_t d_x_cap = 0;
+    float *d_out = nullptr;
+    size_t d_out_cap = 0;
+    float *d_a = nullptr, *d_b = nullptr, *d_c = nullptr, *d_work = nullptr;
+    size_t cap_a = 0, cap_b = 0, cap_c = 0, cap_work = 0;
+};
+
+Ctx g;
+
+const char *err_name(int c)
+{
+    switch (c) {
+    case CATS_OK: return "ok";
+    case CATS_ERR_CUDA: return "CUDA runtime error";
+    case CATS_ERR_ARG: return "invalid argument";
+    case CATS_ERR_NOMEM: return "device out of memory";
+    case CATS_ERR_TIMEOUT: return "device wait timed out";
+    case CATS_ERR_UNSUPPORTED: return "unsupported shape or type";
+    case CATS_ERR_NOT_INIT: return "library not initialised";
+    case CATS_ERR_NCCL: return "collective failed";
+    }
+    return "unknown";
+}
+
+int fail(int code, const char *what, cudaError_t ce = cudaSuccess)
+{
+    g.last_err = code;
+    if (g.strict || !(g.printed & (1u << code))) {
+        g.printed |= 1u << code;
+        fprintf(stderr, "catsgpu: %s: %s%s%s\n", what, err_name(code), ce ? " / " : "", ce ? cudaGetErrorString(ce) : "");
+    }
+    if (g.strict) abort();
+    return code;
+}
+
+int check(cudaError_t e, const char *what)
+{
+    if (e == cudaSuccess) return CATS_OK;
+    return fail(e == cudaErrorMemoryAllocation ? CATS_ERR_NOMEM : CATS_ERR_CUDA, what, e);
+}
+
+bool ensure_init()
+{
+    if (g.init) return true;
+    if (cats_gpu_init(-1) != CATS_OK) return false;
+    return true;
+}
+
+int grow(void **p, size_t *cap, size_t bytes)
+{
+    if (*cap >= bytes) return CATS_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    size_t want = round_up(bytes, 1 << 20);
+    if (cudaMalloc(p, want) != cudaSuccess) return fail(CATS_ERR_NOMEM, "staging buffer");
+    *cap = want;
+    return CATS_OK;
+}
+
+int check_device_error(const char *what)
+{
+    int h = 0;
+    if (cudaMemcpy(&h, g.d_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return fail(CATS_ERR_CUDA, what);
+    if (h) {
+        cudaMemset(g.d_err, 0, 4);
+        return fail(CATS_ERR_TIMEOUT, what);
+    }
+    return CATS_OK;
+}
+
+bool type_ok(int t) { return t == CATS_TYPE_F32 || t == CATS_TYPE_Q4_0 || t == CATS_TYPE_Q8_0; }
+
+int validate_shape(int type, int n, int d)
+{
+    if (n <= 0 || d <= 0) return CATS_ERR_ARG;
+    if (!type_ok(type)) return CATS_ERR_UNSUPPORTED;
+    if (type == CATS_TYPE_F32 ? (n % 4) : (n % 32)) return CATS_ERR_ARG;
+    return CATS_OK;
+}
+
+Reg *lookup(const void *w, int type, int n, int d)
+{
+    auto it = g.weights.find(w);
+    if (it != g.weights.end()) {
+        Reg &r = it->second;
+        if (r.type == type && r.n == n && r.d == d) return &r;
+        cats_gpu_unregister_weight(w);   // same address, new meaning: re-upload
+    }
+    if (cats_gpu_register_weight(w, type, n, d) != CATS_OK) return nullptr;
+    return &g.weights[w];
+}
+
+MatvecArgs args_for(const Reg &r)
+{
+    MatvecArgs a;
+    const WeightLayout &L = r.W.L;
+    a.w = r.W.ptr;
+    a.n = L.n;
+    a.d = L.d;
+    a.R = L.R;
+    a.units = L.units;
+    a.nseg = L.nseg;
+    a.n_tiles = L.n_tiles;
+    a.unit_bytes = L.unit_bytes;
+    a.full_chunk = L.full_chunk;
+    a.last_chunk = L.last_chunk;
+    a.tile_bytes = L.tile_bytes;
+    a.stages = std::max(2, std::min(8, (int)(65536 / round_up(L.full_chunk, 128))));
+    a.err = g.d_err;
+    return a;
+}
+
+void matmul_host(int type, float *xout, void *x, void *w, int n, int d, const char *what)
+{
+    if (!ensure_init()) return;
+    if (!xout || !x || !w) { fail(CATS_ERR_ARG, what); return; }
+    if (int rc = validate_shape(type, n, d)) { fail(rc, what); return; }
+    Reg *r = lookup(w, type, n, d);
+    if (!r) return;
+    const size_t xb = type == CATS_TYPE_F32 ? (size_t)n * 4 : (size_t)(n / 32) * 36;
+    if (grow(&g.d_x, &g.d_x_cap, xb) || grow((void **)&g.d_out, &g.d_out_cap, (size_t)d * 4)) return;
+    if (check(cudaMemcpyAsync(g.d_x, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    MatvecArgs a = args_for(*r);
+    a.xmode = type == CATS_TYPE_F32 ? XM_F32 : XM_Q8_RAW;
+    a.x = g.d_x;
+    a.epi = EPI_STORE;
+    a.out = g.d_out;
+    if (check(launch_matvec(a, 1, type, g.stream, false), what)) return;
+    if (check(cudaMemcpyAsync(xout, g.d_out, (size_t)d * 4, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    if (check(cudaStreamSynchronize(g.stream), what)) return;
+    check_device_error(what);
+}
+
+} // namespace
+
+// ===================================================================== C ABI
+extern "C" {
+
+int cats_gpu_init(int device)
+{
+    if (g.init) return CATS_OK;
+    const char *s = getenv("CATS_GPU_STRICT");
+    g.strict = s && atoi(s) == 1;
+    if (device < 0) {
+        const char *e = getenv("CATS_GPU_DEVICE");
+        device = e ? atoi(e) : 0;
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(CATS_ERR_CUDA, "cats_gpu_init: no CUDA device");
+    if (device >= n) return fail(CATS_ERR_ARG, "cats_gpu_init: device index");
+    if (check(cudaSetDevice(device), "cats_gpu_init")) return g.last_err;
+    cudaDeviceProp prop;
+    if (check(cudaGetDeviceProperties(&prop, device), "cats_gpu_init")) return g.last_err;
+    if (prop.major != 10) return fail(CATS_ERR_UNSUPPORTED, "cats_gpu_init: libcatsgpu needs an sm_100 (B200) device");
+    if (check(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "cats_gpu_init")) return g.last_err;
+    if (check(cudaMalloc(&g.d_err, 4), "cats_gpu_init")) return g.last_err;
+    cudaMemset(g.d_err, 0, 4);
+    g.device = device;
+    g.init = true;
+    return CATS_OK;
+}
+
+void cats_gpu_term(void)
+{
+    if (!g.init) return;
+    cudaStreamSynchronize(g.stream);
+    for (auto &kv : g.weights) if (kv.second.W.ptr) cudaFree(kv.second.W.ptr);
+    g.weights.clear();
+    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err};
+    for (void *b : bufs) if (b) cudaFree(b);
+    g.d_x = nullptr; g.d_out = nullptr; g.d_a = g.d_b = g.d_c = g.d_work = nullptr; g.d_err = nullptr;
+    g.d_x_cap = g.d_out_cap = g.cap_a = g.cap_b = g.cap_c = g.cap_work = 0;
+    cudaStreamDestroy(g.stream);
+    g.stream = nullptr;
+    g.init = false;
+}
+
+int cats_gpu_last_error(void) { return g.last_err; }
+void cats_gpu_clear_error(void) { g.last_err = 0; }
+const char *cats_gpu_error_string(int code) { return err_name(code); }
+
+int cats_gpu_device_error(void)
+{
+    if (!g.init) return 0;
+    int h = 0;
+    cudaMemcpy(&h, g.d_err, 4, cudaMemcpyDeviceToHost);
+    return h;
+}
+
+int cats_gpu_register_weight(const void *w, int type, int n, int d)
+{
+    if (!ensure_init()) return g.last_err;
+    if (!w) return fail(CATS_ERR_ARG, "cats_gpu_register_weight: null weight");
+    if (int rc = validate_shape(type, n, d)) return fail(rc, "cats_gpu_register_weight");
+    auto it = g.weights.find(w);
+    if (it != g.weights.end()) {
+        if (it->second.type == type && it->second.n == n && it->second.d == d) return CATS_OK;
+        cats_gpu_unregister_weight(w);
+    }
+    const size_t bytes = gguf_row_bytes(type, n) * d;
+    uint8_t *stg = nullptr;
+    if (cudaMalloc(&stg, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
+    Reg r;
+    r.type = type; r.n = n; r.d = d;
+    r.W.L = make_layout(type, n, d, 1);
+    int rc = CATS_OK;
+    if (cudaMalloc(&r.W.ptr, r.W.L.total_bytes) != cudaSuccess) rc = fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
+    if (!rc) rc = check(cudaMemcpyAsync(stg, w, bytes, cudaMemcpyHostToDevice, g.stream), "cats_gpu_register_weight");
+    if (!rc) rc = check(launch_repack(stg, r.W.ptr, r.W.L, g.stream), "cats_gpu_register_weight");
+    if (!rc) rc = check(cudaStreamSynchronize(g.stream), "cats_gpu_register_weight");
+    cudaFree(stg);
+    if (rc) { if (r.W.ptr) cudaFree(r.W.ptr); return rc; }
+    g.weights[w] = r;
+    return CATS_OK;
+}
+
+void cats_gpu_unregister_weight(const void *w)
+{
+    auto it = g.weights.find(w);
+    if (it == g.weights.end()) return;
+    cudaStreamSynchronize(g.stream);
+    if (it->second.W.ptr) cudaFree(it->second.W.ptr);
+    g.weights.erase(it);
+}
+
+size_t cats_gpu_weight_device_bytes(const void *w)
+{
+    auto it = g.weights.find(w);
+    return it == g.weights.end() ? 0 : it->second.W.L.total_bytes;
+}
+
+void cats_gpu_matmul_f32(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_F32, xout, x, w, n, d, "cats_gpu_matmul_f32"); }
+void cats_gpu_matmul_q4_0_q8(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_Q4_0, xout, x, w, n, d, "cats_gpu_matmul_q4_0_q8"); }
+void cats_gpu_matmul_q8_0_q8(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_Q8_0, xout, x, w, n, d, "cats_gpu_matmul_q8_0_q8"); }
+
+void cats_gpu_quantize_q8(int8_t *q, float *x, int n)
+{
+    const char *what = "cats_gpu_quantize_q8";
+    if (!ensure_init()) return;
+    if (!q || !x || n <= 0 || n % 32) { fail(CATS_ERR_ARG, what); return; }
+    const size_t xb = (size_t)n * 4, qb = (size_t)(n / 32) * 36;
+    if (grow(&g.d_x, &g.d_x_cap, xb) || grow((void **)&g.d_out, &g.d_out_cap, qb)) return;
+    if (check(cudaMemcpyAsync(g.d_x, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(launch_quantize_q8((int8_t *)g.d_out, (const float *)g.d_x, n, 0, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(q, g.d_out, qb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+static void *dequant_host(int type, void *y, const void *x, int row, int n, const char *what)
+{
+    if (!ensure_init()) return 0;
+    if (!y || !x || row < 0 || n <= 0 || n % 32) { fail(CATS_ERR_ARG, what); return 0; }
+    const size_t rb = gguf_row_bytes(type, n);
+    if (grow(&g.d_x, &g.d_x_cap, rb) || grow((void **)&g.d_out, &g.d_out_cap, (size_t)n * 4)) return 0;
+    const uint8_t *src = static_cast<const uint8_t *>(x) + (size_t)row * rb;
+    if (check(cudaMemcpyAsync(g.d_x, src, rb, cudaMemcpyHostToDevice, g.stream), what)) return 0;
+    if (check(launch_dequantize(type, g.d_out, (const uint8_t *)g.d_x, n, 1, g.stream), what)) return 0;
+    if (check(cudaMemcpyAsync(y, g.d_out, (size_t)n * 4, cudaMemcpyDeviceToHost, g.stream), what)) return 0;
+    check(cudaStreamSynchronize(g.stream), what);
+    return 0;
+}
+
+void *cats_gpu_dequantize_q4_0(void *y, const void *x, int row, int n)
+{ return dequant_host(CATS_TYPE_Q4_0, y, x, row, n, "cats_gpu_dequantize_q4_0"); }
+void *cats_gpu_dequantize_q8_0(void *y, const void *x, int row, int n)
+{ return dequant_host(CATS_TYPE_Q8_0, y, x, row, n, "cats_gpu_dequantize_q8_0"); }
+
+int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q8, void *stream)
+{
+    const char *what = "cats_gpu_matvec_dev";
+    if (!ensure_init()) return g.last_err;
+    auto it = g.weights.find(w);
+    if (it == g.weights.end()) return fail(CATS_ERR_ARG, "cats_gpu_matvec_dev: weight not registered");
+    if (!d_out || !d_x || ((uintptr_t)d_x % 16)) return fail(CATS_ERR_ARG, what);
+    Reg &r = it->second;
+    if (x_is_q8 && r.type == CATS_TYPE_F32) return fail(CATS_ERR_ARG, "cats_gpu_matvec_dev: F32 weight with Q8 input");
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    MatvecArgs a = args_for(r);
+    a.xmode = r.type == CATS_TYPE_F32 ? XM_F32 : (x_is_q8 ? XM_Q8_RAW : XM_Q8_FROM_F32);
+    a.x = d_x;
+    a.epi = EPI_STORE;
+    a.out = d_out;
+    return check(launch_matvec(a, 1, r.type, st, false), what);
+}
+
+int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mode, void *stream)
+{
+    if (!ensure_init()) return g.last_err;
+    if (!d_q || !d_x || n <= 0 || n % 32 || ((uintptr_t)d_x % 16) || ((uintptr_t)d_q % 4))
+        return fail(CATS_ERR_ARG, "cats_gpu_quantize_q8_dev");
+    return check(launch_quantize_q8(d_q, d_x, n, scalar_mode, stream ? (cudaStream_t)stream : g.stream),
+                 "cats_gpu_quantize_q8_dev");
+}
+
+int cats_gpu_dequantize_dev(int type, float *d_y, const void *d_w, int n, int rows, void *stream)
+{
+    if (!ensure_init()) return g.last_err;
+    if (!d_y || !d_w || n <= 0 || n % 32 || rows <= 0 || !type_ok(type)) return fail(CATS_ERR_ARG, "cats_gpu_dequantize_dev");
+    return check(launch_dequantize(type, d_y, (const uint8_t *)d_w, n, rows, stream ? (cudaStream_t)stream : g.stream),
+                 "cats_gpu_dequantize_dev");
+}
+
+// ------------------------------------------------------------------ LLM
+struct cats_gpu_llm {
+    LlmModel m;
+    int *tok_log = nullptr;   // device: argmax ids of generate()
+};
+
+cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg)
+{
+    if (!ensure_init()) return nullptr;
+    if (!cfg || cfg->dim <= 0 || cfg->n_layers <= 0 || cfg->vocab <= 0 || cfg->seq_len <= 0 || !type_ok(cfg->wtype)) {
+        fail(CATS_ERR_ARG, "cats_gpu_llm_create");
+        return nullptr;
+    }
+    LlmConfig c{cfg->dim, cfg->hidden, cfg->n_layers, cfg->n_heads, cfg->n_kv_heads, cfg->vocab, cfg->seq_len,
+                cfg->wtype, cfg->tp_rank, cfg->tp_size > 0 ? cfg->tp_size : 1};
+    if (c.tp_size != 1) { fail(CATS_ERR_UNSUPPORTED, "cats_gpu_llm_create: tensor parallel"); return nullptr; }
+    cats_gpu_llm *h = new cats_gpu_llm();
+    int rc = llm_alloc(&h->m, c);
+    if (rc == CATS_OK && cudaMalloc(&h->tok_log, (size_t)(c.seq_len + 1) * 4) != cudaSuccess) rc = CATS_ERR_NOMEM;
+    if (rc != CATS_OK) {
+        fail(rc, "cats_gpu_llm_create");
+        llm_free(&h->m);
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+
+void cats_gpu_llm_destroy(cats_gpu_llm *h)
+{
+    if (!h) return;
+    if (h->m.stream) cudaStreamSynchronize(h->m.stream);
+    llm_free(&h->m);
+    if (h->tok_log) cudaFree(h->tok_log);
+    delete h;
+}
+
+int cats_gpu_llm_set_weights(cats_gpu_llm *h, const float *emb, const float *rms_att, const float *rms_ffn,
+                             const float *rms_final, const void *wq, const void *wk, const void *wv, const void *wo,
+                             const void *w1, const void *w2, const void *w3, const void *wcls)
+{
+    if (!h || !emb || !rms_att || !rms_ffn || !rms_final || !wq || !wk || !wv || !wo || !w1 || !w2 || !w3 || !wcls)
+        return fail(CATS_ERR_ARG, "cats_gpu_llm_set_weights");
+    int rc = llm_set_weights(&h->m, emb, rms_att, rms_ffn, rms_final, wq, wk, wv, wo, w1, w2, w3, wcls);
+    return rc ? fail(rc, "cats_gpu_llm_set_weights") : CATS_OK;
+}
+
+int cats_gpu_llm_init_random(cats_gpu_llm *h, unsigned long long seed, float std)
+{
+    if (!h) return fail(CATS_ERR_ARG, "cats_gpu_llm_init_random");
+    int rc = llm_init_random(&h->m, seed, std);
+    return rc ? fail(rc, "cats_gpu_llm_init_random") : CATS_OK;
+}
+
+static int ensure_graph(cats_gpu_llm *h)
+{
+    if (!h->m.weights_ready) return fail(CATS_ERR_ARG, "llm: weights not set");
+    if (h->m.exec) return CATS_OK;
+    return check(llm_build_graph(&h->m), "llm: graph capture");
+}
+
+int cats_gpu_llm_set_position(cats_gpu_llm *h, int token, int pos)
+{
+    if (!h || token < 0 || token >= h->m.c.vocab || pos < 0 || pos >= h->m.c.seq_len)
+        return fail(CATS_ERR_ARG, "cats_gpu_llm_set_position");
+    // the pinned staging struct may still be the source of an earlier async copy
+    if (check(cudaStreamSynchronize(h->m.stream), "cats_gpu_llm_set_position")) return g.last_err;
+    StepParams *p = h->m.params_host;
+    p->token = token;
+    p->pos = pos;
+    p->next = 0;
+    p->steps = 0;
+    return check(cudaMemcpyAsync(h->m.params, p, sizeof(StepParams), cudaMemcpyHostToDevice, h->m.stream),
+                 "cats_gpu_llm_set_position");
+}
+
+float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *h, float *logits_host)
+{
+    const char *what = "cats_gpu_llama2_transformer";
+    if (!h || !logits_host) { fail(CATS_ERR_ARG, what); return nullptr; }
+    if (ensure_graph(h)) return nullptr;
+    if (cats_gpu_llm_set_position(h, token, pos)) return nullptr;
+    LlmModel &m = h->m;
+    if (check(cudaGraphLaunch(m.exec, m.stream), what)) return nullptr;
+    if (check(cudaMemcpyAsync(m.logits_host, m.logits, (size_t)m.c.vocab * 4, cudaMemcpyDeviceToHost, m.stream), what))
+        return nullptr;
+    if (check(cudaStreamSynchronize(m.stream), what)) return nullptr;
+    memcpy(logits_host, m.logits_host, (size_t)m.c.vocab * 4);
+    return logits_host;
+}
+
+int cats_gpu_llm_enqueue(cats_gpu_llm *h, int steps)
+{
+    if (!h || steps < 0) return fail(CATS_ERR_ARG, "cats_gpu_llm_enqueue");
+    if (int rc = ensure_graph(h)) return rc;
+    for (int s = 0; s < steps; s++)
+        if (check(cudaGraphLaunch(h->m.exec, h->m.stream), "cats_gpu_llm_enqueue")) return g.last_err;
+    return CATS_OK;
+}
+
+int cats_gpu_llm_generate(cats_gpu_llm *h, int token, int pos, int steps, int *tokens_host)
+{
+    if (!h || steps < 0 || pos + steps > h->m.c.seq_len) return fail(CATS_ERR_ARG, "cats_gpu_llm_generate");
+    if (int rc = ensure_graph(h)) return rc;
+    if (int rc = cats_gpu_llm_set_position(h, token, pos)) return rc;
+    LlmModel &m = h->m;
+    for (int s = 0; s < steps; s++) {
+        if (check(cudaGraphLaunch(m.exec, m.stream), "cats_gpu_llm_generate")) return g.last_err;
+        if (tokens_host &&
+            check(cudaMemcpyAsync(h->tok_log + s, &m.params->next, 4, cudaMemcpyDeviceToDevice, m.stream), "generate"))
+            return g.last_err;
+    }
+    if (tokens_host &&
+        check(cudaMemcpyAsync(tokens_host, h->tok_log, (size_t)steps * 4, cudaMemcpyDeviceToHost, m.stream), "generate"))
+        return g.last_err;
+    return check(cudaStreamSynchronize(m.stream), "cats_gpu_llm_generate");
+}
+
+int cats_gpu_llm_synchronize(cats_gpu_llm *h)
+{
+    if (!h) return fail(CATS_ERR_ARG, "cats_gpu_llm_synchronize");
+    if (check(cudaStreamSynchronize(h->m.stream), "cats_gpu_llm_synchronize")) return g.last_err;
+    int e = 0;
+    cudaMemcpy(&e, h->m.err, 4, cudaMemcpyDeviceToHost);
+    if (e) return fail(CATS_ERR_TIMEOUT, "llm: a device wait timed out");
+    return CATS_OK;
+}
+
+void *cats_gpu_llm_stream(cats_gpu_llm *h) { return h ? (void *)h->m.stream : nullptr; }
+
+int cats_gpu_llm_logits(cats_gpu_llm *h, float *logits_host)
+{
+    if (!h || !logits_host) return fail(CATS_ERR_ARG, "cats_gpu_llm_logits");
+    if (check(cudaMemcpyAsync(logits_host, h->m.logits, (size_t)h->m.c.vocab * 4, cudaMemcpyDeviceToHost, h->m.stream),
+              "cats_gpu_llm_logits"))
+        return g.last_err;
+    return check(cudaStreamSynchronize(h->m.stream), "cats_gpu_llm_logits");
+}
+
+int cats_gpu_llm_next_token(cats_gpu_llm *h)
+{
+    if (!h) return -1;
+    StepParams p;
+    if (cudaMemcpyAsync(&p, h->m.params, sizeof(p), cudaMemcpyDeviceToHost, h->m.stream) != cudaSuccess ||
+        cudaStreamSynchronize(h->m.stream) != cudaSuccess)
+        return -1;
+    return p.next;
+}
+
+size_t cats_gpu_llm_weight_bytes(cats_gpu_llm *h)
+{
+    if (!h) return 0;
+    // algorithmic bytes: the reference-layout weight bytes one step reads
+    const LlmModel &m = h->m;
+    size_t s = 0;
+    auto add = [&](const DevWeight &w) { s += gguf_row_bytes(w.L.type, w.L.n) * w.L.d; };
+    for (auto &w : m.qkv) add(w);
+    for (auto &w : m.wo) add(w);
+    for (auto &w : m.w13) add(w);
+    for (auto &w : m.w2) add(w);
+    add(m.cls);
+    return s;
+}
+
+int cats_gpu_llm_time_matvec(cats_gpu_llm *h, int kind, int reps, float *ms_per_launch, double *bytes_per_launch)
+{
+    if (!h || !ms_per_launch || !bytes_per_launch || kind < 0 || kind > 4 || reps <= 0)
+        return fail(CATS_ERR_ARG, "cats_gpu_llm_time_matvec");
+    if (!h->m.weights_ready) return fail(CATS_ERR_ARG, "cats_gpu_llm_time_matvec: weights not set");
+    return check(llm_time_matvec(&h->m, kind, reps, ms_per_launch, bytes_per_launch), "cats_gpu_llm_time_matvec");
+}
+
+int cats_gpu_synth_tensor(void *host_dst, int type, int n, int d, unsigned long long seed, int tensor_id, float std,
+                          float constant)
+{
+    if (!ensure_init()) return g.last_err;
+    if (!host_dst || !type_ok(type) || n <= 0 || d <= 0 || n % 32) return fail(CATS_ERR_ARG, "cats_gpu_synth_tensor");
+    const size_t bytes = gguf_row_bytes(type, n) * d;
+    uint8_t *buf = nullptr;
+    if (cudaMalloc(&buf, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_synth_tensor");
+    int rc = check(synth_tensor(buf, type, n, d, seed, tensor_id, std, constant, g.stream), "cats_gpu_synth_tensor");
+    if (!rc) rc = check(cudaMemcpyAsync(host_dst, buf, bytes, cudaMemcpyDeviceToHost, g.stream), "cats_gpu_synth_tensor");
+    if (!rc) rc = check(cudaStreamSynchronize(g.stream), "cats_gpu_synth_tensor");
+    cudaFree(buf);
+    return rc;
+}
+
+// ------------------------------------------------------------------ sgemm
+int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda, const float *b,
+                   int ldb, float beta, float *c, int ldc, void *stream)
+{
+    const char *what = "cats_sgemm_dev";
+    if (!ensure_init()) return g.last_err;
+    const bool at = ta == 'T' || ta == 't', bt = tb == 'T' || tb == 't';
+    if ((!at && ta != 'N' && ta != 'n') || (!bt && tb != 'N' && tb != 'n') || m < 0 || n < 0 || k < 0)
+        return fail(CATS_ERR_ARG, what);
+    if (m == 0 || n == 0) return CATS_OK;
+    if (!c || (k > 0 && (!a || !b)) || ldc < n || (k > 0 && (lda < (at ? m : k) || ldb < (bt ? k : n))))
+        return fail(CATS_ERR_ARG, what);
+    SgemmPlan p = sgemm_plan(m, n, k, matvec_num_sms());
+    if (p.work_floats && grow((void **)&g.d_work, &g.cap_work, p.work_floats * 4)) return g.last_err;
+    return check(launch_sgemm(p, at, bt, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, g.d_work,
+                              stream ? (cudaStream_t)stream : g.stream),
+                 what);
+}
+
+void cats_sgemm(char ta, char tb, int m, int n, int k, float alpha, const float *a, const float *b, float beta,
+                float *c)
+{
+    const char *what = "cats_sgemm";
+    if (!ensure_init()) return;
+    const bool at = ta == 'T' || ta == 't', bt = tb == 'T' || tb == 't';
+    if (m < 0 || n < 0 || k < 0 || !c || (k > 0 && (!a || !b))) { fail(CATS_ERR_ARG, what); return; }
+    if (m == 0 || n == 0) return;
+    const size_t ab = (size_t)m * k * 4, bb = (size_t)k * n * 4, cb = (size_t)m * n * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, ab ? ab : 4) || grow((void **)&g.d_b, &g.cap_b, bb ? bb : 4) ||
+        grow((void **)&g.d_c, &g.cap_c, cb))
+        return;
+    if (ab && check(cudaMemcpyAsync(g.d_a, a, ab, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (bb && check(cudaMemcpyAsync(g.d_b, b, bb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (beta != 0.f && check(cudaMemcpyAsync(g.d_c, c, cb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_sgemm_dev(ta, tb, m, n, k, alpha, g.d_a, at ? m : k, g.d_b, bt ? k : n, beta, g.d_c, n, g.stream)) return;
+    if (check(cudaMemcpyAsync(c, g.d_c, cb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+void cats_gemm_rnn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C)
+{ cats_sgemm('N', 'N', M, N, K, alpha, A, B, beta, C); }
+void cats_gemm_rnt(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C)
+{ cats_sgemm('N', 'T', M, N, K, alpha, A, B, beta, C); }
+void cats_gemm_rtn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C)
+{ cats_sgemm('T', 'N', M, N, K, alpha, A, B, beta, C); }
+
+} // extern "C"

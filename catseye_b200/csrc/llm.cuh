@@ -1,0 +1,80 @@
+// llm.cuh — device-resident llama decode step built on the matvec kernel.
+#pragma once
+#include "matvec.cuh"
+#include <vector>
+
+namespace cats {
+
+struct DevWeight {
+    WeightLayout L;
+    uint8_t *ptr = nullptr;
+};
+
+struct LlmConfig {
+    int dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len, wtype;
+    int tp_rank, tp_size;   // tensor parallel shard of this process (1 GPU each)
+};
+
+// step parameters read by the graph from device memory
+struct StepParams {
+    int token;     // input token of this step
+    int pos;       // position of this step
+    int next;      // greedy argmax of the step's logits (written by the advance kernel)
+    int steps;     // number of advance() calls (diagnostics)
+};
+
+typedef void (*AllreduceFn)(void *ctx, float *buf, size_t count, cudaStream_t st);
+typedef void (*ArgmaxReduceFn)(void *ctx, unsigned long long *key, cudaStream_t st);
+
+struct LlmModel {
+    LlmConfig c{};
+    int q_dim = 0, kv_dim = 0, head_size = 0, hidden_loc = 0, vocab_loc = 0, vocab_off = 0;
+    int kv_heads_loc = 0, heads_loc = 0, n_splits = 8;
+    // weights (device)
+    float *emb = nullptr;                 // [vocab][dim] fp32 (replicated)
+    float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
+    std::vector<DevWeight> qkv, wo, w13, w2;
+    DevWeight cls;
+    // state (device)
+    float *x = nullptr, *x2 = nullptr, *delta = nullptr, *q = nullptr, *xb = nullptr, *hb = nullptr;
+    float *logits = nullptr, *kcache = nullptr, *vcache = nullptr;
+    float *part = nullptr;                // attention split partials
+    int *counters = nullptr;              // per-head arrival counters
+    unsigned long long *argmax = nullptr;
+    StepParams *params = nullptr;         // device
+    StepParams *params_host = nullptr;    // pinned
+    float *logits_host = nullptr;         // pinned staging for the host-pointer API
+    int *err = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool weights_ready = false;
+    int stages_cache = 0;
+    // tensor parallel hooks (NCCL), null when tp_size == 1
+    AllreduceFn allreduce = nullptr;
+    ArgmaxReduceFn argmax_reduce = nullptr;
+    void *comm_ctx = nullptr;
+};
+
+int llm_alloc(LlmModel *m, const LlmConfig &c);
+void llm_free(LlmModel *m);
+// upload weights from host blobs in the reference's layout (layer matrices back to back)
+int llm_set_weights(LlmModel *m, const float *emb, const float *rms_att, const float *rms_ffn,
+                    const float *rms_final, const void *wq, const void *wk, const void *wv,
+                    const void *wo, const void *w1, const void *w2, const void *w3, const void *wcls);
+// synthetic weights generated on the device: N(0, std) then block-quantized
+int llm_init_random(LlmModel *m, unsigned long long seed, float std);
+// enqueue one decode step (token/pos from m->params) on m->stream (graph if captured)
+cudaError_t llm_enqueue_step(LlmModel *m, bool advance);
+cudaError_t llm_build_graph(LlmModel *m);
+// Time `reps` passes over every layer's matvec of one kind (0 qkv, 1 wo, 2 w13,
+// 3 w2, 4 classifier) launched back to back with PDL on the model's stream, as
+// in the decode step but storing into scratch.  Outputs the mean device time
+// per launch (CUDA events) and the algorithmic bytes per launch.
+cudaError_t llm_time_matvec(LlmModel *m, int kind, int reps, float *ms_per_launch, double *bytes_per_launch);
+
+// generate one synthetic tensor in the reference's GGUF layout (device dst)
+cudaError_t synth_tensor(uint8_t *dst, int type, int n, int d, unsigned long long seed, int tensor_id,
+                         float std, float constant, cudaStream_t st);
+
+} // namespace cats

@@ -1,0 +1,152 @@
+"""Device-resident llama decode over libcatsgpu (cats_llama2_transformer on a B200).
+
+`GpuLLM` owns a cats_gpu_llm: weights uploaded from host blobs in the
+reference's layouts (what cats_checkpoint_load / cats_gguf_load bind,
+llm/catseye_llm.h:2897-2993) or generated on the device, a fp32 KV cache, and
+a CUDA graph of one decode step.
+"""
+import ctypes as C
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from . import _lib
+
+F32, Q4_0, Q8_0 = 0, 2, 8
+
+
+@dataclass(frozen=True)
+class LlmConfig:
+    dim: int
+    hidden: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    vocab: int
+    seq_len: int
+    wtype: int = F32
+
+    @property
+    def head_size(self):
+        return self.dim // self.n_heads
+
+    @property
+    def kv_dim(self):
+        return self.dim * self.n_kv_heads // self.n_heads
+
+    def with_type(self, t):
+        return replace(self, wtype=t)
+
+
+# the model shapes the benchmarks are quoted on
+STORIES_F32 = LlmConfig(dim=288, hidden=768, n_layers=6, n_heads=6, n_kv_heads=6, vocab=32000, seq_len=256, wtype=F32)
+LLAMA2_7B = LlmConfig(dim=4096, hidden=11008, n_layers=32, n_heads=32, n_kv_heads=32, vocab=32000, seq_len=2048,
+                      wtype=Q4_0)
+LLAMA2_70B = LlmConfig(dim=8192, hidden=28672, n_layers=80, n_heads=64, n_kv_heads=8, vocab=32000, seq_len=2048,
+                       wtype=Q4_0)
+
+
+def weight_bytes(cfg):
+    """Bytes of layer + classifier weights one decode step reads (the reference layout)."""
+    def rb(n):
+        return {F32: n * 4, Q4_0: n // 32 * 18, Q8_0: n // 32 * 34}[cfg.wtype]
+    per_layer = rb(cfg.dim) * (2 * cfg.dim + 2 * cfg.kv_dim + 2 * cfg.hidden) + rb(cfg.hidden) * cfg.dim
+    return cfg.n_layers * per_layer + rb(cfg.dim) * cfg.vocab
+
+
+class GpuLLM:
+    def __init__(self, cfg: LlmConfig, tp_rank=0, tp_size=1):
+        self.lib = _lib.init()
+        self.cfg = cfg
+        c = _lib.LlmConfigC(cfg.dim, cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.vocab, cfg.seq_len,
+                            cfg.wtype, tp_rank, tp_size)
+        self.h = self.lib.cats_gpu_llm_create(C.byref(c))
+        if not self.h:
+            _lib.check(None, "cats_gpu_llm_create")
+            raise _lib.CatsGpuError("cats_gpu_llm_create failed")
+        self._logits = np.zeros(cfg.vocab, dtype=np.float32)
+
+    def set_weights(self, mw):
+        """mw: object with numpy blobs emb, rms_att, rms_ffn, rms_final, wq, wk, wv, wo, w1, w2, w3, wcls."""
+        ptrs = [C.c_void_p(np.ascontiguousarray(getattr(mw, n)).ctypes.data)
+                for n in ("emb", "rms_att", "rms_ffn", "rms_final", "wq", "wk", "wv", "wo", "w1", "w2", "w3", "wcls")]
+        _lib.check(self.lib.cats_gpu_llm_set_weights(self.h, *ptrs), "set_weights")
+
+    def init_random(self, seed, std=0.02):
+        _lib.check(self.lib.cats_gpu_llm_init_random(self.h, seed, std), "init_random")
+
+    def step(self, token, pos, out=None):
+        """cats_llama2_transformer(token, pos): logits of this step (host numpy)."""
+        out = self._logits if out is None else out
+        p = self.lib.cats_gpu_llama2_transformer(token, pos, self.h, C.c_void_p(out.ctypes.data))
+        if not p:
+            _lib.check(None, "llama2_transformer")
+            raise _lib.CatsGpuError("llama2_transformer failed")
+        return out
+
+    def generate(self, token, pos, steps):
+        """Greedy decode fully on the device; returns the argmax ids of the steps."""
+        toks = np.zeros(max(steps, 1), dtype=np.int32)
+        _lib.check(self.lib.cats_gpu_llm_generate(self.h, token, pos, steps, C.c_void_p(toks.ctypes.data)), "generate")
+        return toks[:steps]
+
+    def set_position(self, token, pos):
+        _lib.check(self.lib.cats_gpu_llm_set_position(self.h, token, pos), "set_position")
+
+    def enqueue(self, steps):
+        _lib.check(self.lib.cats_gpu_llm_enqueue(self.h, steps), "enqueue")
+
+    def synchronize(self):
+        _lib.check(self.lib.cats_gpu_llm_synchronize(self.h), "synchronize")
+
+    @property
+    def stream(self):
+        return self.lib.cats_gpu_llm_stream(self.h)
+
+    def logits(self):
+        out = np.zeros(self.cfg.vocab, dtype=np.float32)
+        _lib.check(self.lib.cats_gpu_llm_logits(self.h, C.c_void_p(out.ctypes.data)), "logits")
+        return out
+
+    def next_token(self):
+        return self.lib.cats_gpu_llm_next_token(self.h)
+
+    def weight_bytes(self):
+        return self.lib.cats_gpu_llm_weight_bytes(self.h)
+
+    def time_matvec(self, kind, reps=3):
+        """(ms per launch, algorithmic bytes per launch) of one matvec kind:
+        0 qkv, 1 wo, 2 w13, 3 w2, 4 classifier."""
+        ms, by = C.c_float(), C.c_double()
+        _lib.check(self.lib.cats_gpu_llm_time_matvec(self.h, kind, reps, C.byref(ms), C.byref(by)), "time_matvec")
+        return ms.value, by.value
+
+    def close(self):
+        if self.h:
+            self.lib.cats_gpu_llm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def synth_tensor(t, n, d, seed, tensor_id, std=0.02, constant=0.0):
+    """The device generator's tensor `tensor_id` in GGUF layout (host bytes)."""
+    lib = _lib.init()
+    rb = {F32: n * 4, Q4_0: n // 32 * 18, Q8_0: n // 32 * 34}[t]
+    out = np.zeros(rb * d, dtype=np.uint8)
+    _lib.check(lib.cats_gpu_synth_tensor(C.c_void_p(out.ctypes.data), t, n, d, seed, tensor_id, std, constant),
+               "synth_tensor")
+    return out
+
+
+# tensor ids of the device generator (csrc/llm.cu)
+T_EMB, T_RMS_ATT, T_RMS_FFN, T_RMS_FINAL, T_WCLS, T_LAYER0 = 0, 1, 2, 3, 4, 16
+
+
+def layer_tensor_id(layer, k):
+    """k: 0 wq, 1 wk, 2 wv, 3 wo, 4 w1, 5 w2, 6 w3."""
+    return T_LAYER0 + layer * 8 + k

@@ -1,0 +1,104 @@
+"""Host mirror of catseye's hot-path operator interface over libcatsgpu.
+
+The names and argument meanings follow the reference:
+  matmul(xout, x, w, n, d)         llm/catseye_llm.h:1519-1533 (gguf_matmul[] :2583)
+  quantize(q, x, n)                quantize_q8, :155-225
+  dequantize(y, w, row, n)         _dequantize_q4_0, :483-486
+  sgemm(ta, tb, m, n, k, ...)      sgemm_ocl, sgemm_ocl2.h:208 / gemm_rnn|rnt|rtn, catseye.h:78-129
+Inputs are numpy arrays (host memory, copied per call like the reference's
+GPU backends) or torch CUDA tensors for the device-pointer forms.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+
+F32, Q4_0, Q8_0 = 0, 2, 8
+
+# the type-indexed tables of the reference (gguf_matmul / gguf_quantize / gguf_dequantize)
+_MATMUL = {F32: "cats_gpu_matmul_f32", Q4_0: "cats_gpu_matmul_q4_0_q8", Q8_0: "cats_gpu_matmul_q8_0_q8"}
+_DEQUANT = {Q4_0: "cats_gpu_dequantize_q4_0", Q8_0: "cats_gpu_dequantize_q8_0"}
+
+
+def row_bytes(t, n):
+    return {F32: n * 4, Q4_0: n // 32 * 18, Q8_0: n // 32 * 34}[t]
+
+
+def _p(a):
+    return C.c_void_p(a.ctypes.data)
+
+
+def _dp(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def register_weight(w, t, n, d):
+    """Upload a weight (bytes of [d][n] in GGUF layout) before its first matmul."""
+    lib = _lib.init()
+    _lib.check(lib.cats_gpu_register_weight(_p(w), t, n, d), "register_weight")
+
+
+def unregister_weight(w):
+    _lib.init().cats_gpu_unregister_weight(_p(w))
+
+
+def matmul(t, xout, x, w, n, d):
+    """xout[:d] = W x; x is fp32 (F32) or Q8 blocks (quantized types) as quantize() made them."""
+    lib = _lib.init()
+    getattr(lib, _MATMUL[t])(_p(xout), _p(x), _p(w), n, d)
+    _lib.check(None, _MATMUL[t])
+    return xout
+
+
+def quantize(x):
+    """quantize_q8 of fp32 x -> n/32 blocks of 36 bytes (int8 array)."""
+    lib = _lib.init()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.zeros(x.size // 32 * 36, dtype=np.int8)
+    lib.cats_gpu_quantize_q8(_p(q), _p(x), x.size)
+    _lib.check(None, "quantize_q8")
+    return q
+
+
+def dequantize(t, w, row, n):
+    lib = _lib.init()
+    y = np.zeros(n, dtype=np.float32)
+    getattr(lib, _DEQUANT[t])(_p(y), _p(np.ascontiguousarray(w)), row, n)
+    _lib.check(None, _DEQUANT[t])
+    return y
+
+
+def matvec_dev(w, out, x, x_is_q8=False, stream=None):
+    """Device form: out (cuda tensor, d floats) = W x for a registered weight w (host key)."""
+    lib = _lib.init()
+    _lib.check(lib.cats_gpu_matvec_dev(_p(w), _dp(out), _dp(x), int(x_is_q8), stream), "matvec_dev")
+    return out
+
+
+def quantize_dev(q, x, scalar_mode=False, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_gpu_quantize_q8_dev(_dp(q), _dp(x), x.numel(), int(scalar_mode), stream), "quantize_dev")
+    return q
+
+
+def dequantize_dev(t, y, w, n, rows, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_gpu_dequantize_dev(t, _dp(y), _dp(w), n, rows, stream), "dequantize_dev")
+    return y
+
+
+def sgemm(ta, tb, m, n, k, alpha, a, b, beta, c):
+    """C = alpha*op(A)*op(B) + beta*C on host arrays (C updated in place and returned)."""
+    lib = _lib.init()
+    lib.cats_sgemm(ta.encode(), tb.encode(), m, n, k, alpha, _p(np.ascontiguousarray(a, np.float32)),
+                   _p(np.ascontiguousarray(b, np.float32)), beta, _p(c))
+    _lib.check(None, "cats_sgemm")
+    return c
+
+
+def sgemm_dev(ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_sgemm_dev(ta.encode(), tb.encode(), m, n, k, alpha, _dp(a), lda, _dp(b), ldb, beta,
+                                  _dp(c), ldc, stream), "cats_sgemm_dev")
+    return c

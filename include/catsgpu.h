@@ -1,0 +1,178 @@
+/*
+ * catsgpu.h — C ABI of libcatsgpu.so, the B200 (sm_100a) matrix-multiply hot
+ * path for catseye.  Plain C types only; no CUDA or torch types cross this
+ * boundary (streams are passed as void*, a cudaStream_t).
+ *
+ * Two families of entry points:
+ *  - drop-ins with the reference's exact signatures and host pointers, which a
+ *    catseye program binds in place of the CPU / OpenCL / OpenGL backends;
+ *  - device-pointer ("_dev") entry points with the same arithmetic, for callers
+ *    that keep data resident in HBM, plus the device-resident decode step.
+ *
+ * Errors: the drop-ins return void like the functions they replace.  Every
+ * call records a sticky status readable with cats_gpu_last_error(); with
+ * CATS_GPU_STRICT=1 in the environment the library prints the error and aborts.
+ * Non-void entry points return that status (0 = success).
+ *
+ * Threading: one host thread drives the library at a time; every host-pointer
+ * call is synchronous (outputs are valid on return).
+ */
+#ifndef CATSGPU_H
+#define CATSGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ggml type numbers, as in llm/catseye_llm.h:2557-2580 */
+#define CATS_TYPE_F32  0
+#define CATS_TYPE_Q4_0 2
+#define CATS_TYPE_Q8_0 8
+
+/* status codes */
+#define CATS_OK             0
+#define CATS_ERR_CUDA       1   /* a CUDA runtime call failed */
+#define CATS_ERR_ARG        2   /* bad pointer, size or type, rejected before launch */
+#define CATS_ERR_NOMEM      3   /* device allocation failed */
+#define CATS_ERR_TIMEOUT    4   /* a bounded device-side wait gave up (kernel returned early) */
+#define CATS_ERR_UNSUPPORTED 5  /* shape or type this build does not handle */
+#define CATS_ERR_NOT_INIT   6   /* cats_gpu_init was not called */
+#define CATS_ERR_NCCL       7   /* a collective failed */
+
+/* ------------------------------------------------------------ lifecycle */
+
+/* Select and initialise a device (-1: $CATS_GPU_DEVICE or 0).  Replaces
+ * matmul_gpu_init (llm/gpgpu_matmul.h:24-35, called from cats_llm_malloc,
+ * llm/catseye_llm.h:634-636) and sgemm_ocl_init (sgemm_ocl2.h:200-207). */
+int cats_gpu_init(int device);
+/* Free every device resource.  Replaces matmul_gpu_term (llm/gpgpu_matmul.h:
+ * 106-112, called from cats_llm_free :641-643) and sgemm_ocl_finish
+ * (sgemm_ocl2.h:262-266). */
+void cats_gpu_term(void);
+int cats_gpu_last_error(void);           /* sticky status of the last failing call */
+void cats_gpu_clear_error(void);
+const char *cats_gpu_error_string(int code);
+/* device error word OR-ed by kernels whose bounded waits expired (0 = none) */
+int cats_gpu_device_error(void);
+
+/* ------------------------------------------------------ weight registry */
+
+/* Upload and re-lay-out a weight the caller keeps alive and unchanged
+ * (cats_tensor.data, llm/catseye_llm.h:527-539): [d][n] in the reference's
+ * GGUF row layout.  The drop-in matmuls register on first use; calling this
+ * up front moves the upload out of the first matmul. */
+int cats_gpu_register_weight(const void *w, int type, int n, int d);
+void cats_gpu_unregister_weight(const void *w);
+/* bytes of the device copy of a registered weight (0 if unknown) */
+size_t cats_gpu_weight_device_bytes(const void *w);
+
+/* ------------------------------------------- LLM drop-ins (host pointers) */
+
+/* matmul(xout, x, w, n, d): xout[i] = sum_j W[i][j] x[j], W row-major [d][n]
+ * (MATMUL_FUNC, llm/catseye_llm.h:1519-1533; bound through gguf_matmul[] :2583
+ * and cats_tensor.matmul :2839-2840, :2985-2990).  x is what the tensor's
+ * quantize produced. */
+void cats_gpu_matmul_f32(float *xout, void *x, void *w, int n, int d);      /* matmul_f32  :1529 */
+void cats_gpu_matmul_q4_0_q8(float *xout, void *x, void *w, int n, int d);  /* matmul_q4_0_q8 :1531 */
+void cats_gpu_matmul_q8_0_q8(float *xout, void *x, void *w, int n, int d);  /* GGML_TYPE_Q8_0 (:2566), no
+                                                                               reference matmul: same block scheme */
+/* quantize_q8 (llm/catseye_llm.h:155-225, AVX build rounding), in place like
+ * the reference: n floats -> n/32 blocks of {int8 q[32]; float d}. */
+void cats_gpu_quantize_q8(int8_t *q, float *x, int n);
+/* _dequantize_q4_0 (llm/catseye_llm.h:483-486): row `row` of a [*][n] Q4_0
+ * matrix -> n floats.  Returns 0 like the reference. */
+void *cats_gpu_dequantize_q4_0(void *y, const void *x, int row, int n);
+void *cats_gpu_dequantize_q8_0(void *y, const void *x, int row, int n);
+
+/* -------------------------------------- LLM device-pointer entry points */
+
+/* d_out[d] = W x for a registered weight w (host key); d_x is a device
+ * pointer to n floats (x_is_q8 = 0: quantized on the device for quantized
+ * types) or to n/32 Q8 blocks (x_is_q8 = 1).  stream: cudaStream_t or NULL. */
+int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q8, void *stream);
+/* quantize_q8 on device buffers; scalar_mode selects the plain-C build's
+ * rounding (llm/catseye_llm.h:227-251). */
+int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mode, void *stream);
+/* dequantize `rows` rows of a reference-layout weight on the device */
+int cats_gpu_dequantize_dev(int type, float *d_y, const void *d_w, int n, int rows, void *stream);
+
+/* ------------------------------------------ LLM device-resident decode */
+
+typedef struct cats_gpu_llm cats_gpu_llm;
+
+typedef struct {
+    int dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len;
+    int wtype;              /* CATS_TYPE_F32 / Q4_0 / Q8_0 for wq..w3 and the classifier */
+    int tp_rank, tp_size;   /* tensor-parallel shard (1 process per GPU); 0,1 = no TP */
+} cats_gpu_llm_config;
+
+/* Allocate a model on the current device (cats_llm_malloc, llm/catseye_llm.h:607-637). */
+cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg);
+void cats_gpu_llm_destroy(cats_gpu_llm *m);
+/* Upload weights from host blobs in the reference's layouts (what the
+ * loaders bind, llm/catseye_llm.h:2897-2993): emb [vocab][dim] f32; norms f32;
+ * wq..w3 the n_layers matrices of a kind stored back to back; wcls [vocab][dim]. */
+int cats_gpu_llm_set_weights(cats_gpu_llm *m, const float *emb, const float *rms_att,
+                             const float *rms_ffn, const float *rms_final, const void *wq,
+                             const void *wk, const void *wv, const void *wo, const void *w1,
+                             const void *w2, const void *w3, const void *wcls);
+/* Synthetic weights generated on the device: N(0, std) (norms = 1), then
+ * block-quantized to the model's type; deterministic in seed. */
+int cats_gpu_llm_init_random(cats_gpu_llm *m, unsigned long long seed, float std);
+/* One decode step, cats_llama2_transformer(token, pos, m) (llm/catseye_llm.h:
+ * 1625-1772): token and pos go in, the logits come back in logits_host
+ * (vocab floats).  Returns logits_host, or NULL on error. */
+float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *m, float *logits_host);
+/* Device-resident greedy decoding: run `steps` steps starting at (token, pos),
+ * each step's argmax (sample_argmax, :1944-1956) feeding the next, with no
+ * host round trip.  tokens_host (may be NULL) receives the steps' argmax ids. */
+int cats_gpu_llm_generate(cats_gpu_llm *m, int token, int pos, int steps, int *tokens_host);
+/* Asynchronous form for timing: enqueue `steps` greedy steps on the model's stream. */
+int cats_gpu_llm_enqueue(cats_gpu_llm *m, int steps);
+int cats_gpu_llm_set_position(cats_gpu_llm *m, int token, int pos);
+int cats_gpu_llm_synchronize(cats_gpu_llm *m);
+void *cats_gpu_llm_stream(cats_gpu_llm *m);
+/* copies of device state for tests: logits (vocab floats) and the last argmax */
+int cats_gpu_llm_logits(cats_gpu_llm *m, float *logits_host);
+int cats_gpu_llm_next_token(cats_gpu_llm *m);
+/* Bytes of weights one decode step streams (for roofline accounting). */
+size_t cats_gpu_llm_weight_bytes(cats_gpu_llm *m);
+/* Device time of one kind of matvec launch (0 qkv, 1 wo, 2 w13, 3 w2,
+ * 4 classifier): `reps` passes over all layers, back to back on the model's
+ * stream, timed with CUDA events.  Reports ms per launch and the algorithmic
+ * bytes one launch must move (reference-layout weight + x + out). */
+int cats_gpu_llm_time_matvec(cats_gpu_llm *m, int kind, int reps, float *ms_per_launch,
+                             double *bytes_per_launch);
+/* Write synthetic tensor `tensor_id` of the generator in the reference's GGUF
+ * layout to host memory (tests regenerate the device model's weights). */
+int cats_gpu_synth_tensor(void *host_dst, int type, int n, int d, unsigned long long seed,
+                          int tensor_id, float std, float constant);
+
+/* ------------------------------------------------------------ CNN sgemm */
+
+/* C = alpha*op(A)*op(B) + beta*C, row-major, packed (lda = K|M, ldb = N|K,
+ * ldc = N); ta/tb in 'N','T'.  beta == 0 does not read C.  Host pointers,
+ * copied in and out per call like the reference's GPU backends.
+ * Replaces sgemm_ocl (sgemm_ocl2.h:208-261) and sgemm_gl (sgemm_gl1.h:247-273). */
+void cats_sgemm(char ta, char tb, int m, int n, int k, float alpha, const float *a,
+                const float *b, float beta, float *c);
+/* The three forms catseye.h calls (gemm_rnn / gemm_rnt / gemm_rtn, catseye.h:61-75,78-129). */
+void cats_gemm_rnn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C);
+void cats_gemm_rnt(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C);
+void cats_gemm_rtn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C);
+/* Device pointers with explicit leading dimensions. */
+int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda,
+                   const float *b, int ldb, float beta, float *c, int ldc, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif

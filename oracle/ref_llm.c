@@ -1,0 +1,134 @@
+/*
+ * ref_llm.c — exports the reference's own LLM hot-path functions from a shared
+ * library so the oracle restatement can be pinned against them.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Compiled by oracle/Makefile from the reference
+ * header where it lies (REF_DIR/llm/catseye_llm.h, never copied into this
+ * repository) into oracle/_ref/.  The functions below only forward to the
+ * reference's static functions; they add no arithmetic of their own.
+ */
+#include "catseye_llm.h"
+
+int ref_is_avx(void)
+{
+#ifdef __AVX__
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+float ref_fp16_to_fp32(uint16_t h) { return cats_fp16_to_fp32(h); }
+uint16_t ref_fp32_to_fp16(float f) { return cats_fp32_to_fp16(f); }
+
+/* quantize_q8 works in place in the reference; copy first so the caller's x survives */
+void ref_quantize_q8(int8_t *q, const float *x, int n)
+{
+    float *tmp = malloc(sizeof(float) * n);
+    memcpy(tmp, x, sizeof(float) * n);
+    quantize_q8((int8_t *)tmp, tmp, n);
+    memcpy(q, tmp, (size_t)(n / 32) * 36);
+    free(tmp);
+}
+
+void ref_quantize_q8_K(int8_t *q, const float *x, int n) { quantize_q8_K(q, (real *)x, n); }
+
+void ref_dequantize(int type, float *y, const void *w, int row, int n)
+{
+    gguf_dequantize[type](y, w, row, n);
+}
+
+void ref_matmul(int type, float *xout, void *x, void *w, int n, int d)
+{
+    gguf_matmul[type](xout, x, w, n, d);
+}
+
+#ifdef __AVX__
+void ref_matmul_q4_0_f32(float *xout, void *x, void *w, int n, int d) { matmul_q4_0(xout, x, w, n, d); }
+#endif
+
+int ref_sample_argmax(float *v, int n) { return sample_argmax(v, n); }
+
+/* A cats_llm_model whose tensors point at caller-owned blobs (layer matrices of
+ * one kind stored back to back), bound like cats_checkpoint_load / the GGUF
+ * loader bind them (llm/catseye_llm.h:2839-2840, 2985-2990). */
+typedef struct { cats_llm_model m; } ref_model;
+
+static size_t rowbytes(int type, int n)
+{
+    switch (type) {
+    case GGML_TYPE_F32: return (size_t)n * 4;
+    case GGML_TYPE_Q4_0: return (size_t)(n / 32) * 18;
+    case GGML_TYPE_Q3_K: return (size_t)(n / 256) * 110;
+    case GGML_TYPE_Q6_K: return (size_t)(n / 256) * 210;
+    }
+    return 0;
+}
+
+static void bind(cats_tensor *t, int type, void *data)
+{
+    t->type = type;
+    t->data = data;
+    t->quantize = gguf_quantize[type];
+    t->matmul = gguf_matmul[type];
+}
+
+void *ref_llm_create(int dim, int hidden, int n_layers, int n_heads, int n_kv_heads, int vocab,
+                     int seq_len, int wtype, const float *emb, const float *rms_att,
+                     const float *rms_ffn, const float *rms_final, const void *wq, const void *wk,
+                     const void *wv, const void *wo, const void *w1, const void *w2, const void *w3,
+                     const void *wcls)
+{
+    if (wtype != GGML_TYPE_F32 && wtype != GGML_TYPE_Q4_0 && wtype != GGML_TYPE_Q3_K &&
+        wtype != GGML_TYPE_Q6_K)
+        return NULL;
+    ref_model *r = calloc(1, sizeof(ref_model));
+    cats_llm_model *m = &r->m;
+    m->n_embd = dim; m->n_hidden = hidden; m->n_layer = n_layers; m->n_head = n_heads;
+    m->n_kv_head = n_kv_heads; m->n_vocab = vocab; m->seq_len = seq_len;
+    int kv_dim = dim * n_kv_heads / n_heads;
+    m->token_embedding_table = &m->tensor[0];
+    m->rms_final_weight = &m->tensor[1];
+    m->wcls = &m->tensor[2];
+    bind(m->token_embedding_table, GGML_TYPE_F32, (void *)emb);
+    bind(m->rms_final_weight, GGML_TYPE_F32, (void *)rms_final);
+    bind(m->wcls, wtype, (void *)wcls);
+    for (int l = 0; l < n_layers; l++) {
+        m->rms_att_weight[l] = &m->tensor[3 + l * 9];
+        m->wq[l] = &m->tensor[4 + l * 9];
+        m->wk[l] = &m->tensor[5 + l * 9];
+        m->wv[l] = &m->tensor[6 + l * 9];
+        m->wo[l] = &m->tensor[7 + l * 9];
+        m->rms_ffn_weight[l] = &m->tensor[8 + l * 9];
+        m->w1[l] = &m->tensor[9 + l * 9];
+        m->w2[l] = &m->tensor[10 + l * 9];
+        m->w3[l] = &m->tensor[11 + l * 9];
+        bind(m->rms_att_weight[l], GGML_TYPE_F32, (void *)(rms_att + (size_t)l * dim));
+        bind(m->rms_ffn_weight[l], GGML_TYPE_F32, (void *)(rms_ffn + (size_t)l * dim));
+        bind(m->wq[l], wtype, (char *)wq + rowbytes(wtype, dim) * dim * l);
+        bind(m->wk[l], wtype, (char *)wk + rowbytes(wtype, dim) * kv_dim * l);
+        bind(m->wv[l], wtype, (char *)wv + rowbytes(wtype, dim) * kv_dim * l);
+        bind(m->wo[l], wtype, (char *)wo + rowbytes(wtype, dim) * dim * l);
+        bind(m->w1[l], wtype, (char *)w1 + rowbytes(wtype, dim) * hidden * l);
+        bind(m->w2[l], wtype, (char *)w2 + rowbytes(wtype, hidden) * dim * l);
+        bind(m->w3[l], wtype, (char *)w3 + rowbytes(wtype, dim) * hidden * l);
+    }
+    dequantize = _dequantize_memcpy;
+    cats_llm_malloc(m);
+    return r;
+}
+
+float *ref_llm_step(void *h, int token, int pos)
+{
+    ref_model *r = h;
+    return cats_llama2_transformer(token, pos, &r->m);
+}
+
+void ref_llm_destroy(void *h)
+{
+    ref_model *r = h;
+    cats_llm_model *m = &r->m;
+    free(m->x); free(m->xb); free(m->xb2); free(m->hb); free(m->hb2); free(m->q);
+    free(m->att); free(m->logits); free(m->key_cache); free(m->value_cache);
+    free(r);
+}

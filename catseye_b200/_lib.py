@@ -47,6 +47,8 @@ SIGNATURES = {
     "cats_gpu_llama2_transformer": (_vp, [_i, _i, _vp, _vp]),
     "cats_gpu_llm_generate": (_i, [_vp, _i, _i, _i, _vp]),
     "cats_gpu_llm_enqueue": (_i, [_vp, _i]),
+    "cats_gpu_llm_set_engine": (_i, [_vp, _i]),
+    "cats_gpu_llm_trace_step": (_i, [_vp, _i, _i, _vp, _i, C.POINTER(C.c_int)]),
     "cats_gpu_llm_set_position": (_i, [_vp, _i, _i]),
     "cats_gpu_llm_synchronize": (_i, [_vp]),
     "cats_gpu_llm_stream": (_vp, [_vp]),
@@ -95,8 +97,17 @@ def check(rc, what="catsgpu"):
         if rc:
             lib.cats_gpu_clear_error()
     if rc:
+        lib.cats_gpu_clear_error()
         raise CatsGpuError(f"{what}: {lib.cats_gpu_error_string(rc).decode()} ({rc})")
     return rc
+
+
+def call_void(fn, *args, what=None):
+    """Call a void drop-in and raise if it recorded an error (the sticky
+    status is cleared first, so only this call's outcome is reported)."""
+    load().cats_gpu_clear_error()
+    fn(*args)
+    return check(None, what or fn.__name__)
 
 
 def init(device=-1):

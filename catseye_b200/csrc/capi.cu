@@ -140,7 +140,7 @@ MatvecArgs args_for(const Reg &r)
     a.full_chunk = L.full_chunk;
     a.last_chunk = L.last_chunk;
     a.tile_bytes = L.tile_bytes;
-    a.stages = std::max(2, std::min(8, (int)(65536 / round_up(L.full_chunk, 128))));
+    a.stages = std::max(2, std::min(8, (int)(MV_STAGE_BUDGET / round_up(L.full_chunk, 128))));
     a.err = g.d_err;
     return a;
 }
@@ -160,7 +160,7 @@ void matmul_host(int type, float *xout, void *x, void *w, int n, int d, const ch
     a.x = g.d_x;
     a.epi = EPI_STORE;
     a.out = g.d_out;
-    if (check(launch_matvec(a, 1, type, g.stream, false), what)) return;
+    if (check(launch_matvec(a, r->W.L.rpw, type, g.stream, false), what)) return;
     if (check(cudaMemcpyAsync(xout, g.d_out, (size_t)d * 4, cudaMemcpyDeviceToHost, g.stream), what)) return;
     if (check(cudaStreamSynchronize(g.stream), what)) return;
     check_device_error(what);
@@ -237,7 +237,9 @@ int cats_gpu_register_weight(const void *w, int type, int n, int d)
     if (cudaMalloc(&stg, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
     Reg r;
     r.type = type; r.n = n; r.d = d;
-    r.W.L = make_layout(type, n, d, 1);
+    // two rows per warp halves the activation reads per weight byte; use it
+    // when there are enough 16-row tiles to give every SM two or more
+    r.W.L = make_layout(type, n, d, d >= 2 * 16 * matvec_num_sms() ? 2 : 1);
     int rc = CATS_OK;
     if (cudaMalloc(&r.W.ptr, r.W.L.total_bytes) != cudaSuccess) rc = fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
     if (!rc) rc = check(cudaMemcpyAsync(stg, w, bytes, cudaMemcpyHostToDevice, g.stream), "cats_gpu_register_weight");
@@ -318,7 +320,7 @@ int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q
     a.x = d_x;
     a.epi = EPI_STORE;
     a.out = d_out;
-    return check(launch_matvec(a, 1, r.type, st, false), what);
+    return check(launch_matvec(a, r.W.L.rpw, r.type, st, false), what);
 }
 
 int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mode, void *stream)
@@ -341,6 +343,7 @@ int cats_gpu_dequantize_dev(int type, float *d_y, const void *d_w, int n, int ro
 // ------------------------------------------------------------------ LLM
 struct cats_gpu_llm {
     LlmModel m;
+    int engine = CATS_ENGINE_PERSISTENT;
     int *tok_log = nullptr;   // device: argmax ids of generate()
 };
 
@@ -395,8 +398,35 @@ int cats_gpu_llm_init_random(cats_gpu_llm *h, unsigned long long seed, float std
 static int ensure_graph(cats_gpu_llm *h)
 {
     if (!h->m.weights_ready) return fail(CATS_ERR_ARG, "llm: weights not set");
+    if (h->engine == CATS_ENGINE_PERSISTENT) {
+        int rc = decode_prepare(&h->m);
+        return rc ? fail(rc, "llm: persistent decode setup") : CATS_OK;
+    }
     if (h->m.exec) return CATS_OK;
     return check(llm_build_graph(&h->m), "llm: graph capture");
+}
+
+// Enqueue `steps` greedy steps from the device params on the model's stream.
+static int run_steps(cats_gpu_llm *h, int steps, int *tok_log_dev, const char *what)
+{
+    LlmModel &m = h->m;
+    if (h->engine == CATS_ENGINE_PERSISTENT)
+        return check(decode_launch(&m, steps, tok_log_dev, m.c.seq_len + 1), what);
+    for (int s = 0; s < steps; s++) {
+        if (check(cudaGraphLaunch(m.exec, m.stream), what)) return g.last_err;
+        if (tok_log_dev && check(cudaMemcpyAsync(tok_log_dev + s, &m.params->next, 4, cudaMemcpyDeviceToDevice,
+                                                 m.stream), what))
+            return g.last_err;
+    }
+    return CATS_OK;
+}
+
+int cats_gpu_llm_set_engine(cats_gpu_llm *h, int engine)
+{
+    if (!h || (engine != CATS_ENGINE_PERSISTENT && engine != CATS_ENGINE_GRAPH))
+        return fail(CATS_ERR_ARG, "cats_gpu_llm_set_engine");
+    h->engine = engine;
+    return CATS_OK;
 }
 
 int cats_gpu_llm_set_position(cats_gpu_llm *h, int token, int pos)
@@ -421,21 +451,42 @@ float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *h, float *l
     if (ensure_graph(h)) return nullptr;
     if (cats_gpu_llm_set_position(h, token, pos)) return nullptr;
     LlmModel &m = h->m;
-    if (check(cudaGraphLaunch(m.exec, m.stream), what)) return nullptr;
+    if (run_steps(h, 1, nullptr, what)) return nullptr;
     if (check(cudaMemcpyAsync(m.logits_host, m.logits, (size_t)m.c.vocab * 4, cudaMemcpyDeviceToHost, m.stream), what))
         return nullptr;
     if (check(cudaStreamSynchronize(m.stream), what)) return nullptr;
+    int e = 0;
+    cudaMemcpy(&e, m.err, 4, cudaMemcpyDeviceToHost);
+    if (e) { cudaMemset(m.err, 0, 4); fail(CATS_ERR_TIMEOUT, what); return nullptr; }
     memcpy(logits_host, m.logits_host, (size_t)m.c.vocab * 4);
     return logits_host;
+}
+
+int cats_gpu_llm_trace_step(cats_gpu_llm *h, int token, int pos, unsigned long long *host, int per_cta, int *ctas)
+{
+    const char *what = "cats_gpu_llm_trace_step";
+    if (!h || !host || per_cta <= 0 || !ctas) return fail(CATS_ERR_ARG, what);
+    if (int rc = ensure_graph(h)) return rc;
+    if (int rc = decode_prepare(&h->m)) return fail(rc, what);
+    if (int rc = cats_gpu_llm_set_position(h, token, pos)) return rc;
+    const int grid = matvec_num_sms();
+    const size_t bytes = (size_t)grid * per_cta * 8;
+    unsigned long long *d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, what);
+    cudaMemsetAsync(d, 0, bytes, h->m.stream);
+    int rc = check(decode_launch(&h->m, 1, nullptr, 0, d, per_cta), what);
+    if (!rc) rc = check(cudaMemcpyAsync(host, d, bytes, cudaMemcpyDeviceToHost, h->m.stream), what);
+    if (!rc) rc = check(cudaStreamSynchronize(h->m.stream), what);
+    cudaFree(d);
+    *ctas = grid;
+    return rc;
 }
 
 int cats_gpu_llm_enqueue(cats_gpu_llm *h, int steps)
 {
     if (!h || steps < 0) return fail(CATS_ERR_ARG, "cats_gpu_llm_enqueue");
     if (int rc = ensure_graph(h)) return rc;
-    for (int s = 0; s < steps; s++)
-        if (check(cudaGraphLaunch(h->m.exec, h->m.stream), "cats_gpu_llm_enqueue")) return g.last_err;
-    return CATS_OK;
+    return run_steps(h, steps, nullptr, "cats_gpu_llm_enqueue");
 }
 
 int cats_gpu_llm_generate(cats_gpu_llm *h, int token, int pos, int steps, int *tokens_host)
@@ -444,16 +495,11 @@ int cats_gpu_llm_generate(cats_gpu_llm *h, int token, int pos, int steps, int *t
     if (int rc = ensure_graph(h)) return rc;
     if (int rc = cats_gpu_llm_set_position(h, token, pos)) return rc;
     LlmModel &m = h->m;
-    for (int s = 0; s < steps; s++) {
-        if (check(cudaGraphLaunch(m.exec, m.stream), "cats_gpu_llm_generate")) return g.last_err;
-        if (tokens_host &&
-            check(cudaMemcpyAsync(h->tok_log + s, &m.params->next, 4, cudaMemcpyDeviceToDevice, m.stream), "generate"))
-            return g.last_err;
-    }
+    if (int rc = run_steps(h, steps, tokens_host ? h->tok_log : nullptr, "cats_gpu_llm_generate")) return rc;
     if (tokens_host &&
         check(cudaMemcpyAsync(tokens_host, h->tok_log, (size_t)steps * 4, cudaMemcpyDeviceToHost, m.stream), "generate"))
         return g.last_err;
-    return check(cudaStreamSynchronize(m.stream), "cats_gpu_llm_generate");
+    return cats_gpu_llm_synchronize(h);
 }
 
 int cats_gpu_llm_synchronize(cats_gpu_llm *h)

@@ -1,0 +1,635 @@
+// decode.cu — persistent, cooperative decode kernel: whole tokens in one launch.
+//
+// Restates cats_llama2_transformer (llm/catseye_llm.h:1625-1772) for one
+// B200.  One CTA per SM, launched cooperatively so every CTA is resident.
+//
+//  * A producer warp walks the weights of every layer in step order (qkv, wo,
+//    w1/w3, w2 per layer, then the classifier; this CTA's tiles of each) and
+//    streams their (tile, segment) chunks into a deep shared-memory ring with
+//    1-D bulk copies (TMA engine, L2 evict-first).  It never waits for an
+//    activation, so HBM keeps streaming through every phase boundary.
+//  * Eight consumer warps run the phases.  Between phases the CTAs meet at a
+//    grid barrier (bounded spin on a global counter); after it each CTA
+//    stages the phase's activation (rmsnorm + quantize_q8) in shared memory
+//    and dots the ring's chunks against it.
+//  * Attention (:1677-1723) is split over time: each warp scores one
+//    (head, time-chunk) item with an online softmax; the wo phase merges the
+//    chunks while staging its input.
+//  * After the classifier (:1765-1770) CTA 0 turns the greedy argmax
+//    (:1944-1956) into the next token and position, so `steps` tokens decode
+//    with no host round trip.
+#include "llm.cuh"
+#include "mv_device.cuh"
+#include <algorithm>
+
+namespace cats {
+
+constexpr int DEC_NC = 32 * MV_CONSUMER_WARPS;   // consumer threads
+constexpr int DEC_MAX_STAGES = 32;
+constexpr uint32_t GRID_SPIN_LIMIT = 1u << 23;   // ~1 s of polling with backoff
+
+struct WDesc {
+    const uint8_t *w;
+    int n, d, R, rpw, units, nseg, n_tiles;
+    uint32_t full_chunk, last_chunk;
+    unsigned long long tile_bytes;
+};
+
+struct DecodeArgs {
+    const WDesc *wd;   // per layer: qkv, wo, w13, w2; then the classifier
+    int n_wd;
+    int n_layers, dim, hidden, q_dim, kv_dim, head_size, kv_mul, heads, seq_len, vocab;
+    const float *emb, *rms_att, *rms_ffn, *rms_final;
+    float *x, *q, *xb, *hb, *logits, *kcache, *vcache, *part;
+    int *head_cnt;       // per-head arrival counters of the attention chunks (0 between phases)
+    int max_splits;
+    StepParams *params;
+    unsigned long long *argmax;
+    int *tok_log;
+    int tok_cap;
+    unsigned int *bar;   // grid barrier counter, zeroed before each launch
+    int *abort_flag;     // set by any CTA whose bounded wait expired
+    int steps;
+    int stages;
+    uint32_t slot_bytes, xs_bytes;
+    int *err;
+    unsigned long long *trace;   // optional per-CTA phase timeline (globaltimer ns), trace_stride records each
+    int trace_stride;
+};
+
+__device__ __forceinline__ unsigned long long global_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Thread 0 of each CTA records a timestamp (tracing only).
+__device__ __forceinline__ void trace_mark(const DecodeArgs &a, int &k)
+{
+    if (a.trace && threadIdx.x == 0 && k < a.trace_stride) a.trace[(size_t)blockIdx.x * a.trace_stride + k] = global_ns();
+    k++;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int ld_volatile_i32(const int *p)
+{
+    return *reinterpret_cast<const volatile int *>(p);
+}
+
+struct Smem {
+    uint8_t *ring, *xs;
+    uint64_t *full, *empty;
+    float *red;
+    volatile int *abort_s;   // hint for bounded waits: stop waiting, the kernel is unwinding
+    volatile int *sync_ok;   // grid_sync's decision, written by thread 0 between its two CTA barriers
+};
+
+__device__ __forceinline__ Smem smem_layout(uint8_t *base, const DecodeArgs &a)
+{
+    Smem s;
+    s.ring = base;
+    s.xs = base + (size_t)a.stages * a.slot_bytes;
+    uint8_t *p = s.xs + a.xs_bytes;
+    s.full = reinterpret_cast<uint64_t *>(p);
+    s.empty = s.full + DEC_MAX_STAGES;
+    s.red = reinterpret_cast<float *>(s.empty + DEC_MAX_STAGES);   // 64 floats (also 8 u64 argmax keys at +32)
+    s.abort_s = reinterpret_cast<volatile int *>(s.red + 64);
+    s.sync_ok = s.abort_s + 1;
+    return s;
+}
+
+size_t decode_smem_bytes(int stages, uint32_t slot, uint32_t xs)
+{
+    return (size_t)stages * slot + xs + DEC_MAX_STAGES * 16 + 64 * 4 + 16;
+}
+
+// Grid barrier among the consumer threads of every CTA.  Returns false when
+// this or another CTA gave up waiting; every consumer thread of the CTA gets
+// the same answer (thread 0 decides and publishes it between two CTA
+// barriers), so the CTA's warps always leave the step loop together.
+__device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, unsigned &target)
+{
+    named_bar_sync(1, DEC_NC);
+    if (threadIdx.x == 0) {
+        bool ok = *sm.abort_s == 0;
+        if (ok) {
+            target += gridDim.x;
+            __threadfence();
+            atomicAdd(a.bar, 1u);
+            uint32_t i = 0;
+            while (ld_acquire_u32(a.bar) < target) {
+                if (++i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (i > 16) __nanosleep(64);
+            }
+            __threadfence();
+        }
+        if (!ok) {
+            if (a.err) atomicOr(a.err, CATS_DEVERR_PEER_WAIT);
+            atomicExch(a.abort_flag, 1);
+            *sm.abort_s = 1;
+        }
+        *sm.sync_ok = ok ? 1 : 0;
+    }
+    named_bar_sync(1, DEC_NC);
+    return *sm.sync_ok != 0;
+}
+
+// Bounded wait on an mbarrier that also gives up when the CTA is aborting.
+__device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, const Smem &sm, int *err, int code)
+{
+    for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*sm.abort_s) return false;
+        if (i > 64) __nanosleep(32);
+    }
+    if (err) atomicOr(err, code);
+    *sm.abort_s = 1;
+    return false;
+}
+
+// Warp-collective form for the consumers: every lane observes the phase (so
+// each has the bulk copy's data visible), and the lanes agree on the outcome.
+__device__ __forceinline__ bool ring_wait_warp(uint64_t *bar, uint32_t parity, const Smem &sm, int *err, int code)
+{
+    for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+        const bool ok = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ok)) return true;
+        if (__any_sync(0xffffffffu, *sm.abort_s != 0)) return false;
+        if (i > 64) __nanosleep(32);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (err) atomicOr(err, code);
+        *sm.abort_s = 1;
+    }
+    __syncwarp();
+    return false;
+}
+
+struct Ring {
+    int stage;
+    uint32_t phase;
+};
+
+enum DecEpi { DE_QKV, DE_ADD, DE_SWIGLU, DE_CLS };
+
+// One matvec phase for the consumer warps: this CTA's tiles of weight W,
+// chunks taken from the ring in the producer's order.
+template <int WT, int RPW>
+__device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, const WDesc W, Ring &rg, int epi,
+                                           int l, int pos, unsigned long long &best)
+{
+    constexpr int R = MV_CONSUMER_WARPS * RPW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = blockIdx.x; t < W.n_tiles; t += gridDim.x) {
+        float acc[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; r++) acc[r] = 0.f;
+        for (int s = 0; s < W.nseg; s++) {
+            if (!ring_wait_warp(&sm.full[rg.stage], rg.phase, sm, a.err, CATS_DEVERR_MBAR_FULL)) return false;
+            const int us = min(MV_SEG_UNITS, W.units - MV_SEG_UNITS * s);
+            consume_chunk<WT, RPW>(sm.ring + (size_t)rg.stage * a.slot_bytes, us, s, warp, lane, W.units, sm.xs, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[rg.stage]);
+            if (++rg.stage == a.stages) { rg.stage = 0; rg.phase ^= 1; }
+        }
+#pragma unroll
+        for (int r = 0; r < RPW; r++) acc[r] = warp_sum(acc[r]);
+        if (lane != 0) continue;
+        const int row0 = t * R + warp * RPW;
+        if (row0 >= W.d) continue;
+        if (epi == DE_QKV || epi == DE_SWIGLU) {
+            float v0 = acc[0], v1 = acc[RPW - 1];
+            if (epi == DE_SWIGLU) {
+                a.hb[row0 >> 1] = v0 * (1.f / (1.f + expf(-v0))) * v1;   // silu(w1 x) * (w3 x), :1744-1752
+            } else if (row0 < a.q_dim) {
+                rope_pair(v0, v1, row0, a.head_size, pos);
+                a.q[row0] = v0;
+                a.q[row0 + 1] = v1;
+            } else {
+                const bool is_k = row0 < a.q_dim + a.kv_dim;
+                const int i = row0 - a.q_dim - (is_k ? 0 : a.kv_dim);
+                if (is_k) rope_pair(v0, v1, i, a.head_size, pos);
+                float *c = (is_k ? a.kcache : a.vcache) + ((size_t)l * a.seq_len + pos) * a.kv_dim + i;
+                c[0] = v0;
+                c[1] = v1;
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < RPW; r++) {
+                const int row = row0 + r;
+                if (row >= W.d) break;
+                if (epi == DE_ADD) {
+                    a.x[row] = __ldcg(a.x + row) + acc[r];   // residual (:1731-1733, :1759-1761)
+                } else {
+                    a.logits[row] = acc[r];
+                    const unsigned long long k = argmax_key(acc[r], row);
+                    best = k > best ? k : best;
+                }
+            }
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ int attn_splits(int T, int max_splits)
+{
+    return max(1, min(max_splits, (T + 7) / 8));
+}
+
+// Attention items (head h, time chunk s), one per warp: scores q.k/sqrt(hs)
+// four timesteps at a time (their loads in flight together), online softmax,
+// sum p*v; the partial (max, sum, acc) goes to part[h][s].  The last warp to
+// finish a head merges its chunks into xb (:1706-1722).
+__device__ __forceinline__ void attention_phase(const DecodeArgs &a, int l, int pos)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hs = a.head_size, P = hs + 4;
+    const int T = pos + 1;
+    const int ns = attn_splits(T, a.max_splits);
+    const int chunk = (T + ns - 1) / ns;
+    const float rs = sqrtf((float)hs);
+    const float *kc = a.kcache + (size_t)l * a.seq_len * a.kv_dim;
+    const float *vc = a.vcache + (size_t)l * a.seq_len * a.kv_dim;
+    const int nwarps = gridDim.x * MV_CONSUMER_WARPS;
+    constexpr int U = 4;
+    for (int item = blockIdx.x * MV_CONSUMER_WARPS + warp; item < a.heads * ns; item += nwarps) {
+        const int h = item / ns, s = item % ns;
+        const int t0 = s * chunk, t1 = min(T, t0 + chunk);
+        const int kvo = (h / a.kv_mul) * hs;
+        float qv[8], acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int idx = lane + 32 * k;
+            qv[k] = idx < hs ? __ldcg(a.q + h * hs + idx) : 0.f;
+            acc[k] = 0.f;
+        }
+        float m = -INFINITY, lsum = 0.f;
+        for (int tb = t0; tb < t1; tb += U) {
+            float dot[U], vr[U][8];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int t = min(tb + u, t1 - 1);   // clamped rows are loaded but not used
+                const float *kk = kc + (size_t)t * a.kv_dim + kvo;
+                const float *vv = vc + (size_t)t * a.kv_dim + kvo;
+                dot[u] = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int idx = lane + 32 * k;
+                    if (idx < hs) {
+                        dot[u] = fmaf(qv[k], __ldcg(kk + idx), dot[u]);
+                        vr[u][k] = __ldcg(vv + idx);
+                    } else {
+                        vr[u][k] = 0.f;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) dot[u] = warp_sum(dot[u]);
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (tb + u >= t1) break;
+                const float sc = __fdiv_rn(dot[u], rs);
+                const float mn = fmaxf(m, sc);
+                const float corr = expf(m - mn);
+                const float p = expf(sc - mn);
+                lsum = lsum * corr + p;
+#pragma unroll
+                for (int k = 0; k < 8; k++) acc[k] = acc[k] * corr + p * vr[u][k];
+                m = mn;
+            }
+        }
+        float *out = a.part + ((size_t)h * a.max_splits + s) * P;
+        if (lane == 0) { out[0] = t1 > t0 ? m : -INFINITY; out[1] = lsum; }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int idx = lane + 32 * k;
+            if (idx < hs) out[4 + idx] = acc[k];
+        }
+        // last arriver of head h merges the chunks
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) {
+            __threadfence();
+            prev = atomicAdd(a.head_cnt + h, 1);
+        }
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev != ns - 1) continue;
+        __threadfence();
+        const float *ph = a.part + (size_t)h * a.max_splits * P;
+        float M = -INFINITY;
+        for (int c = 0; c < ns; c++) M = fmaxf(M, __ldcg(ph + (size_t)c * P));
+        float L = 0.f, wts[32];
+        for (int c = 0; c < ns; c++) {
+            const float mc = __ldcg(ph + (size_t)c * P);
+            wts[c & 31] = mc == -INFINITY ? 0.f : expf(mc - M);
+            L += wts[c & 31] * __ldcg(ph + (size_t)c * P + 1);
+        }
+        const float inv = 1.f / L;
+        for (int idx = lane; idx < hs; idx += 32) {
+            float v = 0.f;
+            for (int c = 0; c < ns; c++) v += wts[c & 31] * __ldcg(ph + (size_t)c * P + 4 + idx);
+            a.xb[h * hs + idx] = v * inv;
+        }
+        if (lane == 0) a.head_cnt[h] = 0;
+    }
+}
+
+template <int WT>
+__global__ void __launch_bounds__(MV_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const Smem sm = smem_layout(smem, a);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; s++) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], MV_CONSUMER_WARPS);
+        }
+        *sm.abort_s = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+
+    if (warp == MV_CONSUMER_WARPS) {
+        // ------------------------------------------------------ producer
+        if (lane != 0) return;
+        const uint64_t pol = l2_evict_first_policy();
+        int stage = 0;
+        uint32_t phase = 0, issued = 0, parity = 0;
+        bool ok = true;
+        for (int step = 0; step < a.steps && ok; step++) {
+            for (int wi = 0; wi < a.n_wd && ok; wi++) {
+                const WDesc W = a.wd[wi];
+                for (int t = blockIdx.x; t < W.n_tiles && ok; t += gridDim.x) {
+                    const uint8_t *tb = W.w + (size_t)t * W.tile_bytes;
+                    for (int s = 0; s < W.nseg; s++) {
+                        if (!ring_wait(&sm.empty[stage], phase ^ 1, sm, a.err, CATS_DEVERR_MBAR_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t bytes = s == W.nseg - 1 ? W.last_chunk : W.full_chunk;
+                        mbar_arrive_expect_tx(&sm.full[stage], bytes);
+                        bulk_g2s(sm.ring + (size_t)stage * a.slot_bytes, tb + (size_t)s * W.full_chunk, bytes,
+                                 &sm.full[stage], pol);
+                        issued |= 1u << stage;
+                        parity = (parity & ~(1u << stage)) | (phase << stage);
+                        if (++stage == a.stages) { stage = 0; phase ^= 1; }
+                    }
+                }
+            }
+        }
+        if (!ok) {
+            // the consumers gave up: let every copy in flight land before the CTA exits
+            for (int s = 0; s < a.stages; s++)
+                if (issued & (1u << s)) mbar_wait_bounded(&sm.full[s], (parity >> s) & 1u, nullptr, 0);
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- consumers
+    // Every consumer warp takes the same path through stage_act / grid_sync
+    // (both hold CTA barriers); only grid_sync's broadcast decision ends it.
+    Ring rg{0, 0};
+    unsigned target = 0;
+    unsigned long long best = 0ull;
+    const int tid = threadIdx.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
+    int tk = 0;
+    trace_mark(a, tk);
+    for (int step = 0; step < a.steps; step++) {
+        const int pos = ld_volatile_i32(&a.params->pos);
+        const int token = ld_volatile_i32(&a.params->token);
+        if (pos < 0 || pos >= a.seq_len || token < 0 || token >= a.vocab) {
+            // refused before anything is computed or written (every CTA reads the same values)
+            if (blockIdx.x == 0 && tid == 0 && a.err) atomicOr(a.err, CATS_DEVERR_POS_RANGE);
+            *sm.abort_s = 1;   // the producer stops streaming
+            break;
+        }
+        bool alive = true;
+        for (int l = 0; l < a.n_layers && alive; l++) {
+            const WDesc *wl = a.wd + 4 * l;
+            // qkv: rmsnorm + quantize, [wq;wk;wv], RoPE, k/v into the cache
+            if (l == 0)
+                stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(a.emb + (size_t)token * a.dim), false}, a.dim,
+                              a.rms_att, blockIdx.x == 0 ? a.x : nullptr, sm.xs, sm.red, tid, DEC_NC);
+            else
+                stage_act<WT>(Float4Src{x4, true}, a.dim, a.rms_att + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid,
+                              DEC_NC);
+            trace_mark(a, tk);
+            run_matvec<WT, 2>(a, sm, wl[0], rg, DE_QKV, l, pos, best);
+            trace_mark(a, tk);
+            if (!(alive = grid_sync(a, sm, target))) break;
+            trace_mark(a, tk);
+            attention_phase(a, l, pos);
+            trace_mark(a, tk);
+            if (!(alive = grid_sync(a, sm, target))) break;
+            trace_mark(a, tk);
+            // wo: quantize the attention output, matvec, residual add
+            stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(a.xb), true}, a.q_dim, nullptr, nullptr, sm.xs,
+                          sm.red, tid, DEC_NC);
+            trace_mark(a, tk);
+            run_matvec<WT, 1>(a, sm, wl[1], rg, DE_ADD, l, pos, best);
+            trace_mark(a, tk);
+            if (!(alive = grid_sync(a, sm, target))) break;
+            trace_mark(a, tk);
+            // w1/w3 + SwiGLU
+            stage_act<WT>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid,
+                          DEC_NC);
+            trace_mark(a, tk);
+            run_matvec<WT, 2>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best);
+            trace_mark(a, tk);
+            if (!(alive = grid_sync(a, sm, target))) break;
+            trace_mark(a, tk);
+            // w2 + residual add
+            stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(a.hb), true}, a.hidden, nullptr, nullptr, sm.xs,
+                          sm.red, tid, DEC_NC);
+            trace_mark(a, tk);
+            run_matvec<WT, 1>(a, sm, wl[3], rg, DE_ADD, l, pos, best);
+            trace_mark(a, tk);
+            alive = grid_sync(a, sm, target);
+            trace_mark(a, tk);
+        }
+        if (!alive) break;
+        // classifier + greedy argmax
+        stage_act<WT>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
+        best = 0ull;
+        trace_mark(a, tk);
+        run_matvec<WT, 1>(a, sm, a.wd[4 * a.n_layers], rg, DE_CLS, 0, pos, best);
+        trace_mark(a, tk);
+        unsigned long long *keys = reinterpret_cast<unsigned long long *>(sm.red + 32);
+        if (lane == 0) keys[warp] = best;
+        named_bar_sync(1, DEC_NC);
+        if (tid == 0) {
+            unsigned long long mk = 0;
+            for (int w = 0; w < MV_CONSUMER_WARPS; w++) mk = keys[w] > mk ? keys[w] : mk;
+            if (mk) atomicMax(a.argmax, mk);
+        }
+        if (!grid_sync(a, sm, target)) break;
+        if (blockIdx.x == 0 && tid == 0) {
+            const unsigned long long k = atomicAdd(a.argmax, 0ull);
+            int idx = 0x7fffffff - (int)(uint32_t)(k & 0xffffffffu);
+            if (k == 0ull || idx < 0 || idx >= a.vocab) {
+                idx = 0;
+                if (a.err) atomicOr(a.err, CATS_DEVERR_TOKEN_RANGE);
+            }
+            StepParams *p = a.params;
+            const int n = p->steps;
+            if (a.tok_log && n >= 0 && n < a.tok_cap) a.tok_log[n] = idx;
+            p->next = idx;
+            p->token = idx;
+            p->pos = pos + 1;
+            p->steps = n + 1;
+            *a.argmax = 0ull;
+            __threadfence();
+        }
+        if (!grid_sync(a, sm, target)) break;
+        trace_mark(a, tk);
+    }
+}
+
+// ------------------------------------------------------------------- host
+static WDesc to_desc(const DevWeight &W)
+{
+    WDesc d;
+    d.w = W.ptr;
+    d.n = W.L.n;
+    d.d = W.L.d;
+    d.R = W.L.R;
+    d.rpw = W.L.rpw;
+    d.units = W.L.units;
+    d.nseg = W.L.nseg;
+    d.n_tiles = W.L.n_tiles;
+    d.full_chunk = W.L.full_chunk;
+    d.last_chunk = W.L.last_chunk;
+    d.tile_bytes = W.L.tile_bytes;
+    return d;
+}
+
+int decode_prepare(LlmModel *m)
+{
+    if (m->wdesc) return E_OK;
+    const LlmConfig &c = m->c;
+    std::vector<WDesc> v;
+    uint32_t slot = 0;
+    int maxn = std::max(std::max(c.dim, m->hidden_loc), m->q_dim);
+    for (int l = 0; l < c.n_layers; l++) {
+        for (const DevWeight *w : {&m->qkv[l], &m->wo[l], &m->w13[l], &m->w2[l]}) {
+            v.push_back(to_desc(*w));
+            slot = std::max(slot, w->L.full_chunk);
+        }
+    }
+    v.push_back(to_desc(m->cls));
+    slot = std::max(slot, m->cls.L.full_chunk);
+    slot = (uint32_t)round_up(slot, 128);
+    const uint32_t xs = (uint32_t)round_up(c.wtype == W_F32 ? (size_t)maxn * 4 : (size_t)(maxn / 32) * 40, 128);
+    const size_t cap = 227 * 1024;
+    const size_t fixed = decode_smem_bytes(0, slot, xs);
+    if (fixed + 2 * slot > cap || m->head_size > 256 || m->head_size % 4) return E_UNSUPPORTED;
+    m->dec_stages = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / slot);
+    m->dec_slot = slot;
+    m->dec_xs = xs;
+    m->dec_max_splits = 32;
+    if (cudaMalloc(&m->wdesc, v.size() * sizeof(WDesc)) != cudaSuccess) return E_NOMEM;
+    if (cudaMalloc(&m->dec_part, (size_t)m->heads_loc * m->dec_max_splits * (m->head_size + 4) * 4) != cudaSuccess)
+        return E_NOMEM;
+    if (cudaMalloc(&m->dec_bar, 16) != cudaSuccess) return E_NOMEM;
+    m->n_wdesc = (int)v.size();
+    if (cudaMemcpy(m->wdesc, v.data(), v.size() * sizeof(WDesc), cudaMemcpyHostToDevice) != cudaSuccess) return E_CUDA;
+    return E_OK;
+}
+
+template <int WT>
+static cudaError_t launch_decode_t(const DecodeArgs &a, size_t smem, int grid, cudaStream_t st)
+{
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_decode<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e) return e;
+        attr = true;
+    } else {
+        cudaFuncSetAttribute(k_decode<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(MV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeCooperative;
+    attrs[0].val.cooperative = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_decode<WT>, a);
+}
+
+cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, unsigned long long *trace,
+                          int trace_stride)
+{
+    if (steps <= 0) return cudaSuccess;
+    int rc = decode_prepare(m);
+    if (rc) return rc == E_NOMEM ? cudaErrorMemoryAllocation : cudaErrorInvalidValue;
+    const LlmConfig &c = m->c;
+    DecodeArgs a;
+    a.wd = static_cast<const WDesc *>(m->wdesc);
+    a.n_wd = m->n_wdesc;
+    a.n_layers = c.n_layers;
+    a.dim = c.dim;
+    a.hidden = m->hidden_loc;
+    a.q_dim = m->q_dim;
+    a.kv_dim = m->kv_dim;
+    a.head_size = m->head_size;
+    a.kv_mul = c.n_heads / c.n_kv_heads;
+    a.heads = m->heads_loc;
+    a.seq_len = c.seq_len;
+    a.vocab = c.vocab;
+    a.emb = m->emb;
+    a.rms_att = m->rms_att;
+    a.rms_ffn = m->rms_ffn;
+    a.rms_final = m->rms_final;
+    a.x = m->x;
+    a.q = m->q;
+    a.xb = m->xb;
+    a.hb = m->hb;
+    a.logits = m->logits;
+    a.kcache = m->kcache;
+    a.vcache = m->vcache;
+    a.part = m->dec_part;
+    a.head_cnt = m->counters;
+    a.max_splits = m->dec_max_splits;
+    a.params = m->params;
+    a.argmax = m->argmax;
+    a.tok_log = tok_log;
+    a.tok_cap = tok_cap;
+    a.bar = m->dec_bar;
+    a.abort_flag = reinterpret_cast<int *>(m->dec_bar + 1);
+    a.steps = steps;
+    a.stages = m->dec_stages;
+    a.slot_bytes = m->dec_slot;
+    a.xs_bytes = m->dec_xs;
+    a.err = m->err;
+    a.trace = trace;
+    a.trace_stride = trace_stride;
+    const size_t smem = decode_smem_bytes(a.stages, a.slot_bytes, a.xs_bytes);
+    cudaError_t e = cudaMemsetAsync(m->dec_bar, 0, 16, m->stream);
+    if (e) return e;
+    const int grid = matvec_num_sms();
+    switch (c.wtype) {
+    case W_F32: return launch_decode_t<W_F32>(a, smem, grid, m->stream);
+    case W_Q4_0: return launch_decode_t<W_Q4_0>(a, smem, grid, m->stream);
+    case W_Q8_0: return launch_decode_t<W_Q8_0>(a, smem, grid, m->stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+} // namespace cats

@@ -219,7 +219,7 @@ __global__ void k_advance(StepParams *p, unsigned long long *argmax, int vocab, 
 static int pick_stages(const WeightLayout &L)
 {
     const size_t stride = round_up(L.full_chunk, 128);
-    int s = (int)(65536 / stride);
+    int s = (int)(MV_STAGE_BUDGET / stride);
     return std::max(2, std::min(8, s));
 }
 
@@ -317,6 +317,12 @@ void llm_free(LlmModel *m)
     float **fp[] = {&m->x, &m->x2, &m->delta, &m->q, &m->xb, &m->hb, &m->logits, &m->kcache, &m->vcache,
                     &m->part, &m->emb, &m->rms_att, &m->rms_ffn, &m->rms_final};
     for (auto p : fp) if (*p) { cudaFree(*p); *p = nullptr; }
+    if (m->wdesc) cudaFree(m->wdesc);
+    if (m->dec_part) cudaFree(m->dec_part);
+    if (m->dec_bar) cudaFree(m->dec_bar);
+    m->wdesc = nullptr;
+    m->dec_part = nullptr;
+    m->dec_bar = nullptr;
     if (m->counters) cudaFree(m->counters);
     if (m->argmax) cudaFree(m->argmax);
     if (m->params) cudaFree(m->params);

@@ -50,6 +50,13 @@ struct LlmModel {
     cudaGraphExec_t exec = nullptr;
     bool weights_ready = false;
     int stages_cache = 0;
+    // persistent decode kernel (decode.cu)
+    void *wdesc = nullptr;                // device array of weight descriptors in step order
+    int n_wdesc = 0;
+    float *dec_part = nullptr;            // attention chunk partials [heads][max_splits][hs + 4]
+    unsigned int *dec_bar = nullptr;      // [0] grid barrier counter, [1] abort flag
+    int dec_stages = 0, dec_max_splits = 32;
+    uint32_t dec_slot = 0, dec_xs = 0;
     // tensor parallel hooks (NCCL), null when tp_size == 1
     AllreduceFn allreduce = nullptr;
     ArgmaxReduceFn argmax_reduce = nullptr;
@@ -67,6 +74,15 @@ int llm_init_random(LlmModel *m, unsigned long long seed, float std);
 // enqueue one decode step (token/pos from m->params) on m->stream (graph if captured)
 cudaError_t llm_enqueue_step(LlmModel *m, bool advance);
 cudaError_t llm_build_graph(LlmModel *m);
+// Persistent cooperative decode: `steps` greedy tokens in one launch on
+// m->stream, starting from m->params (token, pos); tok_log (device, may be
+// null) receives the argmax ids.
+// trace (device, may be null): [grid][trace_stride] globaltimer stamps of each
+// CTA's phase boundaries (after staging, after the matvec/attention work,
+// after each grid barrier).
+cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, unsigned long long *trace = nullptr,
+                          int trace_stride = 0);
+int decode_prepare(LlmModel *m);
 // Time `reps` passes over every layer's matvec of one kind (0 qkv, 1 wo, 2 w13,
 // 3 w2, 4 classifier) launched back to back with PDL on the model's stream, as
 // in the decode step but storing into scratch.  Outputs the mean device time

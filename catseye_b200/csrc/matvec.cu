@@ -10,7 +10,7 @@
 // as the reference does.  The producer issues its first copies before the
 // programmatic-dependent-launch wait, so weight streaming overlaps the tail of
 // the kernel before it.
-#include "matvec.cuh"
+#include "mv_device.cuh"
 #include <algorithm>
 
 namespace cats {
@@ -98,42 +98,7 @@ cudaError_t launch_repack(const uint8_t *src, uint8_t *dst, const WeightLayout &
     return cudaGetLastError();
 }
 
-// ------------------------------------------------- Q8 quantizer (shared math)
-// Eight consecutive lanes hold one 32-element block, four elements each
-// (lane g of the group holds elements 4g..4g+3).  Implements the AVX
-// quantize_q8 (llm/catseye_llm.h:155-225): d = amax/127 and id = 127/amax,
-// both correctly rounded floats (the reference divides in double and stores
-// float); q = round-half-even(x*id), saturated to int8.  scalar_mode follows
-// the plain build (:227-251): id = 1/d, q = roundf(x*id).
-__device__ __forceinline__ uint32_t q8_group_quant(float4 v, unsigned gmask, bool scalar_mode, float &d_out,
-                                                   int &sum_out)
-{
-    float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    a = fmaxf(a, __shfl_xor_sync(gmask, a, 1));
-    a = fmaxf(a, __shfl_xor_sync(gmask, a, 2));
-    a = fmaxf(a, __shfl_xor_sync(gmask, a, 4));
-    const float d = __fdiv_rn(a, 127.f);
-    int q[4];
-    const float e[4] = {v.x, v.y, v.z, v.w};
-    if (!scalar_mode) {
-        const float id = a != 0.f ? __fdiv_rn(127.f, a) : 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) q[k] = max(-128, min(127, __float2int_rn(__fmul_rn(e[k], id))));
-    } else {
-        const float id = d != 0.f ? (float)(1.0 / (double)d) : 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) q[k] = (int)(signed char)(int)roundf(__fmul_rn(e[k], id));
-    }
-    int s = q[0] + q[1] + q[2] + q[3];
-    s += __shfl_xor_sync(gmask, s, 1);
-    s += __shfl_xor_sync(gmask, s, 2);
-    s += __shfl_xor_sync(gmask, s, 4);
-    d_out = d;
-    sum_out = s;
-    return (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
-           ((uint32_t)(q[3] & 0xff) << 24);
-}
-
+// ------------------------------------------------- Q8 quantizer (standalone)
 __global__ void k_quantize_q8(int8_t *__restrict__ q, const float *__restrict__ x, int n, int scalar_mode)
 {
     const int n4 = n / 4;
@@ -214,157 +179,6 @@ __host__ __device__ inline SmemPlan smem_plan(const MatvecArgs &a, int type)
 
 size_t matvec_smem_bytes(const MatvecArgs &a, int type) { return smem_plan(a, type).total; }
 
-// Stage the activation into shared memory (consumer warps only, 256 threads).
-template <int WT>
-__device__ __forceinline__ void stage_x(const MatvecArgs &a, uint8_t *xs, float *red, int tid)
-{
-    const int n = a.n;
-    const int lane = tid & 31, warp = tid >> 5;
-    const unsigned gmask = 0xffu << (lane & 24);
-    const int units = a.units;
-    uint8_t *xlo = xs, *xhi = xs + (size_t)units * 16;
-    float2 *dxs = reinterpret_cast<float2 *>(xs + (size_t)units * 32);
-
-    if (a.xmode == XM_Q8_RAW) {
-        const uint8_t *xq = static_cast<const uint8_t *>(a.x);
-        const int nw = n / 4;   // 8 words per 36-byte block
-        for (int i = tid; i < nw; i += 256) {
-            const int b = i >> 3, g = i & 7;
-            const uint32_t wv = *reinterpret_cast<const uint32_t *>(xq + (size_t)b * 36 + g * 4);
-            int s = __dp4a((int)wv, 0x01010101, 0);
-            s += __shfl_xor_sync(gmask, s, 1);
-            s += __shfl_xor_sync(gmask, s, 2);
-            s += __shfl_xor_sync(gmask, s, 4);
-            uint8_t *dst = (g < 4 ? xlo : xhi) + (size_t)b * 16 + (g & 3) * 4;
-            *reinterpret_cast<uint32_t *>(dst) = wv;
-            if (g == 0) dxs[b] = make_float2(*reinterpret_cast<const float *>(xq + (size_t)b * 36 + 32), __int_as_float(s));
-        }
-        named_bar_sync(1, 32 * MV_CONSUMER_WARPS);
-        return;
-    }
-
-    const float *src = static_cast<const float *>(a.x) + (a.x_row ? (size_t)(*a.x_row) * n : 0);
-    const float4 *src4 = reinterpret_cast<const float4 *>(src);
-    const int n4 = n / 4;
-    float scale = 1.f;
-    if (a.norm_w) {
-        // rmsnorm (llm/catseye_llm.h:684-698): ss = mean(x^2) + 1e-5; o = w * (x / sqrt(ss))
-        float ss = 0.f;
-        for (int i = tid; i < n4; i += 256) {
-            float4 v = src4[i];
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        named_bar_sync(1, 32 * MV_CONSUMER_WARPS);
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < MV_CONSUMER_WARPS; w++) tot += red[w];
-        tot = __fdiv_rn(tot, (float)n);
-        tot = __fadd_rn(tot, 1e-5f);
-        scale = __fdiv_rn(1.f, __fsqrt_rn(tot));
-    }
-    const float4 *nw4 = reinterpret_cast<const float4 *>(a.norm_w);
-    const bool wb = a.x_writeback != nullptr && blockIdx.x == 0;
-    float4 *wb4 = reinterpret_cast<float4 *>(a.x_writeback);
-    for (int i = tid; i < n4; i += 256) {
-        float4 v = src4[i];
-        if (wb) wb4[i] = v;
-        if (a.norm_w) {
-            const float4 g = nw4[i];
-            v.x = __fmul_rn(g.x, __fmul_rn(scale, v.x));
-            v.y = __fmul_rn(g.y, __fmul_rn(scale, v.y));
-            v.z = __fmul_rn(g.z, __fmul_rn(scale, v.z));
-            v.w = __fmul_rn(g.w, __fmul_rn(scale, v.w));
-        }
-        if (WT == W_F32) {
-            reinterpret_cast<float4 *>(xs)[i] = v;
-        } else {
-            float d;
-            int s;
-            const uint32_t packed = q8_group_quant(v, gmask, false, d, s);
-            const int b = i >> 3, g = i & 7;
-            uint8_t *dst = (g < 4 ? xlo : xhi) + (size_t)b * 16 + (g & 3) * 4;
-            *reinterpret_cast<uint32_t *>(dst) = packed;
-            if (g == 0) dxs[b] = make_float2(d, __int_as_float(s));
-        }
-    }
-    named_bar_sync(1, 32 * MV_CONSUMER_WARPS);
-}
-
-template <int WT, int RPW>
-__device__ __forceinline__ void consume_chunk(const uint8_t *ch, int us, int s, int warp, int lane, int units,
-                                              const uint8_t *xs, float (&acc)[RPW])
-{
-    constexpr int R = MV_CONSUMER_WARPS * RPW;
-    const int u = s * MV_SEG_UNITS + lane;
-    if (WT == W_F32) {
-        const float4 xv = reinterpret_cast<const float4 *>(xs)[u];
-#pragma unroll
-        for (int r = 0; r < RPW; r++) {
-            const int rr = warp * RPW + r;
-            const float4 wv = *reinterpret_cast<const float4 *>(ch + ((size_t)rr * us + lane) * 16);
-            acc[r] = fmaf(wv.x, xv.x, acc[r]);
-            acc[r] = fmaf(wv.y, xv.y, acc[r]);
-            acc[r] = fmaf(wv.z, xv.z, acc[r]);
-            acc[r] = fmaf(wv.w, xv.w, acc[r]);
-        }
-        return;
-    }
-    const int4 xl = *reinterpret_cast<const int4 *>(xs + (size_t)u * 16);
-    const int4 xh = *reinterpret_cast<const int4 *>(xs + (size_t)units * 16 + (size_t)u * 16);
-    const float2 dxs = reinterpret_cast<const float2 *>(xs + (size_t)units * 32)[u];
-    const uint32_t sstride = (uint32_t)round_up((size_t)us * 2, 16);
-    const uint32_t ub = WT == W_Q4_0 ? 16 : 32;
-    const uint8_t *scales = ch + (size_t)R * us * ub;
-#pragma unroll
-    for (int r = 0; r < RPW; r++) {
-        const int rr = warp * RPW + r;
-        const uint16_t sc = *reinterpret_cast<const uint16_t *>(scales + rr * sstride + lane * 2);
-        int isum;
-        if (WT == W_Q4_0) {
-            const uint4 wq = *reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + lane) * 16);
-            const uint32_t m = 0x0f0f0f0fu;
-            isum = dp4a_us(wq.x & m, xl.x, 0);
-            isum = dp4a_us(wq.y & m, xl.y, isum);
-            isum = dp4a_us(wq.z & m, xl.z, isum);
-            isum = dp4a_us(wq.w & m, xl.w, isum);
-            isum = dp4a_us((wq.x >> 4) & m, xh.x, isum);
-            isum = dp4a_us((wq.y >> 4) & m, xh.y, isum);
-            isum = dp4a_us((wq.z >> 4) & m, xh.z, isum);
-            isum = dp4a_us((wq.w >> 4) & m, xh.w, isum);
-            isum -= 8 * __float_as_int(dxs.y);   // (nibble - 8) * q summed = dp4a - 8 * sum(q)
-        } else {
-            const int4 wl = *reinterpret_cast<const int4 *>(ch + ((size_t)(rr * 2) * us + lane) * 16);
-            const int4 wh = *reinterpret_cast<const int4 *>(ch + ((size_t)(rr * 2 + 1) * us + lane) * 16);
-            isum = __dp4a(wl.x, xl.x, 0);
-            isum = __dp4a(wl.y, xl.y, isum);
-            isum = __dp4a(wl.z, xl.z, isum);
-            isum = __dp4a(wl.w, xl.w, isum);
-            isum = __dp4a(wh.x, xh.x, isum);
-            isum = __dp4a(wh.y, xh.y, isum);
-            isum = __dp4a(wh.z, xh.z, isum);
-            isum = __dp4a(wh.w, xh.w, isum);
-        }
-        const float delta = __fmul_rn(half_bits_to_float(sc), dxs.x);   // d_w * d_x in float
-        acc[r] = fmaf(delta, (float)isum, acc[r]);
-    }
-}
-
-__device__ __forceinline__ void rope_pair(float &a, float &b, int i, int head_size, int pos)
-{
-    // rope_llama (llm/catseye_llm.h:1597-1620)
-    const int hd = i % head_size;
-    const float p = powf(10000.f, (float)hd / (float)head_size);
-    const float freq = (float)(1.0 / (double)p);
-    const float val = (float)pos * freq;
-    float s, c;
-    sincosf(val, &s, &c);
-    const float a0 = a, b0 = b;
-    a = a0 * c - b0 * s;
-    b = a0 * s + b0 * c;
-}
-
 template <int WT, int RPW>
 __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant__ MatvecArgs a)
 {
@@ -421,7 +235,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
 
     // ---------------- consumers
     pdl_wait();
-    stage_x<WT>(a, xs, red, threadIdx.x);
+    constexpr int NC = 32 * MV_CONSUMER_WARPS;
+    if (a.xmode == XM_Q8_RAW) {
+        stage_q8_raw(static_cast<const uint8_t *>(a.x), a.n, xs, threadIdx.x, NC);
+    } else {
+        const float *src = static_cast<const float *>(a.x) + (a.x_row ? (size_t)(*a.x_row) * a.n : 0);
+        stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(src), false}, a.n, a.norm_w,
+                      blockIdx.x == 0 ? a.x_writeback : nullptr, xs, red, threadIdx.x, NC);
+    }
     pdl_launch_dependents();
 
     int stage = 0;
@@ -438,8 +259,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
         for (int s = 0; s < a.nseg; s++) {
             if (!mbar_wait_bounded(&full[stage], phase, a.err, CATS_DEVERR_MBAR_FULL)) { ok = false; break; }
             const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
-            if (lane < us)
-                consume_chunk<WT, RPW>(smem + (size_t)stage * sp.stage_stride, us, s, warp, lane, a.units, xs, acc);
+            consume_chunk<WT, RPW>(smem + (size_t)stage * sp.stage_stride, us, s, warp, lane, a.units, xs, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
             if (++stage == stages) { stage = 0; phase ^= 1; }

@@ -20,7 +20,8 @@ namespace cats {
 
 constexpr int MV_CONSUMER_WARPS = 8;
 constexpr int MV_THREADS = 32 * (MV_CONSUMER_WARPS + 1);   // + one producer warp
-constexpr int MV_SEG_UNITS = 32;                            // units per segment (one per lane)
+constexpr int MV_SEG_UNITS = 64;                            // units per segment (two per lane)
+constexpr size_t MV_STAGE_BUDGET = 96 * 1024;               // ring bytes of the standalone matvec
 
 struct WeightLayout {
     int type = 0;        // W_F32 / W_Q4_0 / W_Q8_0

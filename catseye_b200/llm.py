@@ -13,6 +13,7 @@ import numpy as np
 from . import _lib
 
 F32, Q4_0, Q8_0 = 0, 2, 8
+ENGINE_PERSISTENT, ENGINE_GRAPH = 0, 1
 
 
 @dataclass(frozen=True)
@@ -90,6 +91,11 @@ class GpuLLM:
         _lib.check(self.lib.cats_gpu_llm_generate(self.h, token, pos, steps, C.c_void_p(toks.ctypes.data)), "generate")
         return toks[:steps]
 
+    def set_engine(self, engine):
+        """ENGINE_PERSISTENT (default): one cooperative kernel runs whole tokens;
+        ENGINE_GRAPH: a CUDA graph of per-phase kernels."""
+        _lib.check(self.lib.cats_gpu_llm_set_engine(self.h, engine), "set_engine")
+
     def set_position(self, token, pos):
         _lib.check(self.lib.cats_gpu_llm_set_position(self.h, token, pos), "set_position")
 
@@ -120,6 +126,14 @@ class GpuLLM:
         ms, by = C.c_float(), C.c_double()
         _lib.check(self.lib.cats_gpu_llm_time_matvec(self.h, kind, reps, C.byref(ms), C.byref(by)), "time_matvec")
         return ms.value, by.value
+
+    def trace_step(self, token, pos, per_cta=1024):
+        """One traced step of the persistent engine: [ctas][per_cta] ns stamps."""
+        buf = np.zeros(148 * per_cta, dtype=np.uint64)
+        ctas = C.c_int()
+        _lib.check(self.lib.cats_gpu_llm_trace_step(self.h, token, pos, C.c_void_p(buf.ctypes.data), per_cta,
+                                                    C.byref(ctas)), "trace_step")
+        return buf[:ctas.value * per_cta].reshape(ctas.value, per_cta)
 
     def close(self):
         if self.h:

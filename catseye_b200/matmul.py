@@ -46,8 +46,7 @@ def unregister_weight(w):
 def matmul(t, xout, x, w, n, d):
     """xout[:d] = W x; x is fp32 (F32) or Q8 blocks (quantized types) as quantize() made them."""
     lib = _lib.init()
-    getattr(lib, _MATMUL[t])(_p(xout), _p(x), _p(w), n, d)
-    _lib.check(None, _MATMUL[t])
+    _lib.call_void(getattr(lib, _MATMUL[t]), _p(xout), _p(x), _p(w), n, d, what=_MATMUL[t])
     return xout
 
 
@@ -56,16 +55,14 @@ def quantize(x):
     lib = _lib.init()
     x = np.ascontiguousarray(x, dtype=np.float32)
     q = np.zeros(x.size // 32 * 36, dtype=np.int8)
-    lib.cats_gpu_quantize_q8(_p(q), _p(x), x.size)
-    _lib.check(None, "quantize_q8")
+    _lib.call_void(lib.cats_gpu_quantize_q8, _p(q), _p(x), x.size, what="quantize_q8")
     return q
 
 
 def dequantize(t, w, row, n):
     lib = _lib.init()
     y = np.zeros(n, dtype=np.float32)
-    getattr(lib, _DEQUANT[t])(_p(y), _p(np.ascontiguousarray(w)), row, n)
-    _lib.check(None, _DEQUANT[t])
+    _lib.call_void(getattr(lib, _DEQUANT[t]), _p(y), _p(np.ascontiguousarray(w)), row, n, what=_DEQUANT[t])
     return y
 
 
@@ -91,9 +88,8 @@ def dequantize_dev(t, y, w, n, rows, stream=None):
 def sgemm(ta, tb, m, n, k, alpha, a, b, beta, c):
     """C = alpha*op(A)*op(B) + beta*C on host arrays (C updated in place and returned)."""
     lib = _lib.init()
-    lib.cats_sgemm(ta.encode(), tb.encode(), m, n, k, alpha, _p(np.ascontiguousarray(a, np.float32)),
-                   _p(np.ascontiguousarray(b, np.float32)), beta, _p(c))
-    _lib.check(None, "cats_sgemm")
+    _lib.call_void(lib.cats_sgemm, ta.encode(), tb.encode(), m, n, k, alpha, _p(np.ascontiguousarray(a, np.float32)),
+                   _p(np.ascontiguousarray(b, np.float32)), beta, _p(c), what="cats_sgemm")
     return c
 
 

@@ -132,6 +132,19 @@ float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *m, float *l
  * each step's argmax (sample_argmax, :1944-1956) feeding the next, with no
  * host round trip.  tokens_host (may be NULL) receives the steps' argmax ids. */
 int cats_gpu_llm_generate(cats_gpu_llm *m, int token, int pos, int steps, int *tokens_host);
+/* Decode engines: the persistent cooperative kernel (one launch runs whole
+ * tokens; the default) or a CUDA graph of per-phase kernels chained with
+ * programmatic dependent launch. */
+#define CATS_ENGINE_PERSISTENT 0
+#define CATS_ENGINE_GRAPH      1
+int cats_gpu_llm_set_engine(cats_gpu_llm *m, int engine);
+/* One step of the persistent engine with a phase timeline, the counterpart
+ * of the reference's per-layer CATS_CHECK timings (catseye.h:2110-2117):
+ * host receives [ctas][per_cta] globaltimer stamps (ns) taken by each CTA
+ * after staging an activation, after its matvec or attention work, and after
+ * each grid barrier; *ctas receives the grid size (host must hold 148*per_cta). */
+int cats_gpu_llm_trace_step(cats_gpu_llm *m, int token, int pos, unsigned long long *host, int per_cta,
+                            int *ctas);
 /* Asynchronous form for timing: enqueue `steps` greedy steps on the model's stream. */
 int cats_gpu_llm_enqueue(cats_gpu_llm *m, int steps);
 int cats_gpu_llm_set_position(cats_gpu_llm *m, int token, int pos);

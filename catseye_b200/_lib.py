@@ -62,6 +62,7 @@ SIGNATURES = {
     "cats_gemm_rnt": (None, [_i, _i, _i, _f, _vp, _vp, _f, _vp]),
     "cats_gemm_rtn": (None, [_i, _i, _i, _f, _vp, _vp, _f, _vp]),
     "cats_sgemm_dev": (_i, [_ch, _ch, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
+    "cats_sgemm_dev_noalloc": (_i, [_ch, _ch, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
 }
 
 _LIB = None

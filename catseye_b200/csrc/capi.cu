@@ -168,6 +168,11 @@ void matmul_host(int type, float *xout, void *x, void *w, int n, int d, const ch
 
 } // namespace
 
+namespace cats {
+// the sticky status, for entry points defined in other files
+int capi_fail(int code, const char *what) { return fail(code, what); }
+}
+
 // ===================================================================== C ABI
 extern "C" {
 

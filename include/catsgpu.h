@@ -182,6 +182,25 @@ void cats_gemm_rtn(int M, int N, int K, float alpha, float *A, float *B, float b
 int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda,
                    const float *b, int ldb, float beta, float *c, int ldc, void *stream);
 
+/* cats_sgemm_dev for callers that cannot allocate device memory: a process
+ * whose device memory another allocator already owns, or a latency-critical
+ * loop that must not meet cudaMalloc's implicit device synchronisation.  It
+ * has no counterpart in the reference.  Same arguments and arithmetic as
+ * cats_sgemm_dev, but it allocates nothing: no cudaMalloc, no cudaFree, and
+ * no call to cats_gpu_init (it runs on the current device and the given
+ * stream, NULL = the default stream).  Skinny problems split K into a
+ * workspace that is a fixed array compiled into the library:
+ * CATS_SGEMM_NOALLOC_SCRATCH_FLOATS floats (8 MiB), held by every GPU that
+ * loads the library until the process exits.  A problem whose split-K
+ * workspace would exceed it is rejected with CATS_ERR_ARG before any launch.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and the SM count; make that first call before any
+ * stream capture.  Every call shares the one array, so calls that overlap on
+ * the GPU (other streams, other host threads) race on it; serialize them. */
+#define CATS_SGEMM_NOALLOC_SCRATCH_FLOATS (2 * 1024 * 1024)
+int cats_sgemm_dev_noalloc(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda,
+                           const float *b, int ldb, float beta, float *c, int ldc, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -77,7 +77,7 @@ def load(path=None):
     global _LIB
     if _LIB is not None:
         return _LIB
-    path = path or LIB_PATH
+    path = path or os.environ.get("CATS_GPU_LIB") or LIB_PATH
     if not os.path.exists(path):
         raise CatsGpuError(f"{path} is missing: build it with `make -C catseye_b200/csrc` "
                            "(or __graft_entry__.build()); there is no CPU fallback")

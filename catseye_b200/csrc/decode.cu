@@ -5,28 +5,47 @@
 //
 //  * A producer warp walks the weights of every layer in step order (qkv, wo,
 //    w1/w3, w2 per layer, then the classifier; this CTA's tiles of each) and
-//    streams their (tile, segment) chunks into a deep shared-memory ring with
-//    1-D bulk copies (TMA engine, L2 evict-first).  It never waits for an
+//    streams their (tile, segment) chunks into shared-memory rings with 1-D
+//    bulk copies (TMA engine, L2 evict-first).  It never waits for an
 //    activation, so HBM keeps streaming through every phase boundary.
-//  * Eight consumer warps run the phases.  Between phases the CTAs meet at a
-//    grid barrier (bounded spin on a global counter); after it each CTA
-//    stages the phase's activation (rmsnorm + quantize_q8) in shared memory
-//    and dots the ring's chunks against it.
-//  * Attention (:1677-1723) is split over time: each warp scores one
-//    (head, time-chunk) item with an online softmax; the wo phase merges the
-//    chunks while staging its input.
+//  * Two consumer warp-groups of eight warps run the phases.  The CTA's tiles
+//    of a weight are taken in pairs, one per group; each group has a ring of
+//    its own (slots plus full/empty mbarriers) and the producer alternates
+//    between the two rings, so both groups dot in parallel and every ring
+//    has one consumer that waits on each of its chunks in order (a group
+//    never polls a slot whose previous chunk belongs to someone else, which
+//    could show it a phase that has not started yet).  Between phases all
+//    CTAs meet at a grid barrier (bounded spin on a global counter); after it
+//    each CTA stages the phase's activation (rmsnorm + quantize_q8) in shared
+//    memory, with every load of a thread issued before any is used.
+//  * Attention (:1677-1723) is split over time into short (head, chunk)
+//    items, one per warp, four timesteps' K and V rows in flight at a time,
+//    online softmax; the last warp to finish a head merges its chunks.
 //  * After the classifier (:1765-1770) CTA 0 turns the greedy argmax
 //    (:1944-1956) into the next token and position, so `steps` tokens decode
 //    with no host round trip.
+//
+// Shared memory: a fixed 1 KB header (the mbarriers at offset 0, reduction
+// scratch, flags), then the two rings (group g's slot k at index
+// g * stages + k), then the staged activation.  The mbarriers are
+// invalidated before the kernel exits.
 #include "llm.cuh"
 #include "mv_device.cuh"
 #include <algorithm>
 
 namespace cats {
 
-constexpr int DEC_NC = 32 * MV_CONSUMER_WARPS;   // consumer threads
-constexpr int DEC_MAX_STAGES = 32;
-constexpr uint32_t GRID_SPIN_LIMIT = 1u << 23;   // ~1 s of polling with backoff
+constexpr int DEC_GROUPS = 2;                                 // consumer warp-groups
+constexpr int DEC_GW = MV_CONSUMER_WARPS;                     // warps per group (8): R = 16 rows = 8 x 2
+constexpr int DEC_WARPS = DEC_GROUPS * DEC_GW;                // 16 consumer warps
+constexpr int DEC_NC = 32 * DEC_WARPS;                        // 512 consumer threads
+constexpr int DEC_THREADS = DEC_NC + 32;                      // + the producer warp
+constexpr int DEC_MAX_STAGES = 16;                            // per ring (two rings)
+constexpr int DEC_RPW = 2;                                    // rows per warp in a 16-row tile
+constexpr int DEC_MAX_HS = 128;                               // head size held as one float4 per lane
+constexpr int DEC_STAGE_V = 4;                                // staging loads in flight per thread (512 threads)
+constexpr uint32_t DEC_HEADER = 1024;                         // mbarriers + scratch at the start of smem
+constexpr uint32_t GRID_SPIN_LIMIT = 1u << 23;                // ~1 s of polling with backoff
 
 struct WDesc {
     const uint8_t *w;
@@ -50,7 +69,7 @@ struct DecodeArgs {
     unsigned int *bar;   // grid barrier counter, zeroed before each launch
     int *abort_flag;     // set by any CTA whose bounded wait expired
     int steps;
-    int stages;
+    int stages;          // slots per ring
     uint32_t slot_bytes, xs_bytes;
     int *err;
     unsigned long long *trace;   // optional per-CTA phase timeline (globaltimer ns), trace_stride records each
@@ -94,20 +113,20 @@ struct Smem {
 __device__ __forceinline__ Smem smem_layout(uint8_t *base, const DecodeArgs &a)
 {
     Smem s;
-    s.ring = base;
-    s.xs = base + (size_t)a.stages * a.slot_bytes;
-    uint8_t *p = s.xs + a.xs_bytes;
-    s.full = reinterpret_cast<uint64_t *>(p);
-    s.empty = s.full + DEC_MAX_STAGES;
-    s.red = reinterpret_cast<float *>(s.empty + DEC_MAX_STAGES);   // 64 floats (also 8 u64 argmax keys at +32)
+    s.full = reinterpret_cast<uint64_t *>(base);
+    s.empty = s.full + DEC_GROUPS * DEC_MAX_STAGES;
+    s.red = reinterpret_cast<float *>(s.empty + DEC_GROUPS * DEC_MAX_STAGES);   // 64 floats (16 u64 keys at +32)
     s.abort_s = reinterpret_cast<volatile int *>(s.red + 64);
     s.sync_ok = s.abort_s + 1;
+    s.ring = base + DEC_HEADER;
+    s.xs = s.ring + (size_t)DEC_GROUPS * a.stages * a.slot_bytes;
     return s;
 }
+static_assert(2 * DEC_GROUPS * DEC_MAX_STAGES * 8 + 64 * 4 + 8 <= DEC_HEADER, "smem header overflow");
 
 size_t decode_smem_bytes(int stages, uint32_t slot, uint32_t xs)
 {
-    return (size_t)stages * slot + xs + DEC_MAX_STAGES * 16 + 64 * 4 + 16;
+    return DEC_HEADER + (size_t)DEC_GROUPS * stages * slot + xs;
 }
 
 // Grid barrier among the consumer threads of every CTA.  Returns false when
@@ -129,7 +148,7 @@ __device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, u
                     ok = false;
                     break;
                 }
-                if (i > 16) __nanosleep(64);
+                if (i > 64) __nanosleep(32);
             }
             __threadfence();
         }
@@ -144,7 +163,8 @@ __device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, u
     return *sm.sync_ok != 0;
 }
 
-// Bounded wait on an mbarrier that also gives up when the CTA is aborting.
+// Bounded wait on an mbarrier (producer: one thread) that also gives up when
+// the CTA is unwinding.
 __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, const Smem &sm, int *err, int code)
 {
     for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
@@ -175,124 +195,133 @@ __device__ __forceinline__ bool ring_wait_warp(uint64_t *bar, uint32_t parity, c
     return false;
 }
 
+// Position of the next chunk in one group's ring (slot and wrap parity).
 struct Ring {
-    int stage;
+    int slot;
     uint32_t phase;
 };
 
+__device__ __forceinline__ void ring_adv(Ring &r, int stages)
+{
+    if (++r.slot == stages) { r.slot = 0; r.phase ^= 1; }
+}
+
+// Tiles of a weight this CTA owns: blockIdx.x, blockIdx.x + grid, ...  They
+// are processed in pairs; group g takes tile 2p+g of pair p, through its own
+// ring.  The producer issues a pair's chunks alternately into the two rings
+// (tile A seg 0, tile B seg 0, tile A seg 1, ...).
+__device__ __forceinline__ int my_tiles(const WDesc &W)
+{
+    return (int)blockIdx.x < W.n_tiles ? (W.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+}
+
 enum DecEpi { DE_QKV, DE_ADD, DE_SWIGLU, DE_CLS };
 
-// One matvec phase for the consumer warps: this CTA's tiles of weight W,
-// chunks taken from the ring in the producer's order.
-template <int WT, int RPW>
+// One matvec phase for the consumer warps; `rg` is this warp's group ring.
+template <int WT>
 __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, const WDesc W, Ring &rg, int epi,
                                            int l, int pos, unsigned long long &best)
 {
-    constexpr int R = MV_CONSUMER_WARPS * RPW;
+    constexpr int R = DEC_GW * DEC_RPW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int t = blockIdx.x; t < W.n_tiles; t += gridDim.x) {
-        float acc[RPW];
-#pragma unroll
-        for (int r = 0; r < RPW; r++) acc[r] = 0.f;
-        for (int s = 0; s < W.nseg; s++) {
-            if (!ring_wait_warp(&sm.full[rg.stage], rg.phase, sm, a.err, CATS_DEVERR_MBAR_FULL)) return false;
-            const int us = min(MV_SEG_UNITS, W.units - MV_SEG_UNITS * s);
-            consume_chunk<WT, RPW>(sm.ring + (size_t)rg.stage * a.slot_bytes, us, s, warp, lane, W.units, sm.xs, acc);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[rg.stage]);
-            if (++rg.stage == a.stages) { rg.stage = 0; rg.phase ^= 1; }
-        }
-#pragma unroll
-        for (int r = 0; r < RPW; r++) acc[r] = warp_sum(acc[r]);
-        if (lane != 0) continue;
-        const int row0 = t * R + warp * RPW;
-        if (row0 >= W.d) continue;
-        if (epi == DE_QKV || epi == DE_SWIGLU) {
-            float v0 = acc[0], v1 = acc[RPW - 1];
-            if (epi == DE_SWIGLU) {
-                a.hb[row0 >> 1] = v0 * (1.f / (1.f + expf(-v0))) * v1;   // silu(w1 x) * (w3 x), :1744-1752
-            } else if (row0 < a.q_dim) {
-                rope_pair(v0, v1, row0, a.head_size, pos);
-                a.q[row0] = v0;
-                a.q[row0 + 1] = v1;
-            } else {
-                const bool is_k = row0 < a.q_dim + a.kv_dim;
-                const int i = row0 - a.q_dim - (is_k ? 0 : a.kv_dim);
-                if (is_k) rope_pair(v0, v1, i, a.head_size, pos);
-                float *c = (is_k ? a.kcache : a.vcache) + ((size_t)l * a.seq_len + pos) * a.kv_dim + i;
-                c[0] = v0;
-                c[1] = v1;
+    const int grp = warp / DEC_GW, gw = warp % DEC_GW;
+    const int nt = my_tiles(W);
+    bool ok = true;
+    for (int p = 0; 2 * p + grp < nt && ok; p++) {
+        const int t = blockIdx.x + (2 * p + grp) * gridDim.x;
+        {
+            float acc[DEC_RPW] = {0.f, 0.f};
+            for (int s = 0; s < W.nseg; s++) {
+                const int k = grp * a.stages + rg.slot;
+                if (!ring_wait_warp(&sm.full[k], rg.phase, sm, a.err, CATS_DEVERR_MBAR_FULL)) { ok = false; break; }
+                const int us = min(MV_SEG_UNITS, W.units - MV_SEG_UNITS * s);
+                consume_chunk<WT, DEC_RPW>(sm.ring + (size_t)k * a.slot_bytes, us, s, gw, lane, W.units, sm.xs, acc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.empty[k]);
+                ring_adv(rg, a.stages);
             }
-        } else {
-#pragma unroll
-            for (int r = 0; r < RPW; r++) {
-                const int row = row0 + r;
-                if (row >= W.d) break;
-                if (epi == DE_ADD) {
-                    a.x[row] = __ldcg(a.x + row) + acc[r];   // residual (:1731-1733, :1759-1761)
-                } else {
-                    a.logits[row] = acc[r];
-                    const unsigned long long k = argmax_key(acc[r], row);
-                    best = k > best ? k : best;
+            if (ok) {
+                acc[0] = warp_sum(acc[0]);
+                acc[1] = warp_sum(acc[1]);
+                const int row0 = t * R + gw * DEC_RPW;
+                if (lane == 0 && row0 < W.d) {
+                    float v0 = acc[0], v1 = acc[1];
+                    if (epi == DE_SWIGLU) {
+                        a.hb[row0 >> 1] = v0 * (1.f / (1.f + expf(-v0))) * v1;   // silu(w1 x) * (w3 x), :1744-1752
+                    } else if (epi == DE_QKV) {
+                        if (row0 < a.q_dim) {
+                            rope_pair(v0, v1, row0, a.head_size, pos);
+                            a.q[row0] = v0;
+                            a.q[row0 + 1] = v1;
+                        } else {
+                            const bool is_k = row0 < a.q_dim + a.kv_dim;
+                            const int i = row0 - a.q_dim - (is_k ? 0 : a.kv_dim);
+                            if (is_k) rope_pair(v0, v1, i, a.head_size, pos);
+                            float *c = (is_k ? a.kcache : a.vcache) + ((size_t)l * a.seq_len + pos) * a.kv_dim + i;
+                            c[0] = v0;
+                            c[1] = v1;
+                        }
+                    } else if (epi == DE_ADD) {   // residual (:1731-1733, :1759-1761)
+                        a.x[row0] = __ldcg(a.x + row0) + v0;
+                        if (row0 + 1 < W.d) a.x[row0 + 1] = __ldcg(a.x + row0 + 1) + v1;
+                    } else {
+                        a.logits[row0] = v0;
+                        unsigned long long k = argmax_key(v0, row0);
+                        if (row0 + 1 < W.d) {
+                            a.logits[row0 + 1] = v1;
+                            const unsigned long long k1 = argmax_key(v1, row0 + 1);
+                            k = k1 > k ? k1 : k;
+                        }
+                        best = k > best ? k : best;
+                    }
                 }
             }
         }
     }
-    return true;
+    return ok;
 }
 
 __device__ __forceinline__ int attn_splits(int T, int max_splits)
 {
-    return max(1, min(max_splits, (T + 7) / 8));
+    return max(1, min(max_splits, (T + 3) / 4));
 }
 
 // Attention items (head h, time chunk s), one per warp: scores q.k/sqrt(hs)
-// four timesteps at a time (their loads in flight together), online softmax,
-// sum p*v; the partial (max, sum, acc) goes to part[h][s].  The last warp to
-// finish a head merges its chunks into xb (:1706-1722).
+// with K and V rows read as one float4 per lane, four timesteps in flight,
+// online softmax, sum p*v; the partial (max, sum, acc) goes to part[h][s].
+// The last warp to finish a head merges its chunks into xb (:1706-1722).
 __device__ __forceinline__ void attention_phase(const DecodeArgs &a, int l, int pos)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hs = a.head_size, P = hs + 4;
+    const bool mine = lane * 4 < hs;                 // lanes holding 4 dims of the head
     const int T = pos + 1;
     const int ns = attn_splits(T, a.max_splits);
     const int chunk = (T + ns - 1) / ns;
     const float rs = sqrtf((float)hs);
     const float *kc = a.kcache + (size_t)l * a.seq_len * a.kv_dim;
     const float *vc = a.vcache + (size_t)l * a.seq_len * a.kv_dim;
-    const int nwarps = gridDim.x * MV_CONSUMER_WARPS;
+    const int nwarps = gridDim.x * DEC_WARPS;
     constexpr int U = 4;
-    for (int item = blockIdx.x * MV_CONSUMER_WARPS + warp; item < a.heads * ns; item += nwarps) {
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int item = blockIdx.x * DEC_WARPS + warp; item < a.heads * ns; item += nwarps) {
         const int h = item / ns, s = item % ns;
         const int t0 = s * chunk, t1 = min(T, t0 + chunk);
-        const int kvo = (h / a.kv_mul) * hs;
-        float qv[8], acc[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int idx = lane + 32 * k;
-            qv[k] = idx < hs ? __ldcg(a.q + h * hs + idx) : 0.f;
-            acc[k] = 0.f;
-        }
+        const int kvo = (h / a.kv_mul) * hs + lane * 4;
+        const float4 qv = mine ? __ldcg(reinterpret_cast<const float4 *>(a.q + h * hs) + lane) : z4;
+        float4 acc = z4;
         float m = -INFINITY, lsum = 0.f;
         for (int tb = t0; tb < t1; tb += U) {
-            float dot[U], vr[U][8];
+            float4 kr[U], vr[U];
 #pragma unroll
             for (int u = 0; u < U; u++) {
                 const int t = min(tb + u, t1 - 1);   // clamped rows are loaded but not used
-                const float *kk = kc + (size_t)t * a.kv_dim + kvo;
-                const float *vv = vc + (size_t)t * a.kv_dim + kvo;
-                dot[u] = 0.f;
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    const int idx = lane + 32 * k;
-                    if (idx < hs) {
-                        dot[u] = fmaf(qv[k], __ldcg(kk + idx), dot[u]);
-                        vr[u][k] = __ldcg(vv + idx);
-                    } else {
-                        vr[u][k] = 0.f;
-                    }
-                }
+                kr[u] = mine ? __ldcg(reinterpret_cast<const float4 *>(kc + (size_t)t * a.kv_dim + kvo)) : z4;
+                vr[u] = mine ? __ldcg(reinterpret_cast<const float4 *>(vc + (size_t)t * a.kv_dim + kvo)) : z4;
             }
+            float dot[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) dot[u] = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
 #pragma unroll
             for (int u = 0; u < U; u++) dot[u] = warp_sum(dot[u]);
 #pragma unroll
@@ -303,19 +332,17 @@ __device__ __forceinline__ void attention_phase(const DecodeArgs &a, int l, int 
                 const float corr = expf(m - mn);
                 const float p = expf(sc - mn);
                 lsum = lsum * corr + p;
-#pragma unroll
-                for (int k = 0; k < 8; k++) acc[k] = acc[k] * corr + p * vr[u][k];
+                acc.x = acc.x * corr + p * vr[u].x;
+                acc.y = acc.y * corr + p * vr[u].y;
+                acc.z = acc.z * corr + p * vr[u].z;
+                acc.w = acc.w * corr + p * vr[u].w;
                 m = mn;
             }
         }
         float *out = a.part + ((size_t)h * a.max_splits + s) * P;
         if (lane == 0) { out[0] = t1 > t0 ? m : -INFINITY; out[1] = lsum; }
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int idx = lane + 32 * k;
-            if (idx < hs) out[4 + idx] = acc[k];
-        }
-        // last arriver of head h merges the chunks
+        if (mine) reinterpret_cast<float4 *>(out + 4)[lane] = acc;
+        // the last arriver of head h merges the chunks
         __syncwarp();
         int prev = 0;
         if (lane == 0) {
@@ -326,80 +353,84 @@ __device__ __forceinline__ void attention_phase(const DecodeArgs &a, int l, int 
         if (prev != ns - 1) continue;
         __threadfence();
         const float *ph = a.part + (size_t)h * a.max_splits * P;
-        float M = -INFINITY;
-        for (int c = 0; c < ns; c++) M = fmaxf(M, __ldcg(ph + (size_t)c * P));
-        float L = 0.f, wts[32];
-        for (int c = 0; c < ns; c++) {
-            const float mc = __ldcg(ph + (size_t)c * P);
-            wts[c & 31] = mc == -INFINITY ? 0.f : expf(mc - M);
-            L += wts[c & 31] * __ldcg(ph + (size_t)c * P + 1);
+        // chunk maxima and sums: lanes take chunks c = lane, lane + 32
+        float mc[2], lc[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int c = lane + 32 * k;
+            mc[k] = c < ns ? __ldcg(ph + (size_t)c * P) : -INFINITY;
+            lc[k] = c < ns ? __ldcg(ph + (size_t)c * P + 1) : 0.f;
         }
+        const float M = warp_max(fmaxf(mc[0], mc[1]));
+        float L = 0.f;
+#pragma unroll
+        for (int k = 0; k < 2; k++) L += mc[k] == -INFINITY ? 0.f : expf(mc[k] - M) * lc[k];
+        L = warp_sum(L);
         const float inv = 1.f / L;
-        for (int idx = lane; idx < hs; idx += 32) {
-            float v = 0.f;
-            for (int c = 0; c < ns; c++) v += wts[c & 31] * __ldcg(ph + (size_t)c * P + 4 + idx);
-            a.xb[h * hs + idx] = v * inv;
+        float4 v = z4;
+        for (int c = 0; c < ns; c++) {
+            const float w = __shfl_sync(0xffffffffu, c < 32 ? mc[0] : mc[1], c & 31);
+            if (w == -INFINITY || !mine) continue;
+            const float e = expf(w - M);
+            const float4 ac = __ldcg(reinterpret_cast<const float4 *>(ph + (size_t)c * P + 4) + lane);
+            v.x += e * ac.x;
+            v.y += e * ac.y;
+            v.z += e * ac.z;
+            v.w += e * ac.w;
         }
+        if (mine)
+            reinterpret_cast<float4 *>(a.xb + h * hs)[lane] = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
         if (lane == 0) a.head_cnt[h] = 0;
     }
 }
 
-template <int WT>
-__global__ void __launch_bounds__(MV_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a)
+// Producer (one thread): stream every chunk of every step's weights, in the
+// order the consumers take them.
+__device__ __forceinline__ void produce(const DecodeArgs &a, const Smem &sm)
 {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const Smem sm = smem_layout(smem, a);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < a.stages; s++) {
-            mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], MV_CONSUMER_WARPS);
-        }
-        *sm.abort_s = 0;
-        fence_barrier_init();
-        fence_proxy_async_smem();
-    }
-    __syncthreads();
-
-    if (warp == MV_CONSUMER_WARPS) {
-        // ------------------------------------------------------ producer
-        if (lane != 0) return;
-        const uint64_t pol = l2_evict_first_policy();
-        int stage = 0;
-        uint32_t phase = 0, issued = 0, parity = 0;
-        bool ok = true;
-        for (int step = 0; step < a.steps && ok; step++) {
-            for (int wi = 0; wi < a.n_wd && ok; wi++) {
-                const WDesc W = a.wd[wi];
-                for (int t = blockIdx.x; t < W.n_tiles && ok; t += gridDim.x) {
-                    const uint8_t *tb = W.w + (size_t)t * W.tile_bytes;
-                    for (int s = 0; s < W.nseg; s++) {
-                        if (!ring_wait(&sm.empty[stage], phase ^ 1, sm, a.err, CATS_DEVERR_MBAR_EMPTY)) {
+    const uint64_t pol = l2_evict_first_policy();
+    Ring r[DEC_GROUPS] = {{0, 0}, {0, 0}};
+    uint32_t issued = 0, parity = 0;   // per slot (both rings): ever used, parity of its last phase
+    bool ok = true;
+    for (int step = 0; step < a.steps && ok; step++) {
+        for (int wi = 0; wi < a.n_wd && ok; wi++) {
+            const WDesc W = a.wd[wi];
+            const int nt = my_tiles(W);
+            for (int p = 0; 2 * p < nt && ok; p++) {
+                const int n_in = min(2, nt - 2 * p);
+                for (int s = 0; s < W.nseg && ok; s++) {
+                    const uint32_t bytes = s == W.nseg - 1 ? W.last_chunk : W.full_chunk;
+                    for (int g = 0; g < n_in; g++) {
+                        const int k = g * a.stages + r[g].slot;
+                        if (!ring_wait(&sm.empty[k], r[g].phase ^ 1, sm, a.err, CATS_DEVERR_MBAR_EMPTY)) {
                             ok = false;
                             break;
                         }
-                        const uint32_t bytes = s == W.nseg - 1 ? W.last_chunk : W.full_chunk;
-                        mbar_arrive_expect_tx(&sm.full[stage], bytes);
-                        bulk_g2s(sm.ring + (size_t)stage * a.slot_bytes, tb + (size_t)s * W.full_chunk, bytes,
-                                 &sm.full[stage], pol);
-                        issued |= 1u << stage;
-                        parity = (parity & ~(1u << stage)) | (phase << stage);
-                        if (++stage == a.stages) { stage = 0; phase ^= 1; }
+                        const int t = blockIdx.x + (2 * p + g) * gridDim.x;
+                        mbar_arrive_expect_tx(&sm.full[k], bytes);
+                        bulk_g2s(sm.ring + (size_t)k * a.slot_bytes,
+                                 W.w + (size_t)t * W.tile_bytes + (size_t)s * W.full_chunk, bytes, &sm.full[k], pol);
+                        issued |= 1u << k;
+                        parity = (parity & ~(1u << k)) | (r[g].phase << k);
+                        ring_adv(r[g], a.stages);
                     }
                 }
             }
         }
-        if (!ok) {
-            // the consumers gave up: let every copy in flight land before the CTA exits
-            for (int s = 0; s < a.stages; s++)
-                if (issued & (1u << s)) mbar_wait_bounded(&sm.full[s], (parity >> s) & 1u, nullptr, 0);
-        }
-        return;
     }
+    // Every issued copy lands before the CTA exits, also when the consumers
+    // stopped early (the last phase of a slot is the only one that can be open).
+    for (int k = 0; k < DEC_GROUPS * a.stages; k++)
+        if (issued & (1u << k)) mbar_wait_bounded(&sm.full[k], (parity >> k) & 1u, nullptr, 0);
+}
 
-    // ---------------------------------------------------------- consumers
-    // Every consumer warp takes the same path through stage_act / grid_sync
-    // (both hold CTA barriers); only grid_sync's broadcast decision ends it.
+// Consumers (16 warps).  Every consumer warp takes the same path through
+// stage_act / grid_sync (both hold CTA barriers); only grid_sync's broadcast
+// decision ends it.
+template <int WT>
+__device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Ring rg{0, 0};
     unsigned target = 0;
     unsigned long long best = 0ull;
@@ -421,13 +452,13 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_decode(const __grid_constant_
             const WDesc *wl = a.wd + 4 * l;
             // qkv: rmsnorm + quantize, [wq;wk;wv], RoPE, k/v into the cache
             if (l == 0)
-                stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(a.emb + (size_t)token * a.dim), false}, a.dim,
-                              a.rms_att, blockIdx.x == 0 ? a.x : nullptr, sm.xs, sm.red, tid, DEC_NC);
+                stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.emb + (size_t)token * a.dim), false},
+                                           a.dim, a.rms_att, blockIdx.x == 0 ? a.x : nullptr, sm.xs, sm.red, tid, DEC_NC);
             else
-                stage_act<WT>(Float4Src{x4, true}, a.dim, a.rms_att + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid,
-                              DEC_NC);
+                stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_att + (size_t)l * a.dim, nullptr, sm.xs,
+                                           sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT, 2>(a, sm, wl[0], rg, DE_QKV, l, pos, best);
+            run_matvec<WT>(a, sm, wl[0], rg, DE_QKV, l, pos, best);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
@@ -436,43 +467,43 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_decode(const __grid_constant_
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
             // wo: quantize the attention output, matvec, residual add
-            stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(a.xb), true}, a.q_dim, nullptr, nullptr, sm.xs,
-                          sm.red, tid, DEC_NC);
+            stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.xb), true}, a.q_dim, nullptr,
+                                       nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT, 1>(a, sm, wl[1], rg, DE_ADD, l, pos, best);
+            run_matvec<WT>(a, sm, wl[1], rg, DE_ADD, l, pos, best);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
             // w1/w3 + SwiGLU
-            stage_act<WT>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid,
-                          DEC_NC);
+            stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs,
+                                       sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT, 2>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best);
+            run_matvec<WT>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
             // w2 + residual add
-            stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(a.hb), true}, a.hidden, nullptr, nullptr, sm.xs,
-                          sm.red, tid, DEC_NC);
+            stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.hb), true}, a.hidden, nullptr,
+                                       nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT, 1>(a, sm, wl[3], rg, DE_ADD, l, pos, best);
+            run_matvec<WT>(a, sm, wl[3], rg, DE_ADD, l, pos, best);
             trace_mark(a, tk);
             alive = grid_sync(a, sm, target);
             trace_mark(a, tk);
         }
         if (!alive) break;
         // classifier + greedy argmax
-        stage_act<WT>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
+        stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
         best = 0ull;
         trace_mark(a, tk);
-        run_matvec<WT, 1>(a, sm, a.wd[4 * a.n_layers], rg, DE_CLS, 0, pos, best);
+        run_matvec<WT>(a, sm, a.wd[4 * a.n_layers], rg, DE_CLS, 0, pos, best);
         trace_mark(a, tk);
         unsigned long long *keys = reinterpret_cast<unsigned long long *>(sm.red + 32);
         if (lane == 0) keys[warp] = best;
         named_bar_sync(1, DEC_NC);
         if (tid == 0) {
             unsigned long long mk = 0;
-            for (int w = 0; w < MV_CONSUMER_WARPS; w++) mk = keys[w] > mk ? keys[w] : mk;
+            for (int w = 0; w < DEC_WARPS; w++) mk = keys[w] > mk ? keys[w] : mk;
             if (mk) atomicMax(a.argmax, mk);
         }
         if (!grid_sync(a, sm, target)) break;
@@ -498,6 +529,39 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_decode(const __grid_constant_
     }
 }
 
+template <int WT>
+__global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const Smem sm = smem_layout(smem, a);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < DEC_GROUPS * a.stages; s++) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], DEC_GW);   // the eight warps of the ring's group
+        }
+        *sm.abort_s = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+    if (warp == DEC_WARPS) {
+        if (lane == 0) produce(a, sm);
+    } else {
+        consume<WT>(a, sm);
+    }
+    // Every thread gets here (none returns early) once all copies have landed
+    // and every arrive is done: retire the mbarriers so the next kernel on
+    // this SM may use these bytes for ordinary data.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < DEC_GROUPS * a.stages; s++) {
+            mbar_inval(&sm.full[s]);
+            mbar_inval(&sm.empty[s]);
+        }
+    }
+}
+
 // ------------------------------------------------------------------- host
 static WDesc to_desc(const DevWeight &W)
 {
@@ -520,26 +584,29 @@ int decode_prepare(LlmModel *m)
 {
     if (m->wdesc) return E_OK;
     const LlmConfig &c = m->c;
+    if (m->head_size > DEC_MAX_HS || m->head_size % 4 || c.dim > 4 * DEC_STAGE_V * DEC_NC) return E_UNSUPPORTED;
     std::vector<WDesc> v;
     uint32_t slot = 0;
     int maxn = std::max(std::max(c.dim, m->hidden_loc), m->q_dim);
-    for (int l = 0; l < c.n_layers; l++) {
-        for (const DevWeight *w : {&m->qkv[l], &m->wo[l], &m->w13[l], &m->w2[l]}) {
-            v.push_back(to_desc(*w));
-            slot = std::max(slot, w->L.full_chunk);
-        }
-    }
-    v.push_back(to_desc(m->cls));
-    slot = std::max(slot, m->cls.L.full_chunk);
+    auto add = [&](const DevWeight &w) -> bool {
+        if (w.L.R != DEC_GW * DEC_RPW) return false;   // the persistent kernel consumes 16-row tiles
+        v.push_back(to_desc(w));
+        slot = std::max(slot, w.L.full_chunk);
+        return true;
+    };
+    for (int l = 0; l < c.n_layers; l++)
+        for (const DevWeight *w : {&m->qkv[l], &m->wo[l], &m->w13[l], &m->w2[l]})
+            if (!add(*w)) return E_UNSUPPORTED;
+    if (!add(m->cls)) return E_UNSUPPORTED;
     slot = (uint32_t)round_up(slot, 128);
     const uint32_t xs = (uint32_t)round_up(c.wtype == W_F32 ? (size_t)maxn * 4 : (size_t)(maxn / 32) * 40, 128);
     const size_t cap = 227 * 1024;
     const size_t fixed = decode_smem_bytes(0, slot, xs);
-    if (fixed + 2 * slot > cap || m->head_size > 256 || m->head_size % 4) return E_UNSUPPORTED;
-    m->dec_stages = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / slot);
+    if (fixed + (size_t)DEC_GROUPS * 2 * slot > cap) return E_UNSUPPORTED;   // at least two slots per ring
+    m->dec_stages = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / ((size_t)DEC_GROUPS * slot));
     m->dec_slot = slot;
     m->dec_xs = xs;
-    m->dec_max_splits = 32;
+    m->dec_max_splits = 64;
     if (cudaMalloc(&m->wdesc, v.size() * sizeof(WDesc)) != cudaSuccess) return E_NOMEM;
     if (cudaMalloc(&m->dec_part, (size_t)m->heads_loc * m->dec_max_splits * (m->head_size + 4) * 4) != cudaSuccess)
         return E_NOMEM;
@@ -552,17 +619,11 @@ int decode_prepare(LlmModel *m)
 template <int WT>
 static cudaError_t launch_decode_t(const DecodeArgs &a, size_t smem, int grid, cudaStream_t st)
 {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_decode<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e) return e;
-        attr = true;
-    } else {
-        cudaFuncSetAttribute(k_decode<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    }
+    cudaError_t e = cudaFuncSetAttribute(k_decode<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(MV_THREADS);
+    cfg.blockDim = dim3(DEC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attrs[1];

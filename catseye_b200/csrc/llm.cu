@@ -12,6 +12,7 @@
 // then the classifier (final rmsnorm + matvec + greedy argmax, :1765-1770)
 // and a one-thread kernel that feeds the argmax back as the next token.
 #include "llm.cuh"
+#include "mv_device.cuh"
 #include <algorithm>
 #include <cstring>
 
@@ -250,6 +251,8 @@ int llm_alloc(LlmModel *m, const LlmConfig &c)
     if (c.dim % c.n_heads || c.n_heads % c.n_kv_heads || c.n_heads % tp || c.n_kv_heads % tp ||
         c.hidden % tp || c.vocab % tp || c.dim % 32 || (c.hidden / tp) % 32 || (c.dim / tp) % 32)
         return E_ARG;
+    // the matvec's rmsnorm prologue holds the whole vector in one staging pass
+    if (c.dim > 4 * STAGE_V * 32 * MV_CONSUMER_WARPS) return E_ARG;
     m->head_size = c.dim / c.n_heads;
     m->heads_loc = c.n_heads / tp;
     m->kv_heads_loc = c.n_kv_heads / tp;
@@ -380,7 +383,7 @@ static int build_layer(LlmModel *m, int l, Src wq, Src wk, Src wv, Src wo, Src w
     // wo: all dim rows, this rank's input columns
     const size_t cw_o = gguf_row_bytes(t, m->q_dim);
     if (copy_slice(stg, cw_o, wo, rb_dim, 0, c.dim, (size_t)r * cw_o, cw_o, st) != cudaSuccess) return E_CUDA;
-    if ((rc = finish_weight(m->wo[l], t, m->q_dim, c.dim, 1, stg, st))) return rc;
+    if ((rc = finish_weight(m->wo[l], t, m->q_dim, c.dim, 2, stg, st))) return rc;
     if (cudaStreamSynchronize(st) != cudaSuccess) return E_CUDA;
     // w13: this rank's hidden rows of w1 and w3, interleaved (row 2i = w1_i, 2i+1 = w3_i)
     if (copy_slice(stg, 2 * rb_dim, w1, rb_dim, (size_t)r * m->hidden_loc, m->hidden_loc, 0, rb_dim, st) != cudaSuccess)
@@ -393,7 +396,7 @@ static int build_layer(LlmModel *m, int l, Src wq, Src wk, Src wv, Src wo, Src w
     // w2: all dim rows, this rank's hidden columns
     const size_t cw_2 = gguf_row_bytes(t, m->hidden_loc);
     if (copy_slice(stg, cw_2, w2, rb_hid, 0, c.dim, (size_t)r * cw_2, cw_2, st) != cudaSuccess) return E_CUDA;
-    if ((rc = finish_weight(m->w2[l], t, m->hidden_loc, c.dim, 1, stg, st))) return rc;
+    if ((rc = finish_weight(m->w2[l], t, m->hidden_loc, c.dim, 2, stg, st))) return rc;
     (void)kvd_full;
     return cudaStreamSynchronize(st) == cudaSuccess ? E_OK : E_CUDA;
 }
@@ -403,7 +406,7 @@ static int build_cls(LlmModel *m, Src wcls, uint8_t *stg)
     const LlmConfig &c = m->c;
     const size_t rb = gguf_row_bytes(c.wtype, c.dim);
     if (copy_slice(stg, rb, wcls, rb, (size_t)m->vocab_off, m->vocab_loc, 0, rb, m->stream) != cudaSuccess) return E_CUDA;
-    int rc = finish_weight(m->cls, c.wtype, c.dim, m->vocab_loc, 1, stg, m->stream);
+    int rc = finish_weight(m->cls, c.wtype, c.dim, m->vocab_loc, 2, stg, m->stream);
     if (rc) return rc;
     return cudaStreamSynchronize(m->stream) == cudaSuccess ? E_OK : E_CUDA;
 }
@@ -582,7 +585,7 @@ cudaError_t llm_enqueue_step(LlmModel *m, bool advance)
         a.x = m->xb;
         if (!tp) { a.epi = EPI_ADD; a.out = m->x; }
         else { a.epi = EPI_STORE; a.out = m->delta; }
-        if ((e = launch_matvec(a, 1, c.wtype, st, true))) return e;
+        if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
         if (tp) { m->allreduce(m->comm_ctx, m->delta, c.dim, st); }
 
         a = base_args(m->w13[l], m->err);
@@ -599,7 +602,7 @@ cudaError_t llm_enqueue_step(LlmModel *m, bool advance)
         a.x = m->hb;
         a.epi = EPI_ADD;
         a.out = m->x;
-        if ((e = launch_matvec(a, 1, c.wtype, st, true))) return e;
+        if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
     }
     MatvecArgs a = base_args(m->cls, m->err);
     a.xmode = xmode;
@@ -608,7 +611,7 @@ cudaError_t llm_enqueue_step(LlmModel *m, bool advance)
     a.epi = EPI_STORE_ARGMAX;
     a.out = m->logits + m->vocab_off;
     a.argmax = m->argmax;
-    if ((e = launch_matvec(a, 1, c.wtype, st, true))) return e;
+    if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
     if (advance && (e = launch_advance(m, st))) return e;
     return cudaSuccess;
 }

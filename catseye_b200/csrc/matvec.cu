@@ -160,80 +160,72 @@ cudaError_t launch_dequantize(int type, float *y, const uint8_t *w, int n, int r
 }
 
 // ------------------------------------------------------------------ matvec
+// Shared memory: a 384-byte header at offset 0 (8 full + 8 empty mbarriers,
+// then the reduction scratch), the ring of stages, the staged activation.
 struct SmemPlan {
-    uint32_t stage_stride, xs_off, xs_bytes, bar_off, red_off, total;
+    uint32_t stage_stride, ring_off, xs_off, xs_bytes, bar_off, red_off, total;
 };
 
 __host__ __device__ inline SmemPlan smem_plan(const MatvecArgs &a, int type)
 {
     SmemPlan p;
+    p.bar_off = 0;
+    p.red_off = 16 * 8;
+    p.ring_off = 384;
     p.stage_stride = (uint32_t)round_up(a.full_chunk, 128);
-    p.xs_off = p.stage_stride * a.stages;
+    p.xs_off = p.ring_off + p.stage_stride * a.stages;
     if (type == W_F32) p.xs_bytes = (uint32_t)round_up((size_t)a.n * 4, 128);
     else p.xs_bytes = (uint32_t)round_up((size_t)a.units * 40, 128);   // lo16 + hi16 + (d, sum)
-    p.bar_off = p.xs_off + p.xs_bytes;
-    p.red_off = p.bar_off + 16 * 8;                                      // up to 8 full + 8 empty
-    p.total = p.red_off + 256;
+    p.total = p.xs_off + p.xs_bytes;
     return p;
 }
 
 size_t matvec_smem_bytes(const MatvecArgs &a, int type) { return smem_plan(a, type).total; }
 
+// Producer (one thread): weights only, so it does not wait for the upstream
+// grid.  Returns after every issued copy has landed and been released.
+__device__ __forceinline__ void mv_produce(const MatvecArgs &a, const SmemPlan &sp, uint8_t *smem, uint64_t *full,
+                                           uint64_t *empty)
+{
+    const int stages = a.stages;
+    uint8_t *ring = smem + sp.ring_off;
+    const uint64_t pol = l2_evict_first_policy();
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+        const uint8_t *tb = a.w + (size_t)t * a.tile_bytes;
+        for (int s = 0; s < a.nseg; s++) {
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1, a.err, CATS_DEVERR_MBAR_EMPTY)) {
+                ok = false;
+                break;
+            }
+            const uint32_t bytes = (s == a.nseg - 1) ? a.last_chunk : a.full_chunk;
+            mbar_arrive_expect_tx(&full[stage], bytes);
+            bulk_g2s(ring + (size_t)stage * sp.stage_stride, tb + (size_t)s * a.full_chunk, bytes, &full[stage], pol);
+            if (++stage == stages) { stage = 0; phase ^= 1; }
+        }
+    }
+    // drain: every issued copy must have landed and been released before the CTA exits
+    for (int k = 0; k < stages; k++) {
+        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, a.err, CATS_DEVERR_MBAR_EMPTY)) {
+            mbar_wait_bounded(&full[stage], phase, nullptr, 0);
+        }
+        if (++stage == stages) { stage = 0; phase ^= 1; }
+    }
+}
+
+// Consumer warps: stage the activation, dot every chunk of this CTA's tiles,
+// run the epilogue.
 template <int WT, int RPW>
-__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant__ MatvecArgs a)
+__device__ __forceinline__ void mv_consume(const MatvecArgs &a, const SmemPlan &sp, uint8_t *smem, uint64_t *full,
+                                           uint64_t *empty, float *red)
 {
     constexpr int R = MV_CONSUMER_WARPS * RPW;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const SmemPlan sp = smem_plan(a, WT);
     const int stages = a.stages;
     uint8_t *xs = smem + sp.xs_off;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + sp.bar_off);
-    uint64_t *empty = full + 8;
-    float *red = reinterpret_cast<float *>(smem + sp.red_off);
+    uint8_t *ring = smem + sp.ring_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < stages; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], MV_CONSUMER_WARPS);
-        }
-        fence_barrier_init();
-        fence_proxy_async_smem();
-    }
-    __syncthreads();
-
-    if (warp == MV_CONSUMER_WARPS) {
-        // ---------------- producer: weights only, so it does not wait for the upstream grid
-        if (lane == 0) {
-            const uint64_t pol = l2_evict_first_policy();
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
-                const uint8_t *tb = a.w + (size_t)t * a.tile_bytes;
-                for (int s = 0; s < a.nseg; s++) {
-                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1, a.err, CATS_DEVERR_MBAR_EMPTY)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t bytes = (s == a.nseg - 1) ? a.last_chunk : a.full_chunk;
-                    mbar_arrive_expect_tx(&full[stage], bytes);
-                    bulk_g2s(smem + (size_t)stage * sp.stage_stride, tb + (size_t)s * a.full_chunk, bytes, &full[stage], pol);
-                    if (++stage == stages) { stage = 0; phase ^= 1; }
-                }
-            }
-            // drain: every issued copy must have landed and been released before the CTA exits
-            for (int k = 0; k < stages; k++) {
-                if (!mbar_wait_bounded(&empty[stage], phase ^ 1, a.err, CATS_DEVERR_MBAR_EMPTY)) {
-                    mbar_wait_bounded(&full[stage], phase, nullptr, 0);
-                }
-                if (++stage == stages) { stage = 0; phase ^= 1; }
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumers
     pdl_wait();
     constexpr int NC = 32 * MV_CONSUMER_WARPS;
     if (a.xmode == XM_Q8_RAW) {
@@ -259,7 +251,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
         for (int s = 0; s < a.nseg; s++) {
             if (!mbar_wait_bounded(&full[stage], phase, a.err, CATS_DEVERR_MBAR_FULL)) { ok = false; break; }
             const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
-            consume_chunk<WT, RPW>(smem + (size_t)stage * sp.stage_stride, us, s, warp, lane, a.units, xs, acc);
+            consume_chunk<WT, RPW>(ring + (size_t)stage * sp.stage_stride, us, s, warp, lane, a.units, xs, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
             if (++stage == stages) { stage = 0; phase ^= 1; }
@@ -315,6 +307,42 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
             unsigned long long m = 0;
             for (int w = 0; w < MV_CONSUMER_WARPS; w++) m = keys[w] > m ? keys[w] : m;
             if (m) atomicMax(a.argmax, m);
+        }
+    }
+}
+
+template <int WT, int RPW>
+__global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant__ MatvecArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const SmemPlan sp = smem_plan(a, WT);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + sp.bar_off);
+    uint64_t *empty = full + 8;
+    float *red = reinterpret_cast<float *>(smem + sp.red_off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], MV_CONSUMER_WARPS);
+        }
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+    if (warp == MV_CONSUMER_WARPS) {
+        if (lane == 0) mv_produce(a, sp, smem, full, empty);
+    } else {
+        mv_consume<WT, RPW>(a, sp, smem, full, empty, red);
+    }
+    // No thread returns early: once all copies have landed and every arrive
+    // is done, retire the mbarriers so the next kernel on this SM may use
+    // these bytes for ordinary data.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; s++) {
+            mbar_inval(&full[s]);
+            mbar_inval(&empty[s]);
         }
     }
 }

@@ -62,7 +62,12 @@ struct Float4Src {
 // writeback (if set) receives the pre-norm vector.  Called by the `nthr`
 // consumer threads (tid 0..nthr-1, a multiple of 32) of the CTA; synchronizes
 // them on named barrier 1 before returning.
-template <int WT, class Src>
+// Each thread issues all of its loads of a pass (V float4 each) before using
+// any, so a pass costs one L2 round trip.  With rmsnorm the vector must fit
+// one pass (n <= 4 * V * nthr; the hosts check it).
+constexpr int STAGE_V = 8;
+
+template <int WT, int V = STAGE_V, class Src>
 __device__ __forceinline__ void stage_act(const Src &src, int n, const float *norm_w, float *writeback,
                                           uint8_t *xs, float *red, int tid, int nthr)
 {
@@ -72,44 +77,53 @@ __device__ __forceinline__ void stage_act(const Src &src, int n, const float *no
     uint8_t *xlo = xs, *xhi = xs + (size_t)units * 16;
     float2 *dxs = reinterpret_cast<float2 *>(xs + (size_t)units * 32);
     const int n4 = n / 4;
-    float scale = 1.f;
-    if (norm_w) {
-        float ss = 0.f;
-        for (int i = tid; i < n4; i += nthr) {
-            const float4 v = src(i);
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        named_bar_sync(1, nthr);
-        float tot = 0.f;
-        for (int w = 0; w < nthr / 32; w++) tot += red[w];
-        tot = __fdiv_rn(tot, (float)n);
-        tot = __fadd_rn(tot, 1e-5f);
-        scale = __fdiv_rn(1.f, __fsqrt_rn(tot));
-    }
     const float4 *nw4 = reinterpret_cast<const float4 *>(norm_w);
     float4 *wb4 = reinterpret_cast<float4 *>(writeback);
-    for (int i = tid; i < n4; i += nthr) {
-        float4 v = src(i);
-        if (wb4) wb4[i] = v;
-        if (norm_w) {
-            const float4 g = nw4[i];
-            v.x = __fmul_rn(g.x, __fmul_rn(scale, v.x));
-            v.y = __fmul_rn(g.y, __fmul_rn(scale, v.y));
-            v.z = __fmul_rn(g.z, __fmul_rn(scale, v.z));
-            v.w = __fmul_rn(g.w, __fmul_rn(scale, v.w));
+    for (int base = 0; base < n4; base += V * nthr) {
+        float4 v[V], g[V];
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            const int i = base + tid + k * nthr;
+            v[k] = i < n4 ? src(i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            g[k] = (norm_w && i < n4) ? nw4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
         }
-        if (WT == W_F32) {
-            reinterpret_cast<float4 *>(xs)[i] = v;
-        } else {
-            float d;
-            int s;
-            const uint32_t packed = q8_group_quant(v, gmask, false, d, s);
-            const int b = i >> 3, g = i & 7;
-            uint8_t *dst = (g < 4 ? xlo : xhi) + (size_t)b * 16 + (g & 3) * 4;
-            *reinterpret_cast<uint32_t *>(dst) = packed;
-            if (g == 0) dxs[b] = make_float2(d, __int_as_float(s));
+        float scale = 1.f;
+        if (norm_w) {
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < V; k++) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            named_bar_sync(1, nthr);
+            float tot = 0.f;
+            for (int w = 0; w < nthr / 32; w++) tot += red[w];
+            tot = __fdiv_rn(tot, (float)n);
+            tot = __fadd_rn(tot, 1e-5f);
+            scale = __fdiv_rn(1.f, __fsqrt_rn(tot));
+        }
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            const int i = base + tid + k * nthr;
+            if (i >= n4) continue;   // whole 8-lane groups leave together (n4 % 8 == 0, nthr % 8 == 0)
+            float4 x = v[k];
+            if (wb4) wb4[i] = x;
+            if (norm_w) {
+                x.x = __fmul_rn(g[k].x, __fmul_rn(scale, x.x));
+                x.y = __fmul_rn(g[k].y, __fmul_rn(scale, x.y));
+                x.z = __fmul_rn(g[k].z, __fmul_rn(scale, x.z));
+                x.w = __fmul_rn(g[k].w, __fmul_rn(scale, x.w));
+            }
+            if (WT == W_F32) {
+                reinterpret_cast<float4 *>(xs)[i] = x;
+            } else {
+                float d;
+                int s;
+                const uint32_t packed = q8_group_quant(x, gmask, false, d, s);
+                const int b = i >> 3, q = i & 7;
+                uint8_t *dst = (q < 4 ? xlo : xhi) + (size_t)b * 16 + (q & 3) * 4;
+                *reinterpret_cast<uint32_t *>(dst) = packed;
+                if (q == 0) dxs[b] = make_float2(d, __int_as_float(s));
+            }
         }
     }
     named_bar_sync(1, nthr);

@@ -1,7 +1,10 @@
 """Benchmark: batch-1 decode of the Llama-2-7B-shape Q4_0 model on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload llama7b_q4_0|llama7b_q8_0|stories_f32]
+                    [--workload llama7b_q4_0|llama7b_q8_0|stories_f32] [--layers L]
+
+--layers L keeps the workload's shapes with L layers (a small case for
+profiling; the workload name then carries the layer count).
 
 One step = one decode token: every layer's rmsnorm + quantize + qkv matvec +
 RoPE, attention over the KV cache, wo, w1/w3 + SwiGLU, w2, then the classifier
@@ -47,10 +50,16 @@ PROMPT = 8
 SEED = 20241201
 
 
-def cfg_for(workload):
+def cfg_for(workload, layers=0):
+    from dataclasses import replace
     from catseye_b200 import llm
     name, t = WORKLOADS[workload]
-    return getattr(llm, name).with_type(t)
+    cfg = getattr(llm, name).with_type(t)
+    return replace(cfg, n_layers=layers) if layers else cfg
+
+
+def workload_name(args):
+    return args.workload + (f"_{args.layers}layers" if args.layers else "")
 
 
 def peaks():
@@ -75,7 +84,7 @@ class Clocks:
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "25"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -162,7 +171,7 @@ def run_ours(args, dist, rank, ws, local):
     from catseye_b200 import _lib, llm
     _lib.init(local)
     torch.cuda.set_device(local)
-    cfg = cfg_for(args.workload)
+    cfg = cfg_for(args.workload, args.layers)
     m = llm.GpuLLM(cfg)
     m.init_random(SEED)
     stream = torch.cuda.ExternalStream(m.stream)
@@ -230,11 +239,12 @@ def run_ours(args, dist, rank, ws, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama7b_q4_0", choices=sorted(WORKLOADS))
+    ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -243,16 +253,14 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
-        cfg = cfg_for(args.workload)
-        for _ in range(args.warmup and 0):
-            pass
+        cfg = cfg_for(args.workload, args.layers)
         cb = cpu_reference(cfg, "reference", samples=max(3, min(args.steps, 5)))
         line = {"impl": "reference", "metric": "decode tok/s (batch 1)", "value": round(cb["value"], 3),
                 "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(1e3 / cb["value"], 3), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)",
                                                8: "q8_0 x q8"}[cfg.wtype],
-                "data": "synthetic", "config": {"workload": args.workload, "batch": 1, "prompt": PROMPT},
+                "data": "synthetic", "config": {"workload": workload_name(args), "batch": 1, "prompt": PROMPT},
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -271,7 +279,7 @@ def main():
     traffic = None
     tf = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tf):
-        traffic = json.load(open(tf)).get(args.workload, {}).get("dram_bytes_per_step")
+        traffic = json.load(open(tf)).get(workload_name(args), {}).get("dram_bytes_per_step")
         traffic = traffic * args.steps if traffic else None
     line = {
         "metric": "decode tok/s (batch 1)", "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws,
@@ -279,9 +287,11 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)", 8: "q8_0 x q8"}[cfg.wtype],
         "data": "synthetic",
-        "config": {"workload": args.workload, "batch": 1, "prompt": PROMPT, "dim": cfg.dim, "layers": cfg.n_layers,
+        "config": {"workload": workload_name(args), "batch": 1, "prompt": PROMPT, "dim": cfg.dim,
+                   "layers": cfg.n_layers, "context": cfg.seq_len,
                    "parallelism": f"replicas{ws}" if ws > 1 else "single",
-                   "l2": "weights 3.7 GB > 126 MB L2; no flush" if cfg.wtype else "weights 37 MB; L2-resident"},
+                   "l2": (f"weights {wbytes / 1e9:.2f} GB per step > 126 MB L2; no flush" if wbytes > 126e6 else
+                          f"weights {wbytes / 1e6:.0f} MB per step; L2-resident, no flush")},
         "roofline": {"bound": "hbm", "kernel": "k_decode (persistent cooperative decode, %d steps per launch)"
                      % args.steps, "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,

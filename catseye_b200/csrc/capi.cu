@@ -475,7 +475,7 @@ int cats_gpu_llm_trace_step(cats_gpu_llm *h, int token, int pos, unsigned long l
     if (int rc = decode_prepare(&h->m)) return fail(rc, what);
     if (int rc = cats_gpu_llm_set_position(h, token, pos)) return rc;
     const int grid = matvec_num_sms();
-    const size_t bytes = (size_t)grid * per_cta * 8;
+    const size_t bytes = (size_t)2 * grid * per_cta * 8;   // globaltimer plane, then clock64 plane
     unsigned long long *d = nullptr;
     if (cudaMalloc(&d, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, what);
     cudaMemsetAsync(d, 0, bytes, h->m.stream);

@@ -3,21 +3,23 @@
 // Restates cats_llama2_transformer (llm/catseye_llm.h:1625-1772) for one
 // B200.  One CTA per SM, launched cooperatively so every CTA is resident.
 //
-//  * A producer warp walks the weights of every layer in step order (qkv, wo,
-//    w1/w3, w2 per layer, then the classifier; this CTA's tiles of each) and
-//    streams their (tile, segment) chunks into shared-memory rings with 1-D
-//    bulk copies (TMA engine, L2 evict-first).  It never waits for an
+//  * Two producer lanes walk the weights of every layer in step order (qkv,
+//    wo, w1/w3, w2 per layer, then the classifier; this CTA's tiles of each)
+//    and stream their (tile, segment) chunks into shared-memory rings with
+//    1-D bulk copies (TMA engine, L2 evict-first).  They never wait for an
 //    activation, so HBM keeps streaming through every phase boundary.
 //  * Two consumer warp-groups of eight warps run the phases.  The CTA's tiles
 //    of a weight are taken in pairs, one per group; each group has a ring of
-//    its own (slots plus full/empty mbarriers) and the producer alternates
-//    between the two rings, so both groups dot in parallel and every ring
-//    has one consumer that waits on each of its chunks in order (a group
-//    never polls a slot whose previous chunk belongs to someone else, which
-//    could show it a phase that has not started yet).  Between phases all
-//    CTAs meet at a grid barrier (bounded spin on a global counter); after it
-//    each CTA stages the phase's activation (rmsnorm + quantize_q8) in shared
-//    memory, with every load of a thread issued before any is used.
+//    its own (slots plus full/empty mbarriers) fed by its own producer lane,
+//    so both groups dot in parallel and every ring has one consumer that
+//    waits on each of its chunks in order (a group never polls a slot whose
+//    previous chunk belongs to someone else, which could show it a phase that
+//    has not started yet).  Between phases all CTAs meet at a grid barrier
+//    (release add, acquire polls, bounded); after it each CTA stages the
+//    phase's activation (rmsnorm + quantize_q8) in shared memory, with every
+//    load of a thread issued before any is used.  The weight descriptors are
+//    copied into shared memory at the start: a global load queued behind the
+//    SM's weight copies takes microseconds.
 //  * Attention (:1677-1723) is split over time into short (head, chunk)
 //    items, one per warp, four timesteps' K and V rows in flight at a time,
 //    online softmax; the last warp to finish a head merges its chunks.
@@ -26,12 +28,13 @@
 //    with no host round trip.
 //
 // Shared memory: a fixed 1 KB header (the mbarriers at offset 0, reduction
-// scratch, flags), then the two rings (group g's slot k at index
-// g * stages + k), then the staged activation.  The mbarriers are
-// invalidated before the kernel exits.
+// scratch, flags), the weight descriptors, then the two rings (group g's
+// slot k at index g * stages + k), then the staged activation.  The
+// mbarriers are invalidated before the kernel exits.
 #include "llm.cuh"
 #include "mv_device.cuh"
 #include <algorithm>
+#include <cstdlib>
 
 namespace cats {
 
@@ -44,14 +47,17 @@ constexpr int DEC_MAX_STAGES = 16;                            // per ring (two r
 constexpr int DEC_RPW = 2;                                    // rows per warp in a 16-row tile
 constexpr int DEC_MAX_HS = 128;                               // head size held as one float4 per lane
 constexpr int DEC_STAGE_V = 4;                                // staging loads in flight per thread (512 threads)
+constexpr int DEC_STAGE_V_WIDE = 6;                           // the same without rmsnorm: the hidden vector in one pass
 constexpr uint32_t DEC_HEADER = 1024;                         // mbarriers + scratch at the start of smem
-constexpr uint32_t GRID_SPIN_LIMIT = 1u << 23;                // ~1 s of polling with backoff
+constexpr uint32_t GRID_SPIN_LIMIT = 1u << 22;                // polls of ~0.5-1 us each: a few seconds at most
 
+// One weight in the tile-chunk layout (16-row tiles, 64-unit segments).
 struct WDesc {
     const uint8_t *w;
-    int n, d, R, rpw, units, nseg, n_tiles;
-    uint32_t full_chunk, last_chunk;
     unsigned long long tile_bytes;
+    int d, units, nseg, n_tiles;
+    uint32_t full_chunk, last_chunk;
+    int pad[2];
 };
 
 struct DecodeArgs {
@@ -83,11 +89,20 @@ __device__ __forceinline__ unsigned long long global_ns()
     return t;
 }
 
-// Thread 0 of each CTA records a timestamp (tracing only).
+// Thread 0 of each CTA records a timestamp (tracing only): globaltimer ns in
+// trace[cta][k], the SM's clock64 in trace[grid + cta][k].
+__device__ __forceinline__ void trace_put(const DecodeArgs &a, int &k, unsigned long long ns, long long clk)
+{
+    if (a.trace && threadIdx.x == 0 && k < a.trace_stride) {
+        a.trace[(size_t)blockIdx.x * a.trace_stride + k] = ns;
+        a.trace[(size_t)(gridDim.x + blockIdx.x) * a.trace_stride + k] = (unsigned long long)clk;
+    }
+    k++;
+}
+
 __device__ __forceinline__ void trace_mark(const DecodeArgs &a, int &k)
 {
-    if (a.trace && threadIdx.x == 0 && k < a.trace_stride) a.trace[(size_t)blockIdx.x * a.trace_stride + k] = global_ns();
-    k++;
+    trace_put(a, k, a.trace ? global_ns() : 0ull, a.trace ? clock64() : 0ll);
 }
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
@@ -95,6 +110,11 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ int ld_volatile_i32(const int *p)
@@ -108,7 +128,13 @@ struct Smem {
     float *red;
     volatile int *abort_s;   // hint for bounded waits: stop waiting, the kernel is unwinding
     volatile int *sync_ok;   // grid_sync's decision, written by thread 0 between its two CTA barriers
+    WDesc *wd;               // the weight descriptors, copied in at the start (global reads cost microseconds)
 };
+
+__host__ __device__ inline size_t desc_bytes(int n_wd)
+{
+    return round_up((size_t)n_wd * sizeof(WDesc), 128);
+}
 
 __device__ __forceinline__ Smem smem_layout(uint8_t *base, const DecodeArgs &a)
 {
@@ -118,15 +144,17 @@ __device__ __forceinline__ Smem smem_layout(uint8_t *base, const DecodeArgs &a)
     s.red = reinterpret_cast<float *>(s.empty + DEC_GROUPS * DEC_MAX_STAGES);   // 64 floats (16 u64 keys at +32)
     s.abort_s = reinterpret_cast<volatile int *>(s.red + 64);
     s.sync_ok = s.abort_s + 1;
-    s.ring = base + DEC_HEADER;
+    s.wd = reinterpret_cast<WDesc *>(base + DEC_HEADER);
+    s.ring = base + DEC_HEADER + desc_bytes(a.n_wd);
     s.xs = s.ring + (size_t)DEC_GROUPS * a.stages * a.slot_bytes;
     return s;
 }
 static_assert(2 * DEC_GROUPS * DEC_MAX_STAGES * 8 + 64 * 4 + 8 <= DEC_HEADER, "smem header overflow");
+static_assert(sizeof(WDesc) % 16 == 0, "descriptors are copied as 16-byte words");
 
-size_t decode_smem_bytes(int stages, uint32_t slot, uint32_t xs)
+size_t decode_smem_bytes(int n_wd, int stages, uint32_t slot, uint32_t xs)
 {
-    return DEC_HEADER + (size_t)DEC_GROUPS * stages * slot + xs;
+    return DEC_HEADER + desc_bytes(n_wd) + (size_t)DEC_GROUPS * stages * slot + xs;
 }
 
 // Grid barrier among the consumer threads of every CTA.  Returns false when
@@ -140,17 +168,16 @@ __device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, u
         bool ok = *sm.abort_s == 0;
         if (ok) {
             target += gridDim.x;
-            __threadfence();
-            atomicAdd(a.bar, 1u);
+            // the release covers the CTA's writes ordered before it by the CTA
+            // barrier; the acquire polls make the other CTAs' writes visible
+            red_release_add(a.bar, 1u);
             uint32_t i = 0;
             while (ld_acquire_u32(a.bar) < target) {
-                if (++i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag)) {
+                if ((++i & 63) == 0 && (i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag))) {
                     ok = false;
                     break;
                 }
-                if (i > 64) __nanosleep(32);
             }
-            __threadfence();
         }
         if (!ok) {
             if (a.err) atomicOr(a.err, CATS_DEVERR_PEER_WAIT);
@@ -217,29 +244,62 @@ __device__ __forceinline__ int my_tiles(const WDesc &W)
 
 enum DecEpi { DE_QKV, DE_ADD, DE_SWIGLU, DE_CLS };
 
+// Residual rows (row0, row0 + 1) of tile t for this warp, read by lane 0.  A
+// load queued behind the SM's weight copies takes microseconds, so these are
+// issued well before the epilogue needs them: for a warp's first tile before
+// the phase's activation staging, for later tiles before their dots.
+__device__ __forceinline__ void residual_rows(const DecodeArgs &a, const WDesc &W, int t, float (&xr)[2])
+{
+    const int lane = threadIdx.x & 31, gw = (threadIdx.x >> 5) % DEC_GW;
+    const int row0 = t * DEC_GW * DEC_RPW + gw * DEC_RPW;
+    xr[0] = xr[1] = 0.f;
+    if (lane == 0 && row0 < W.d) {
+        xr[0] = __ldcg(a.x + row0);
+        if (row0 + 1 < W.d) xr[1] = __ldcg(a.x + row0 + 1);
+    }
+}
+
+// The first tile's residual rows of this warp (see residual_rows).
+__device__ __forceinline__ void residual_first(const DecodeArgs &a, const WDesc &W, float (&xr)[2])
+{
+    const int grp = (threadIdx.x >> 5) / DEC_GW;
+    xr[0] = xr[1] = 0.f;
+    if (grp < my_tiles(W)) residual_rows(a, W, blockIdx.x + grp * gridDim.x, xr);
+}
+
 // One matvec phase for the consumer warps; `rg` is this warp's group ring.
+// xr_first: the residual rows of the warp's first tile (DE_ADD only).
 template <int WT>
 __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, const WDesc W, Ring &rg, int epi,
-                                           int l, int pos, unsigned long long &best)
+                                           int l, int pos, unsigned long long &best, int &tk,
+                                           const float (&xr_first)[2])
 {
     constexpr int R = DEC_GW * DEC_RPW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = warp / DEC_GW, gw = warp % DEC_GW;
     const int nt = my_tiles(W);
     bool ok = true;
+    // tracing: when thread 0 first had a chunk, and when it finished its last dot
+    unsigned long long ns_first = 0, ns_dots = 0;
+    long long ck_first = 0, ck_dots = 0;
     for (int p = 0; 2 * p + grp < nt && ok; p++) {
         const int t = blockIdx.x + (2 * p + grp) * gridDim.x;
         {
+            // residual rows of a later tile: loaded now, used after the dots
+            float xr[2] = {xr_first[0], xr_first[1]};
+            if (p > 0 && epi == DE_ADD) residual_rows(a, W, t, xr);
             float acc[DEC_RPW] = {0.f, 0.f};
             for (int s = 0; s < W.nseg; s++) {
                 const int k = grp * a.stages + rg.slot;
                 if (!ring_wait_warp(&sm.full[k], rg.phase, sm, a.err, CATS_DEVERR_MBAR_FULL)) { ok = false; break; }
+                if (a.trace && p == 0 && s == 0) { ns_first = global_ns(); ck_first = clock64(); }
                 const int us = min(MV_SEG_UNITS, W.units - MV_SEG_UNITS * s);
                 consume_chunk<WT, DEC_RPW>(sm.ring + (size_t)k * a.slot_bytes, us, s, gw, lane, W.units, sm.xs, acc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.empty[k]);
                 ring_adv(rg, a.stages);
             }
+            if (a.trace) { ns_dots = global_ns(); ck_dots = clock64(); }
             if (ok) {
                 acc[0] = warp_sum(acc[0]);
                 acc[1] = warp_sum(acc[1]);
@@ -262,8 +322,8 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
                             c[1] = v1;
                         }
                     } else if (epi == DE_ADD) {   // residual (:1731-1733, :1759-1761)
-                        a.x[row0] = __ldcg(a.x + row0) + v0;
-                        if (row0 + 1 < W.d) a.x[row0 + 1] = __ldcg(a.x + row0 + 1) + v1;
+                        a.x[row0] = xr[0] + v0;
+                        if (row0 + 1 < W.d) a.x[row0 + 1] = xr[1] + v1;
                     } else {
                         a.logits[row0] = v0;
                         unsigned long long k = argmax_key(v0, row0);
@@ -278,6 +338,8 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
             }
         }
     }
+    trace_put(a, tk, ns_first, ck_first);
+    trace_put(a, tk, ns_dots, ck_dots);
     return ok;
 }
 
@@ -384,44 +446,44 @@ __device__ __forceinline__ void attention_phase(const DecodeArgs &a, int l, int 
     }
 }
 
-// Producer (one thread): stream every chunk of every step's weights, in the
-// order the consumers take them.
-__device__ __forceinline__ void produce(const DecodeArgs &a, const Smem &sm)
+// Producer of group g's ring (lane g of the producer warp): streams the
+// chunks of the group's tiles (tile 2p + g of every pair p of every weight,
+// step after step) into the group's ring, in the order the group takes them.
+// The two producers run independently, so a group that is behind never holds
+// back the other's copies.
+__device__ __forceinline__ void produce(const DecodeArgs &a, const Smem &sm, int g)
 {
     const uint64_t pol = l2_evict_first_policy();
-    Ring r[DEC_GROUPS] = {{0, 0}, {0, 0}};
-    uint32_t issued = 0, parity = 0;   // per slot (both rings): ever used, parity of its last phase
+    Ring r{0, 0};
+    uint32_t issued = 0, parity = 0;   // per slot of this ring: ever used, parity of its last phase
     bool ok = true;
     for (int step = 0; step < a.steps && ok; step++) {
         for (int wi = 0; wi < a.n_wd && ok; wi++) {
-            const WDesc W = a.wd[wi];
+            const WDesc W = sm.wd[wi];
             const int nt = my_tiles(W);
-            for (int p = 0; 2 * p < nt && ok; p++) {
-                const int n_in = min(2, nt - 2 * p);
-                for (int s = 0; s < W.nseg && ok; s++) {
+            for (int p = 0; 2 * p + g < nt && ok; p++) {
+                const int t = blockIdx.x + (2 * p + g) * gridDim.x;
+                for (int s = 0; s < W.nseg; s++) {
                     const uint32_t bytes = s == W.nseg - 1 ? W.last_chunk : W.full_chunk;
-                    for (int g = 0; g < n_in; g++) {
-                        const int k = g * a.stages + r[g].slot;
-                        if (!ring_wait(&sm.empty[k], r[g].phase ^ 1, sm, a.err, CATS_DEVERR_MBAR_EMPTY)) {
-                            ok = false;
-                            break;
-                        }
-                        const int t = blockIdx.x + (2 * p + g) * gridDim.x;
-                        mbar_arrive_expect_tx(&sm.full[k], bytes);
-                        bulk_g2s(sm.ring + (size_t)k * a.slot_bytes,
-                                 W.w + (size_t)t * W.tile_bytes + (size_t)s * W.full_chunk, bytes, &sm.full[k], pol);
-                        issued |= 1u << k;
-                        parity = (parity & ~(1u << k)) | (r[g].phase << k);
-                        ring_adv(r[g], a.stages);
+                    const int k = g * a.stages + r.slot;
+                    if (!ring_wait(&sm.empty[k], r.phase ^ 1, sm, a.err, CATS_DEVERR_MBAR_EMPTY)) {
+                        ok = false;
+                        break;
                     }
+                    mbar_arrive_expect_tx(&sm.full[k], bytes);
+                    bulk_g2s(sm.ring + (size_t)k * a.slot_bytes,
+                             W.w + (size_t)t * W.tile_bytes + (size_t)s * W.full_chunk, bytes, &sm.full[k], pol);
+                    issued |= 1u << r.slot;
+                    parity = (parity & ~(1u << r.slot)) | (r.phase << r.slot);
+                    ring_adv(r, a.stages);
                 }
             }
         }
     }
     // Every issued copy lands before the CTA exits, also when the consumers
     // stopped early (the last phase of a slot is the only one that can be open).
-    for (int k = 0; k < DEC_GROUPS * a.stages; k++)
-        if (issued & (1u << k)) mbar_wait_bounded(&sm.full[k], (parity >> k) & 1u, nullptr, 0);
+    for (int s = 0; s < a.stages; s++)
+        if (issued & (1u << s)) mbar_wait_bounded(&sm.full[g * a.stages + s], (parity >> s) & 1u, nullptr, 0);
 }
 
 // Consumers (16 warps).  Every consumer warp takes the same path through
@@ -436,6 +498,7 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
     unsigned long long best = 0ull;
     const int tid = threadIdx.x;
     const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
+    const float no_rows[2] = {0.f, 0.f};
     int tk = 0;
     trace_mark(a, tk);
     for (int step = 0; step < a.steps; step++) {
@@ -449,7 +512,7 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
         }
         bool alive = true;
         for (int l = 0; l < a.n_layers && alive; l++) {
-            const WDesc *wl = a.wd + 4 * l;
+            const WDesc *wl = sm.wd + 4 * l;
             // qkv: rmsnorm + quantize, [wq;wk;wv], RoPE, k/v into the cache
             if (l == 0)
                 stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.emb + (size_t)token * a.dim), false},
@@ -458,35 +521,38 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
                 stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_att + (size_t)l * a.dim, nullptr, sm.xs,
                                            sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT>(a, sm, wl[0], rg, DE_QKV, l, pos, best);
+            run_matvec<WT>(a, sm, wl[0], rg, DE_QKV, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
+            float xr[2];
+            residual_first(a, wl[1], xr);   // x is final until the wo epilogue
             attention_phase(a, l, pos);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
             // wo: quantize the attention output, matvec, residual add
-            stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.xb), true}, a.q_dim, nullptr,
-                                       nullptr, sm.xs, sm.red, tid, DEC_NC);
+            stage_act<WT, DEC_STAGE_V, false>(Float4Src{reinterpret_cast<const float4 *>(a.xb), true}, a.q_dim,
+                                              nullptr, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT>(a, sm, wl[1], rg, DE_ADD, l, pos, best);
+            run_matvec<WT>(a, sm, wl[1], rg, DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
+            residual_first(a, wl[3], xr);   // x is final until the w2 epilogue
             // w1/w3 + SwiGLU
             stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs,
                                        sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best);
+            run_matvec<WT>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
-            // w2 + residual add
-            stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.hb), true}, a.hidden, nullptr,
-                                       nullptr, sm.xs, sm.red, tid, DEC_NC);
+            // w2 + residual add (the hidden vector in one pass: 4 * 6 * 512 >= 11008)
+            stage_act<WT, DEC_STAGE_V_WIDE, false>(Float4Src{reinterpret_cast<const float4 *>(a.hb), true}, a.hidden,
+                                                   nullptr, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT>(a, sm, wl[3], rg, DE_ADD, l, pos, best);
+            run_matvec<WT>(a, sm, wl[3], rg, DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
             alive = grid_sync(a, sm, target);
             trace_mark(a, tk);
@@ -496,7 +562,7 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
         stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
         best = 0ull;
         trace_mark(a, tk);
-        run_matvec<WT>(a, sm, a.wd[4 * a.n_layers], rg, DE_CLS, 0, pos, best);
+        run_matvec<WT>(a, sm, sm.wd[4 * a.n_layers], rg, DE_CLS, 0, pos, best, tk, no_rows);
         trace_mark(a, tk);
         unsigned long long *keys = reinterpret_cast<unsigned long long *>(sm.red + 32);
         if (lane == 0) keys[warp] = best;
@@ -535,6 +601,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
     extern __shared__ __align__(128) uint8_t smem[];
     const Smem sm = smem_layout(smem, a);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const int4 *src = reinterpret_cast<const int4 *>(a.wd);
+        int4 *dst = reinterpret_cast<int4 *>(sm.wd);
+        const int n16 = a.n_wd * (int)(sizeof(WDesc) / 16);
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < DEC_GROUPS * a.stages; s++) {
             mbar_init(&sm.full[s], 1);
@@ -546,7 +618,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
     }
     __syncthreads();
     if (warp == DEC_WARPS) {
-        if (lane == 0) produce(a, sm);
+        if (lane < DEC_GROUPS) produce(a, sm, lane);
     } else {
         consume<WT>(a, sm);
     }
@@ -565,12 +637,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
 // ------------------------------------------------------------------- host
 static WDesc to_desc(const DevWeight &W)
 {
-    WDesc d;
+    WDesc d{};
     d.w = W.ptr;
-    d.n = W.L.n;
     d.d = W.L.d;
-    d.R = W.L.R;
-    d.rpw = W.L.rpw;
     d.units = W.L.units;
     d.nseg = W.L.nseg;
     d.n_tiles = W.L.n_tiles;
@@ -601,18 +670,33 @@ int decode_prepare(LlmModel *m)
     slot = (uint32_t)round_up(slot, 128);
     const uint32_t xs = (uint32_t)round_up(c.wtype == W_F32 ? (size_t)maxn * 4 : (size_t)(maxn / 32) * 40, 128);
     const size_t cap = 227 * 1024;
-    const size_t fixed = decode_smem_bytes(0, slot, xs);
+    const size_t fixed = decode_smem_bytes((int)v.size(), 0, slot, xs);
     if (fixed + (size_t)DEC_GROUPS * 2 * slot > cap) return E_UNSUPPORTED;   // at least two slots per ring
     m->dec_stages = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / ((size_t)DEC_GROUPS * slot));
+    // tuning: CATS_DECODE_RING_STAGES caps the slots per ring (weight bytes in flight per SM)
+    if (const char *e = getenv("CATS_DECODE_RING_STAGES")) {
+        const int s = atoi(e);
+        if (s >= 2 && s < m->dec_stages) m->dec_stages = s;
+    }
     m->dec_slot = slot;
     m->dec_xs = xs;
     m->dec_max_splits = 64;
-    if (cudaMalloc(&m->wdesc, v.size() * sizeof(WDesc)) != cudaSuccess) return E_NOMEM;
-    if (cudaMalloc(&m->dec_part, (size_t)m->heads_loc * m->dec_max_splits * (m->head_size + 4) * 4) != cudaSuccess)
+    // all or nothing: wdesc is set last, so a failed setup is retried in full
+    void *wd = nullptr;
+    const size_t part_bytes = (size_t)m->heads_loc * m->dec_max_splits * (m->head_size + 4) * 4;
+    bool ok = cudaMalloc(&wd, v.size() * sizeof(WDesc)) == cudaSuccess;
+    ok = ok && (m->dec_part || cudaMalloc(&m->dec_part, part_bytes) == cudaSuccess);
+    ok = ok && (m->dec_bar || cudaMalloc(&m->dec_bar, 16) == cudaSuccess);
+    if (!ok) {
+        if (wd) cudaFree(wd);
         return E_NOMEM;
-    if (cudaMalloc(&m->dec_bar, 16) != cudaSuccess) return E_NOMEM;
+    }
+    if (cudaMemcpy(wd, v.data(), v.size() * sizeof(WDesc), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(wd);
+        return E_CUDA;
+    }
     m->n_wdesc = (int)v.size();
-    if (cudaMemcpy(m->wdesc, v.data(), v.size() * sizeof(WDesc), cudaMemcpyHostToDevice) != cudaSuccess) return E_CUDA;
+    m->wdesc = wd;
     return E_OK;
 }
 
@@ -681,7 +765,7 @@ cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, uns
     a.err = m->err;
     a.trace = trace;
     a.trace_stride = trace_stride;
-    const size_t smem = decode_smem_bytes(a.stages, a.slot_bytes, a.xs_bytes);
+    const size_t smem = decode_smem_bytes(a.n_wd, a.stages, a.slot_bytes, a.xs_bytes);
     cudaError_t e = cudaMemsetAsync(m->dec_bar, 0, 16, m->stream);
     if (e) return e;
     const int grid = matvec_num_sms();

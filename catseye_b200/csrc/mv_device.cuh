@@ -67,10 +67,12 @@ struct Float4Src {
 // one pass (n <= 4 * V * nthr; the hosts check it).
 constexpr int STAGE_V = 8;
 
-template <int WT, int V = STAGE_V, class Src>
+// NORM = false compiles the form without rmsnorm (norm_w must be null).
+template <int WT, int V = STAGE_V, bool NORM = true, class Src>
 __device__ __forceinline__ void stage_act(const Src &src, int n, const float *norm_w, float *writeback,
                                           uint8_t *xs, float *red, int tid, int nthr)
 {
+    if (!NORM) norm_w = nullptr;
     const int lane = tid & 31, warp = tid >> 5;
     const unsigned gmask = 0xffu << (lane & 24);
     const int units = WT == W_F32 ? n / 4 : n / 32;

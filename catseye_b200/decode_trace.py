@@ -4,36 +4,50 @@
 
 Runs a Llama-2-7B-shaped model (random weights, the given weight type and
 layer count), feeds a few prompt tokens, then traces single steps: thread 0
-of every CTA stamps %globaltimer at each phase boundary of the kernel
-(activation staging, each matvec, each grid barrier, attention).  Printed
-per phase kind, summed over layers: the mean time a CTA spends in it, and
-the critical path (latest CTA to finish the phase minus earliest to start).
+of every CTA stamps %globaltimer and its SM's clock64 at each phase boundary
+of the kernel.  A matvec is split into: waiting for its first weight chunk
+(`_wait`), the dots (`_dots`, first chunk ready to last dot done) and the
+epilogue (`_epi`).  Printed per phase kind, summed over layers: the mean time
+a CTA spends in it (from globaltimer, and from clock64 at the step's mean
+clock rate), and the critical path (latest CTA to finish the phase minus the
+earliest to start it, globaltimer).
 """
 import argparse
 from dataclasses import replace
 
 import numpy as np
 
-PHASES = ["stage_qkv", "mv_qkv", "sync_qkv", "attention", "sync_attn", "stage_wo", "mv_wo", "sync_wo",
-          "stage_w13", "mv_w13", "sync_w13", "stage_w2", "mv_w2", "sync_w2"]
+
+def _mv(name):
+    return [f"{name}_wait", f"{name}_dots", f"{name}_epi"]
 
 
-def phase_table(tr, n_layers):
-    """Per-phase (mean per CTA, critical path) in microseconds, summed over layers."""
-    tr = tr.astype(np.int64)
-    t = (tr - tr[:, 0].min()) / 1e3
+PHASES = (["stage_qkv"] + _mv("mv_qkv") + ["sync_qkv", "attention", "sync_attn", "stage_wo"] + _mv("mv_wo") +
+          ["sync_wo", "stage_w13"] + _mv("mv_w13") + ["sync_w13", "stage_w2"] + _mv("mv_w2") + ["sync_w2"])
+TAIL = ["stage_cls"] + _mv("mv_cls") + ["argmax_and_syncs"]
+
+
+def phase_table(ns, clk, n_layers):
+    """{phase: (mean us per CTA from ns, mean us per CTA from clock64, critical us)} summed over layers."""
+    ns = ns.astype(np.int64)
+    clk = clk.astype(np.int64)
+    t = (ns - ns[:, 0].min()) / 1e3
+    end = 1 + len(PHASES) * n_layers + len(TAIL) - 1
+    mhz = float(np.mean((clk[:, end] - clk[:, 0]) / np.maximum(ns[:, end] - ns[:, 0], 1) * 1e3))
+    c = clk / mhz
     out = {}
+
+    def add(name, i):
+        m, mc, cr = out.get(name, (0.0, 0.0, 0.0))
+        out[name] = (m + float((t[:, i] - t[:, i - 1]).mean()), mc + float((c[:, i] - c[:, i - 1]).mean()),
+                     cr + float(t[:, i].max() - t[:, i - 1].min()))
+
     for l in range(n_layers):
-        b = 1 + len(PHASES) * l
         for k, name in enumerate(PHASES):
-            prev, cur = t[:, b + k - 1], t[:, b + k]
-            m, c = out.get(name, (0.0, 0.0))
-            out[name] = (m + float((cur - prev).mean()), c + float(cur.max() - prev.min()))
-    b = 1 + len(PHASES) * n_layers
-    for k, name in enumerate(["stage_cls", "mv_cls", "argmax_and_syncs"]):
-        prev, cur = t[:, b + k - 1], t[:, b + k]
-        out[name] = (float((cur - prev).mean()), float(cur.max() - prev.min()))
-    return out, float(t[:, b + 2].max())
+            add(name, 1 + len(PHASES) * l + k)
+    for k, name in enumerate(TAIL):
+        add(name, 1 + len(PHASES) * n_layers + k)
+    return out, float(t[:, end].max()), mhz
 
 
 def main():
@@ -50,14 +64,15 @@ def main():
     m.init_random(7)
     for pos in range(args.pos):
         m.step(pos + 1, pos)
+    per_cta = 1 + len(PHASES) * args.layers + len(TAIL) + 8
     for rep in range(args.reps):
-        tr = m.trace_step(5, args.pos + rep)
-        tab, total = phase_table(tr, args.layers)
-        print(f"step at pos {args.pos + rep}: {total:.1f} us")
-        for name, (mean, crit) in tab.items():
+        ns, clk = m.trace_step(5, args.pos + rep, per_cta)
+        tab, total, mhz = phase_table(ns, clk, args.layers)
+        print(f"step at pos {args.pos + rep}: {total:.1f} us, SM clock {mhz:.0f} MHz")
+        for name, (mean, mean_c, crit) in tab.items():
             per = args.layers if name in PHASES else 1
-            print(f"  {name:18s} mean/CTA {mean:8.1f} us ({mean / per:6.2f} per layer)  "
-                  f"critical {crit:8.1f} us ({crit / per:6.2f} per layer)")
+            print(f"  {name:18s} mean/CTA {mean / per:6.2f} us (clock64 {mean_c / per:6.2f})  "
+                  f"critical {crit / per:6.2f} us   [per layer; total {mean:7.1f} us]")
     m.close()
 
 

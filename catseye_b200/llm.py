@@ -128,12 +128,14 @@ class GpuLLM:
         return ms.value, by.value
 
     def trace_step(self, token, pos, per_cta=1024):
-        """One traced step of the persistent engine: [ctas][per_cta] ns stamps."""
-        buf = np.zeros(148 * per_cta, dtype=np.uint64)
+        """One traced step of the persistent engine: ([ctas][per_cta] globaltimer
+        ns, [ctas][per_cta] SM clock64) stamps."""
+        buf = np.zeros(2 * 148 * per_cta, dtype=np.uint64)
         ctas = C.c_int()
         _lib.check(self.lib.cats_gpu_llm_trace_step(self.h, token, pos, C.c_void_p(buf.ctypes.data), per_cta,
                                                     C.byref(ctas)), "trace_step")
-        return buf[:ctas.value * per_cta].reshape(ctas.value, per_cta)
+        n = ctas.value * per_cta
+        return buf[:n].reshape(ctas.value, per_cta), buf[n:2 * n].reshape(ctas.value, per_cta)
 
     def close(self):
         if self.h:

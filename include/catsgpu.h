@@ -140,9 +140,11 @@ int cats_gpu_llm_generate(cats_gpu_llm *m, int token, int pos, int steps, int *t
 int cats_gpu_llm_set_engine(cats_gpu_llm *m, int engine);
 /* One step of the persistent engine with a phase timeline, the counterpart
  * of the reference's per-layer CATS_CHECK timings (catseye.h:2110-2117):
- * host receives [ctas][per_cta] globaltimer stamps (ns) taken by each CTA
- * after staging an activation, after its matvec or attention work, and after
- * each grid barrier; *ctas receives the grid size (host must hold 148*per_cta). */
+ * host receives [2][ctas][per_cta] stamps taken by thread 0 of each CTA:
+ * globaltimer ns, then the SM's clock64, at the start of the step, after
+ * staging an activation, when its first weight chunk of a matvec was ready,
+ * after its last dot, after its epilogue, after attention and after each grid
+ * barrier; *ctas receives the grid size (host must hold 2*148*per_cta). */
 int cats_gpu_llm_trace_step(cats_gpu_llm *m, int token, int pos, unsigned long long *host, int per_cta,
                             int *ctas);
 /* Asynchronous form for timing: enqueue `steps` greedy steps on the model's stream. */

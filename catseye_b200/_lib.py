@@ -63,6 +63,12 @@ SIGNATURES = {
     "cats_gemm_rtn": (None, [_i, _i, _i, _f, _vp, _vp, _f, _vp]),
     "cats_sgemm_dev": (_i, [_ch, _ch, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
     "cats_sgemm_dev_noalloc": (_i, [_ch, _ch, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i, _vp]),
+    "cats_im2col": (None, [_vp] + [_i] * 9 + [_vp]),
+    "cats_im2col_dev": (_i, [_vp] + [_i] * 9 + [_vp, _vp]),
+    "cats_conv2d_forward": (None, [_vp, _vp, _vp] + [_i] * 8),
+    "cats_conv2d_forward_dev": (_i, [_vp, _vp, _vp] + [_i] * 8 + [_vp]),
+    "cats_linear_forward": (None, [_vp, _vp, _vp, _i, _i, _i]),
+    "cats_linear_forward_dev": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
 }
 
 _LIB = None

@@ -5,6 +5,7 @@
 // buffers for the host-pointer drop-ins, and the sticky error status that the
 // void drop-in signatures cannot return.
 #include "../../include/catsgpu.h"
+#include "conv.cuh"
 #include "llm.cuh"
 #include "sgemm.cuh"
 #include <cstdio>
@@ -621,5 +622,97 @@ void cats_gemm_rnt(int M, int N, int K, float alpha, float *A, float *B, float b
 { cats_sgemm('N', 'T', M, N, K, alpha, A, B, beta, C); }
 void cats_gemm_rtn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C)
 { cats_sgemm('T', 'N', M, N, K, alpha, A, B, beta, C); }
+
+// ---------------------------------------------------------------- CNN forward
+static bool conv_geom_ok(int c, int h, int w, int kh, int kw, int ph, int pw, int sh, int sw)
+{
+    return c > 0 && h > 0 && w > 0 && kh > 0 && kw > 0 && ph >= 0 && pw >= 0 && sh > 0 && sw > 0 &&
+           conv_out(h, kh, ph, sh) > 0 && conv_out(w, kw, pw, sw) > 0;
+}
+
+int cats_im2col_dev(const float *im, int channels, int height, int width, int kh, int kw, int ph, int pw, int sh,
+                    int sw, float *col, void *stream)
+{
+    const char *what = "cats_im2col_dev";
+    if (!ensure_init()) return g.last_err;
+    if (!im || !col || !conv_geom_ok(channels, height, width, kh, kw, ph, pw, sh, sw)) return fail(CATS_ERR_ARG, what);
+    return check(launch_im2col(im, channels, height, width, kh, kw, ph, pw, sh, sw, col,
+                               stream ? (cudaStream_t)stream : g.stream),
+                 what);
+}
+
+void cats_im2col(const float *im, int channels, int height, int width, int kh, int kw, int ph, int pw, int sh,
+                 int sw, float *col)
+{
+    const char *what = "cats_im2col";
+    if (!ensure_init()) return;
+    if (!im || !col || !conv_geom_ok(channels, height, width, kh, kw, ph, pw, sh, sw)) { fail(CATS_ERR_ARG, what); return; }
+    const size_t ib = (size_t)channels * height * width * 4;
+    const size_t cb = (size_t)channels * kh * kw * conv_out(height, kh, ph, sh) * conv_out(width, kw, pw, sw) * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, ib) || grow((void **)&g.d_c, &g.cap_c, cb)) return;
+    if (check(cudaMemcpyAsync(g.d_a, im, ib, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_im2col_dev(g.d_a, channels, height, width, kh, kw, ph, pw, sh, sw, g.d_c, g.stream)) return;
+    if (check(cudaMemcpyAsync(col, g.d_c, cb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+int cats_conv2d_forward_dev(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch,
+                            int ksize, int pad, int stride, void *stream)
+{
+    const char *what = "cats_conv2d_forward_dev";
+    if (!ensure_init()) return g.last_err;
+    if (!x || !w || !z || batch <= 0 || ch <= 0 || !conv_geom_ok(ich, h, wd, ksize, ksize, pad, pad, stride, stride))
+        return fail(CATS_ERR_ARG, what);
+    return check(launch_conv2d_forward(x, w, z, batch, ich, h, wd, ch, ksize, pad, stride,
+                                       stream ? (cudaStream_t)stream : g.stream),
+                 what);
+}
+
+void cats_conv2d_forward(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch,
+                         int ksize, int pad, int stride)
+{
+    const char *what = "cats_conv2d_forward";
+    if (!ensure_init()) return;
+    if (!x || !w || !z || batch <= 0 || ch <= 0 || !conv_geom_ok(ich, h, wd, ksize, ksize, pad, pad, stride, stride)) {
+        fail(CATS_ERR_ARG, what);
+        return;
+    }
+    const size_t xb = (size_t)batch * ich * h * wd * 4, wb = (size_t)ch * ich * ksize * ksize * 4;
+    const size_t zb = (size_t)batch * ch * conv_out(h, ksize, pad, stride) * conv_out(wd, ksize, pad, stride) * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, xb) || grow((void **)&g.d_b, &g.cap_b, wb) ||
+        grow((void **)&g.d_c, &g.cap_c, zb))
+        return;
+    if (check(cudaMemcpyAsync(g.d_a, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_b, w, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_conv2d_forward_dev(g.d_a, g.d_b, g.d_c, batch, ich, h, wd, ch, ksize, pad, stride, g.stream)) return;
+    if (check(cudaMemcpyAsync(z, g.d_c, zb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+int cats_linear_forward_dev(const float *x, const float *w, float *z, int batch, int in, int out, void *stream)
+{
+    const char *what = "cats_linear_forward_dev";
+    if (!ensure_init()) return g.last_err;
+    if (!x || !w || !z || batch <= 0 || in <= 0 || out <= 0) return fail(CATS_ERR_ARG, what);
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    if (check(launch_bias_rows(w + (size_t)in * out, z, batch, out, st), what)) return g.last_err;
+    return cats_sgemm_dev('N', 'T', batch, out, in, 1.f, x, in, w, in, 1.f, z, out, st);
+}
+
+void cats_linear_forward(const float *x, const float *w, float *z, int batch, int in, int out)
+{
+    const char *what = "cats_linear_forward";
+    if (!ensure_init()) return;
+    if (!x || !w || !z || batch <= 0 || in <= 0 || out <= 0) { fail(CATS_ERR_ARG, what); return; }
+    const size_t xb = (size_t)batch * in * 4, wb = ((size_t)in * out + out) * 4, zb = (size_t)batch * out * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, xb) || grow((void **)&g.d_b, &g.cap_b, wb) ||
+        grow((void **)&g.d_c, &g.cap_c, zb))
+        return;
+    if (check(cudaMemcpyAsync(g.d_a, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_b, w, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_linear_forward_dev(g.d_a, g.d_b, g.d_c, batch, in, out, g.stream)) return;
+    if (check(cudaMemcpyAsync(z, g.d_c, zb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
 
 } // extern "C"

@@ -98,3 +98,53 @@ def sgemm_dev(ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, stream=None)
     _lib.check(lib.cats_sgemm_dev(ta.encode(), tb.encode(), m, n, k, alpha, _dp(a), lda, _dp(b), ldb, beta,
                                   _dp(c), ldc, stream), "cats_sgemm_dev")
     return c
+
+
+# ---------------------------------------------------------------- CNN forward
+def conv_out(n, k, pad, stride):
+    """Output length of a convolution axis (0 for a geometry the library refuses)."""
+    if stride <= 0 or k <= 0 or pad < 0:
+        return 0
+    return max(0, (n + 2 * pad - k) // stride + 1)
+
+
+def im2col(im, channels, height, width, kh, kw, ph, pw, sh, sw):
+    """im2col (catseye.h:508-532) of one host image -> host [c*kh*kw][oh*ow]."""
+    lib = _lib.init()
+    col = np.empty(channels * kh * kw * conv_out(height, kh, ph, sh) * conv_out(width, kw, pw, sw), np.float32)
+    _lib.call_void(lib.cats_im2col, _p(np.ascontiguousarray(im, np.float32)), channels, height, width, kh, kw, ph,
+                   pw, sh, sw, _p(col), what="cats_im2col")
+    return col
+
+
+def conv2d_forward(x, w, batch, ich, h, wd, ch, ksize, pad, stride):
+    """Batched convolution forward (CatsEye_convolutional_forward) on host arrays -> z[b][ch][oh*ow]."""
+    lib = _lib.init()
+    z = np.empty(batch * ch * conv_out(h, ksize, pad, stride) * conv_out(wd, ksize, pad, stride), np.float32)
+    _lib.call_void(lib.cats_conv2d_forward, _p(np.ascontiguousarray(x, np.float32)),
+                   _p(np.ascontiguousarray(w, np.float32)), _p(z), batch, ich, h, wd, ch, ksize, pad, stride,
+                   what="cats_conv2d_forward")
+    return z
+
+
+def conv2d_forward_dev(x, w, z, batch, ich, h, wd, ch, ksize, pad, stride, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_conv2d_forward_dev(_dp(x), _dp(w), _dp(z), batch, ich, h, wd, ch, ksize, pad, stride,
+                                           stream), "cats_conv2d_forward_dev")
+    return z
+
+
+def linear_forward(x, w, batch, n_in, n_out):
+    """Linear forward (CatsEye_linear_forward): w holds [out][in] weights then out biases."""
+    lib = _lib.init()
+    z = np.empty(batch * n_out, np.float32)
+    _lib.call_void(lib.cats_linear_forward, _p(np.ascontiguousarray(x, np.float32)),
+                   _p(np.ascontiguousarray(w, np.float32)), _p(z), batch, n_in, n_out, what="cats_linear_forward")
+    return z
+
+
+def linear_forward_dev(x, w, z, batch, n_in, n_out, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_linear_forward_dev(_dp(x), _dp(w), _dp(z), batch, n_in, n_out, stream),
+               "cats_linear_forward_dev")
+    return z

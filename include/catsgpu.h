@@ -203,6 +203,31 @@ int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const flo
 int cats_sgemm_dev_noalloc(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda,
                            const float *b, int ldb, float beta, float *c, int ldc, void *stream);
 
+/* ---- CNN forward callers of the GEMM ---------------------------------------
+ * Replace im2col (catseye.h:508-532), CatsEye_convolutional_forward
+ * (catseye.h:557-588) and CatsEye_linear_forward (catseye.h:416-444) for a
+ * whole batch.  The plain forms take host pointers (copied in and out); the
+ * _dev forms take device pointers and enqueue on `stream` (NULL: the
+ * library's stream).  Sizes must be positive, ksize/stride >= 1, pad >= 0. */
+
+/* col[(c*kh + i)*kw + j][oh][ow] = im[c][oh*sh - ph + i][ow*sw - pw + j] (0 outside). */
+void cats_im2col(const float *im, int channels, int height, int width, int kh, int kw, int ph, int pw,
+                 int sh, int sw, float *col);
+int cats_im2col_dev(const float *im, int channels, int height, int width, int kh, int kw, int ph, int pw,
+                    int sh, int sw, float *col, void *stream);
+/* z[b][ch][oh*ow] = sum_k w[ch][k] * im2col(x[b])[k][oh*ow], x = [batch][ich][h][wd],
+ * w = [ch][ich*ksize*ksize], no bias; oh = (h + 2*pad - ksize)/stride + 1, ow likewise.
+ * One implicit GEMM over the batch (the reference runs im2col + gemm_rnn per sample).
+ * The reference's 1x1 convolution multiplies x without im2col, which is the
+ * same only for pad 0 and stride 1 (the only 1x1 form its layers build). */
+void cats_conv2d_forward(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch,
+                         int ksize, int pad, int stride);
+int cats_conv2d_forward_dev(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch,
+                            int ksize, int pad, int stride, void *stream);
+/* z[b][o] = sum_i x[b][i] * w[o][i] + w[in*out + o] (gemm_rnt, then the bias kept after the weights). */
+void cats_linear_forward(const float *x, const float *w, float *z, int batch, int in, int out);
+int cats_linear_forward_dev(const float *x, const float *w, float *z, int batch, int in, int out, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -24,6 +24,14 @@ cpu_baseline : the reference's own CPU step (oracle/_ref, all cores) on a
         bounded sample (1- and 2-layer models of the same shapes, extrapolated).
 
 --impl reference times only that CPU reference on the same workload.
+
+--workload sgemm_4096 | cnn_forward_b128 measure the CNN side instead: a
+4096^3 fp32 NN sgemm (cats_sgemm_dev), or the 32x32x3 CNN's four
+convolutions and two linear layers at batch 128 (cats_conv2d_forward_dev /
+cats_linear_forward_dev, 25.15 GFLOP).  value = GFLOP/s on device buffers;
+e2e = the host-pointer API with its copies; roofline against the nominal
+fp32 SIMT peak; cpu_baseline = the reference's gemm_rnn / layer forwards
+(oracle/_ref, OpenMP on all cores) on a bounded sample.
 With torchrun (N > 1) every rank decodes its own replica (no collective on
 the data path yet): value = sum over ranks, time = max over ranks.
 """
@@ -236,6 +244,219 @@ def run_ours(args, dist, rank, ws, local):
     return ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg
 
 
+# ------------------------------------------------ fp32 GEMM workloads (CNN side)
+# (kind, batch, ich|in, h, w, ch|out, ksize, pad, stride): the 32x32x3 CNN's
+# four convolutions and two linear layers at batch 128 (25.15 GFLOP)
+CNN_LAYERS = [("conv", 128, 3, 32, 32, 64, 3, 1, 1), ("conv", 128, 64, 32, 32, 64, 3, 1, 1),
+              ("conv", 128, 64, 16, 16, 128, 3, 1, 1), ("conv", 128, 128, 16, 16, 128, 3, 1, 1),
+              ("linear", 128, 8192, 0, 0, 256, 0, 0, 0), ("linear", 128, 256, 0, 0, 10, 0, 0, 0)]
+SGEMM_SIZE = 4096
+
+
+def _conv_out(n, k, pad, stride):
+    return (n + 2 * pad - k) // stride + 1
+
+
+def layer_flops(L):
+    kind, b, ci, h, w, co, k, pad, s = L
+    if kind == "linear":
+        return 2 * b * ci * co
+    return 2 * b * co * _conv_out(h, k, pad, s) * _conv_out(w, k, pad, s) * ci * k * k
+
+
+def fp32_peak():
+    """Nominal fp32 SIMT peak: 148 SMs x 128 FMA/clock x 2 x the max SM clock."""
+    mhz = 1965.0
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        mhz = float(json.load(open(p)).get("sm_max_mhz", mhz))
+    return 148 * 128 * 2 * mhz * 1e6 / 1e12
+
+
+def gemm_cpu_reference(workload):
+    """The reference's own CPU code (oracle/_ref, OpenMP on all cores) on a bounded sample."""
+    from oracle.cpu import Reference
+    rc = Reference("cnn")
+    rng = np.random.default_rng(SEED)
+    if workload == "sgemm_4096":
+        n = 2048
+        A = rng.uniform(-1, 1, n * n).astype(np.float32)
+        B = rng.uniform(-1, 1, n * n).astype(np.float32)
+        C = np.zeros(n * n, np.float32)
+        ts = []
+        for _ in range(2):
+            t0 = time.perf_counter()
+            rc.sgemm("N", "N", n, n, n, 1.0, A, B, 0.0, C)
+            ts.append(time.perf_counter() - t0)
+        return {"value": 2 * n ** 3 / min(ts) / 1e9, "unit": "GFLOP/s", "cores": os.cpu_count(), "kind": "reference",
+                "sample": f"gemm_rnn {n}^3 (17.2 GFLOP), best of 2"}
+    # CNN: every layer at batch 4 (the linear layers at 128), scaled to batch 128
+    t_total = 0.0
+    for L in CNN_LAYERS:
+        kind, b, ci, h, w, co, k, pad, s = L
+        if kind == "conv":
+            bs = 4
+            x = rng.uniform(0, 1, bs * ci * h * w).astype(np.float32)
+            wt = rng.standard_normal(co * ci * k * k).astype(np.float32)
+            t0 = time.perf_counter()
+            rc.conv2d_forward(x, wt, bs, ci, h, w, co, k, pad, s)
+            t_total += (time.perf_counter() - t0) * b / bs
+        else:
+            x = rng.uniform(-1, 1, b * ci).astype(np.float32)
+            wt = rng.uniform(-1, 1, ci * co + co).astype(np.float32)
+            t0 = time.perf_counter()
+            rc.linear_forward(x, wt, b, ci, co)
+            t_total += time.perf_counter() - t0
+    gf = sum(layer_flops(L) for L in CNN_LAYERS)
+    return {"value": gf / t_total / 1e9, "unit": "GFLOP/s", "cores": os.cpu_count(), "kind": "reference",
+            "sample": f"convolutions at batch 4 scaled x32, linear layers at batch 128; {t_total:.2f} s per forward"}
+
+
+def run_gemm(args, dist, rank, ws, local):
+    """One step: a 4096^3 NN sgemm, or the CNN's conv/linear layers at batch 128."""
+    import torch
+    from catseye_b200 import _lib
+    from catseye_b200 import matmul as mm
+    _lib.init(local)
+    torch.cuda.set_device(local)
+    # a stream of our own: the default stream's handle is 0, which the
+    # library reads as "the library's stream" (events there would not see it)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    assert sp != 0
+    g = torch.Generator(device="cuda").manual_seed(SEED + rank)
+
+    def urand(n, lo=-1.0, hi=1.0):
+        return torch.rand(n, device="cuda", generator=g) * (hi - lo) + lo
+
+    if args.workload == "sgemm_4096":
+        n = SGEMM_SIZE
+        A, B, Cm = urand(n * n), urand(n * n), torch.empty(n * n, device="cuda")
+        flops, launches = 2 * n ** 3, 1
+        hA, hB, hC = A.cpu().numpy(), B.cpu().numpy(), np.empty(n * n, np.float32)
+
+        def step():
+            mm.sgemm_dev("N", "N", n, n, n, 1.0, A, n, B, n, 0.0, Cm, n, stream=sp)
+
+        def host_step():
+            mm.sgemm("N", "N", n, n, n, 1.0, hA, hB, 0.0, hC)
+            return hC
+
+        h2d, d2h = 2 * n * n * 4, n * n * 4
+        cfg = {"workload": "sgemm_4096", "M": n, "N": n, "K": n, "form": "NN", "alpha": 1.0, "beta": 0.0,
+               "l2": "A, B, C 64 MB each (192 MB > 126 MB L2); no flush"}
+    else:
+        bufs, host = [], []
+        for L in CNN_LAYERS:
+            kind, b, ci, h, w, co, k, pad, s = L
+            if kind == "conv":
+                nz = b * co * _conv_out(h, k, pad, s) * _conv_out(w, k, pad, s)
+                x, wt = urand(b * ci * h * w, 0.0, 1.0), urand(co * ci * k * k) * (2.0 / (ci * k * k)) ** 0.5
+            else:
+                nz = b * co
+                x, wt = urand(b * ci), urand(ci * co + co) * 0.05
+            bufs.append((L, x, wt, torch.empty(nz, device="cuda")))
+            host.append((L, x.cpu().numpy(), wt.cpu().numpy()))
+        flops = sum(layer_flops(L) for L in CNN_LAYERS)
+        launches = 9   # 4 convolutions; per linear layer a bias fill and the GEMM (+ split-K reduce for 8192->256)
+
+        def step():
+            for L, x, wt, z in bufs:
+                kind, b, ci, h, w, co, k, pad, s = L
+                if kind == "conv":
+                    mm.conv2d_forward_dev(x, wt, z, b, ci, h, w, co, k, pad, s, stream=sp)
+                else:
+                    mm.linear_forward_dev(x, wt, z, b, ci, co, stream=sp)
+
+        def host_step():
+            out = None
+            for L, x, wt in host:
+                kind, b, ci, h, w, co, k, pad, s = L
+                out = (mm.conv2d_forward(x, wt, b, ci, h, w, co, k, pad, s) if kind == "conv"
+                       else mm.linear_forward(x, wt, b, ci, co))
+            return out
+
+        h2d = sum(x.nbytes + wt.nbytes for _, x, wt in host)
+        d2h = sum(z.numel() * 4 for _, _, _, z in bufs)
+        cfg = {"workload": "cnn_forward_b128", "batch": 128, "input": "32x32x3",
+               "layers": "conv3x3 3->64, 64->64 (32x32), 64->128, 128->128 (16x16), linear 8192->256, 256->10",
+               "excluded": "ReLU and max-pool (elementwise, outside the GEMM path); each layer gets its own input",
+               "l2": "activations 32-268 MB per layer; no flush"}
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    torch.cuda.synchronize()   # inputs were made on the default stream
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # end to end through the host-pointer API (copies in and out every step)
+    host_step()
+    e2e_steps = max(1, min(args.e2e_steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        host_step()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    return ms, e2e_s, e2e_steps, flops, launches, h2d, d2h, cfg, clk.summary()
+
+
+def gemm_main(args):
+    metric = "SGEMM GFLOP/s" if args.workload == "sgemm_4096" else "CNN forward GFLOP/s (conv + linear, batch 128)"
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        cb = gemm_cpu_reference(args.workload)
+        print(json.dumps({"impl": "reference", "metric": metric, "value": round(cb["value"], 2), "unit": "GFLOP/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": args.workload}, "cpu_baseline": cb,
+                          "e2e": {"value": round(cb["value"], 2), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
+    dist, rank, ws, local = dist_init()
+    ms, e2e_s, e2e_steps, flops, launches, h2d, d2h, cfg, clocks = run_gemm(args, dist, rank, ws, local)
+    if rank == 0:
+        gfs = ws * flops * args.steps / (ms * 1e-3) / 1e9
+        peak = fp32_peak()
+        achieved = flops * args.steps / (ms * 1e-3) / 1e12
+        cfg["parallelism"] = f"replicas{ws}" if ws > 1 else "single"
+        line = {"metric": metric, "value": round(gfs, 1), "unit": "GFLOP/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+                "roofline": {"bound": "fp32-simt", "kernel": "k_sgemm" if args.workload == "sgemm_4096"
+                             else "k_conv_fwd + k_sgemm", "achieved": round(achieved, 2), "peak": round(peak, 1),
+                             "peak_kind": "nominal (148 SMs x 128 FMA/clock x 2 x max SM clock)", "unit": "TFLOP/s",
+                             "frac": round(achieved / peak, 4), "traffic": None},
+                "e2e": {"value": round(ws * flops * e2e_steps / e2e_s / 1e9, 1), "unit": "GFLOP/s",
+                        "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+                "gpu_launches": launches * args.steps, "clocks": clocks}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = gemm_cpu_reference(args.workload)
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -243,11 +464,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama7b_q4_0", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="llama7b_q4_0", choices=sorted(WORKLOADS) + ["sgemm_4096", "cnn_forward_b128"])
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload in ("sgemm_4096", "cnn_forward_b128"):
+        gemm_main(args)
+        return
 
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

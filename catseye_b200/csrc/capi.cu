@@ -361,9 +361,11 @@ cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg)
         return nullptr;
     }
     LlmConfig c{cfg->dim, cfg->hidden, cfg->n_layers, cfg->n_heads, cfg->n_kv_heads, cfg->vocab, cfg->seq_len,
-                cfg->wtype, cfg->tp_rank, cfg->tp_size > 0 ? cfg->tp_size : 1};
-    if (c.tp_size != 1) { fail(CATS_ERR_UNSUPPORTED, "cats_gpu_llm_create: tensor parallel"); return nullptr; }
+                cfg->wtype, cfg->tp_size > 1 ? cfg->tp_rank : 0, cfg->tp_size > 0 ? cfg->tp_size : 1};
+    if (c.tp_rank < 0 || c.tp_rank >= c.tp_size) { fail(CATS_ERR_ARG, "cats_gpu_llm_create: tp_rank"); return nullptr; }
     cats_gpu_llm *h = new cats_gpu_llm();
+    // the persistent kernel has no exchange step yet: sharded models use the per-phase graph
+    if (c.tp_size > 1) h->engine = CATS_ENGINE_GRAPH;
     int rc = llm_alloc(&h->m, c);
     if (rc == CATS_OK && cudaMalloc(&h->tok_log, (size_t)(c.seq_len + 1) * 4) != cudaSuccess) rc = CATS_ERR_NOMEM;
     if (rc != CATS_OK) {
@@ -409,6 +411,7 @@ static int ensure_graph(cats_gpu_llm *h)
         return rc ? fail(rc, "llm: persistent decode setup") : CATS_OK;
     }
     if (h->m.exec) return CATS_OK;
+    if (h->m.c.tp_size > 1 && !h->m.comm_ctx) return fail(CATS_ERR_ARG, "llm: tensor parallel model not connected");
     return check(llm_build_graph(&h->m), "llm: graph capture");
 }
 
@@ -431,8 +434,27 @@ int cats_gpu_llm_set_engine(cats_gpu_llm *h, int engine)
 {
     if (!h || (engine != CATS_ENGINE_PERSISTENT && engine != CATS_ENGINE_GRAPH))
         return fail(CATS_ERR_ARG, "cats_gpu_llm_set_engine");
+    if (engine == CATS_ENGINE_PERSISTENT && h->m.c.tp_size > 1)
+        return fail(CATS_ERR_UNSUPPORTED, "cats_gpu_llm_set_engine: the persistent engine runs one GPU");
     h->engine = engine;
     return CATS_OK;
+}
+
+size_t cats_gpu_tp_unique_id_bytes(void) { return tp_unique_id_bytes(); }
+
+int cats_gpu_tp_unique_id(void *id, size_t bytes)
+{
+    if (!ensure_init()) return g.last_err;
+    int rc = tp_unique_id(id, bytes);
+    return rc ? fail(rc, "cats_gpu_tp_unique_id") : CATS_OK;
+}
+
+int cats_gpu_llm_tp_connect(cats_gpu_llm *h, const void *id)
+{
+    if (!h || !id || h->m.c.tp_size < 2) return fail(CATS_ERR_ARG, "cats_gpu_llm_tp_connect");
+    if (check(cudaSetDevice(g.device), "cats_gpu_llm_tp_connect")) return g.last_err;
+    int rc = tp_connect(&h->m, id);
+    return rc ? fail(rc, "cats_gpu_llm_tp_connect") : CATS_OK;
 }
 
 int cats_gpu_llm_set_position(cats_gpu_llm *h, int token, int pos)

@@ -216,6 +216,18 @@ __global__ void k_advance(StepParams *p, unsigned long long *argmax, int vocab, 
     *argmax = 0ull;
 }
 
+// x += delta (tensor parallel: the allreduced output of wo or w2, :1731-1733, :1759-1761)
+__global__ void k_residual_add(float *__restrict__ x, const float *__restrict__ delta, int n)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] += delta[i];
+}
+
+static cudaError_t launch_residual_add(float *x, const float *delta, int n, cudaStream_t st)
+{
+    k_residual_add<<<std::min(cdiv(n, 256), 148), 256, 0, st>>>(x, delta, n);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------ model setup
 static int pick_stages(const WeightLayout &L)
 {
@@ -308,10 +320,12 @@ static void free_w(DevWeight &w)
 
 void llm_free(LlmModel *m)
 {
+    if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     m->exec = nullptr;
     m->graph = nullptr;
+    tp_release(m);   // after the graph that holds its NCCL calls
     for (auto &w : m->qkv) free_w(w);
     for (auto &w : m->wo) free_w(w);
     for (auto &w : m->w13) free_w(w);
@@ -580,13 +594,18 @@ cudaError_t llm_enqueue_step(LlmModel *m, bool advance)
 
         if ((e = launch_attention(m, l, st))) return e;
 
+        // wo (and w2 below): with tensor parallelism each rank holds a column
+        // slice, so its output is a partial sum: sum-allreduce, then add
         a = base_args(m->wo[l], m->err);
         a.xmode = xmode;
         a.x = m->xb;
         if (!tp) { a.epi = EPI_ADD; a.out = m->x; }
         else { a.epi = EPI_STORE; a.out = m->delta; }
         if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
-        if (tp) { m->allreduce(m->comm_ctx, m->delta, c.dim, st); }
+        if (tp) {
+            m->allreduce(m->comm_ctx, m->delta, c.dim, st);
+            if ((e = launch_residual_add(m->x, m->delta, c.dim, st))) return e;
+        }
 
         a = base_args(m->w13[l], m->err);
         a.xmode = xmode;
@@ -594,15 +613,18 @@ cudaError_t llm_enqueue_step(LlmModel *m, bool advance)
         a.norm_w = m->rms_ffn + (size_t)l * c.dim;
         a.epi = EPI_SWIGLU;
         a.out = m->hb;
-        if (tp) return cudaErrorNotSupported;   // the residual-add prologue for TP is wired by the TP layer
         if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
 
         a = base_args(m->w2[l], m->err);
         a.xmode = xmode;
         a.x = m->hb;
-        a.epi = EPI_ADD;
-        a.out = m->x;
+        if (!tp) { a.epi = EPI_ADD; a.out = m->x; }
+        else { a.epi = EPI_STORE; a.out = m->delta; }
         if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
+        if (tp) {
+            m->allreduce(m->comm_ctx, m->delta, c.dim, st);
+            if ((e = launch_residual_add(m->x, m->delta, c.dim, st))) return e;
+        }
     }
     MatvecArgs a = base_args(m->cls, m->err);
     a.xmode = xmode;
@@ -611,7 +633,13 @@ cudaError_t llm_enqueue_step(LlmModel *m, bool advance)
     a.epi = EPI_STORE_ARGMAX;
     a.out = m->logits + m->vocab_off;
     a.argmax = m->argmax;
+    a.argmax_base = m->vocab_off;
     if ((e = launch_matvec(a, 2, c.wtype, st, true))) return e;
+    if (tp) {
+        // the greedy token over every rank's vocabulary rows, and the full logits
+        m->argmax_reduce(m->comm_ctx, m->argmax, st);
+        m->allgather(m->comm_ctx, m->logits, (size_t)m->vocab_loc, c.tp_rank, st);
+    }
     if (advance && (e = launch_advance(m, st))) return e;
     return cudaSuccess;
 }

@@ -25,6 +25,7 @@ struct StepParams {
 
 typedef void (*AllreduceFn)(void *ctx, float *buf, size_t count, cudaStream_t st);
 typedef void (*ArgmaxReduceFn)(void *ctx, unsigned long long *key, cudaStream_t st);
+typedef void (*AllgatherFn)(void *ctx, float *buf, size_t count_per_rank, int rank, cudaStream_t st);
 
 struct LlmModel {
     LlmConfig c{};
@@ -57,11 +58,19 @@ struct LlmModel {
     unsigned int *dec_bar = nullptr;      // [0] grid barrier counter, [1] abort flag
     int dec_stages = 0, dec_max_splits = 32;
     uint32_t dec_slot = 0, dec_xs = 0;
-    // tensor parallel hooks (NCCL), null when tp_size == 1
+    // tensor parallel hooks (NCCL, tp.cu), null when tp_size == 1
     AllreduceFn allreduce = nullptr;
     ArgmaxReduceFn argmax_reduce = nullptr;
+    AllgatherFn allgather = nullptr;
     void *comm_ctx = nullptr;
 };
+
+// tensor parallel (tp.cu): an NCCL unique id (made on one rank, passed to all),
+// the communicator of a model's rank, and its release
+int tp_unique_id(void *out, size_t bytes);
+size_t tp_unique_id_bytes();
+int tp_connect(LlmModel *m, const void *id_bytes);
+void tp_release(LlmModel *m);
 
 int llm_alloc(LlmModel *m, const LlmConfig &c);
 void llm_free(LlmModel *m);

@@ -292,7 +292,7 @@ __device__ __forceinline__ void mv_consume(const MatvecArgs &a, const SmemPlan &
                     if (a.epi == EPI_ADD) a.out[row] += acc[r];
                     else a.out[row] = acc[r];
                     if (a.epi == EPI_STORE_ARGMAX) {
-                        const unsigned long long k = argmax_key(acc[r], row);
+                        const unsigned long long k = argmax_key(acc[r], a.argmax_base + row);
                         best = k > best ? k : best;
                     }
                 }

@@ -83,6 +83,7 @@ struct MatvecArgs {
     int q_dim = 0, kv_dim = 0, head_size = 0;
     int kv_rows = 0;                  // QKV: rows of the cache (seq_len); pos >= kv_rows is refused
     unsigned long long *argmax = nullptr;
+    int argmax_base = 0;              // ARGMAX: index of row 0 (a tensor-parallel rank's vocabulary offset)
 
     int *err = nullptr;               // device error word
 };

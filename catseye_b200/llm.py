@@ -76,6 +76,12 @@ class GpuLLM:
     def init_random(self, seed, std=0.02):
         _lib.check(self.lib.cats_gpu_llm_init_random(self.h, seed, std), "init_random")
 
+    def tp_connect(self, unique_id):
+        """Join this rank's NCCL communicator (every rank calls it with the same id)."""
+        _framework_nccl_first()
+        buf = C.create_string_buffer(bytes(unique_id), len(unique_id))
+        _lib.check(self.lib.cats_gpu_llm_tp_connect(self.h, buf), "tp_connect")
+
     def step(self, token, pos, out=None):
         """cats_llama2_transformer(token, pos): logits of this step (host numpy)."""
         out = self._logits if out is None else out
@@ -166,3 +172,29 @@ T_EMB, T_RMS_ATT, T_RMS_FFN, T_RMS_FINAL, T_WCLS, T_LAYER0 = 0, 1, 2, 3, 4, 16
 def layer_tensor_id(layer, k):
     """k: 0 wq, 1 wk, 2 wv, 3 wo, 4 w1, 5 w2, 6 w3."""
     return T_LAYER0 + layer * 8 + k
+
+
+def _framework_nccl_first():
+    """The library opens NCCL at first use and takes a libnccl.so.2 that is
+    already loaded; importing torch first makes that torch's own copy, so the
+    process holds one NCCL."""
+    import torch  # noqa: F401
+
+
+def tp_unique_id():
+    """A fresh NCCL unique id for a tensor-parallel model (bytes)."""
+    _framework_nccl_first()
+    lib = _lib.init()
+    n = lib.cats_gpu_tp_unique_id_bytes()
+    buf = C.create_string_buffer(n)
+    _lib.check(lib.cats_gpu_tp_unique_id(buf, n), "tp_unique_id")
+    return buf.raw
+
+
+def tp_share_id(group=None, make_id=tp_unique_id):
+    """Rank 0 of the torch.distributed group makes the unique id, every rank
+    gets the same bytes back (broadcast over the group's backend, gloo or nccl)."""
+    import torch.distributed as dist
+    box = [make_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    return box[0]

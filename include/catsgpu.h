@@ -138,6 +138,20 @@ int cats_gpu_llm_generate(cats_gpu_llm *m, int token, int pos, int steps, int *t
 #define CATS_ENGINE_PERSISTENT 0
 #define CATS_ENGINE_GRAPH      1
 int cats_gpu_llm_set_engine(cats_gpu_llm *m, int engine);
+/* Tensor parallelism, one process per GPU (tp_size > 1 in the config).  The
+ * model is sharded as the Megatron split of the llama layer: wq/wk/wv and
+ * w1/w3 by rows (whole heads), wo and w2 by input columns on 32-block
+ * boundaries, the classifier by vocabulary rows.  One rank makes an NCCL
+ * unique id (cats_gpu_tp_unique_id_bytes() bytes) and the caller hands it to
+ * every rank; each rank calls cats_gpu_llm_tp_connect with it (the calls of
+ * all ranks must overlap: NCCL waits for every rank) before its first step.
+ * Sharded models run the per-phase graph engine: after wo and after w2 an
+ * NCCL sum allreduce of dim floats, after the classifier a max allreduce of
+ * the greedy key and an allgather of the logits.  Every rank feeds the same
+ * tokens and gets the full logits. */
+size_t cats_gpu_tp_unique_id_bytes(void);
+int cats_gpu_tp_unique_id(void *id, size_t bytes);
+int cats_gpu_llm_tp_connect(cats_gpu_llm *m, const void *id);
 /* One step of the persistent engine with a phase timeline, the counterpart
  * of the reference's per-layer CATS_CHECK timings (catseye.h:2110-2117):
  * host receives [2][ctas][per_cta] stamps taken by thread 0 of each CTA:

@@ -1,0 +1,57 @@
+"""Host logic of tensor parallelism on CPU (gloo, world size 2): every rank
+receives rank 0's unique id, and the sharding rule refuses shapes whose
+slices do not fall on 32-element blocks."""
+import os
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank(rank, world, port, out):
+    import torch.distributed as dist
+    from catseye_b200.llm import tp_share_id
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        got = tp_share_id(make_id=lambda: bytes(range(128)) if rank == 0 else b"wrong")
+        out.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_unique_id_reaches_every_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0] == res[1] == bytes(range(128))
+
+
+@pytest.mark.parametrize("dim,heads,kv,hidden,tp,ok", [
+    (4096, 32, 32, 11008, 2, True), (4096, 32, 32, 11008, 8, True), (8192, 64, 8, 28672, 8, True),
+    (288, 6, 6, 768, 2, False),      # 144 columns per rank: not a whole number of 32-blocks
+    (512, 8, 2, 1376, 4, False),     # 2 kv heads cannot split 4 ways
+    (4096, 32, 32, 11008, 3, False)])
+def test_sharding_rule(dim, heads, kv, hidden, tp, ok):
+    """The rule llm_alloc applies (C side) restated: heads, kv heads, hidden
+    and vocab split evenly, every column slice a whole number of blocks."""
+    vocab = 32000
+    fits = (dim % heads == 0 and heads % kv == 0 and heads % tp == 0 and kv % tp == 0 and hidden % tp == 0
+            and vocab % tp == 0 and (hidden // tp) % 32 == 0 and (dim // tp) % 32 == 0)
+    assert fits == ok

@@ -7,6 +7,7 @@
 #include "../../include/catsgpu.h"
 #include "conv.cuh"
 #include "llm.cuh"
+#include "qgemm.cuh"
 #include "sgemm.cuh"
 #include <cstdio>
 #include <cstdlib>
@@ -38,6 +39,8 @@ struct Ctx {
     size_t d_out_cap = 0;
     float *d_a = nullptr, *d_b = nullptr, *d_c = nullptr, *d_work = nullptr;
     size_t cap_a = 0, cap_b = 0, cap_c = 0, cap_work = 0;
+    __half *d_x16 = nullptr;   // fp16 activations of the batched product
+    size_t cap_x16 = 0;
 };
 
 Ctx g;
@@ -207,10 +210,11 @@ void cats_gpu_term(void)
     cudaStreamSynchronize(g.stream);
     for (auto &kv : g.weights) if (kv.second.W.ptr) cudaFree(kv.second.W.ptr);
     g.weights.clear();
-    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err};
+    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err, g.d_x16};
     for (void *b : bufs) if (b) cudaFree(b);
     g.d_x = nullptr; g.d_out = nullptr; g.d_a = g.d_b = g.d_c = g.d_work = nullptr; g.d_err = nullptr;
-    g.d_x_cap = g.d_out_cap = g.cap_a = g.cap_b = g.cap_c = g.cap_work = 0;
+    g.d_x16 = nullptr;
+    g.d_x_cap = g.d_out_cap = g.cap_a = g.cap_b = g.cap_c = g.cap_work = g.cap_x16 = 0;
     cudaStreamDestroy(g.stream);
     g.stream = nullptr;
     g.init = false;
@@ -327,6 +331,39 @@ int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q
     a.epi = EPI_STORE;
     a.out = d_out;
     return check(launch_matvec(a, r.W.L.rpw, r.type, st, false), what);
+}
+
+int cats_gpu_qgemm_dev(const void *w, const float *d_x, float *d_y, int T, void *stream)
+{
+    const char *what = "cats_gpu_qgemm_dev";
+    if (!ensure_init()) return g.last_err;
+    auto it = g.weights.find(w);
+    if (it == g.weights.end()) return fail(CATS_ERR_ARG, "cats_gpu_qgemm_dev: weight not registered");
+    Reg &r = it->second;
+    if (!d_x || !d_y || T <= 0 || ((uintptr_t)d_x % 16)) return fail(CATS_ERR_ARG, what);
+    if (!qgemm_supported(r.W.L)) return fail(CATS_ERR_UNSUPPORTED, what);
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    const size_t xb = (size_t)T * r.n * 2;
+    if (grow((void **)&g.d_x16, &g.cap_x16, xb)) return g.last_err;
+    if (check(launch_f32_to_f16(d_x, g.d_x16, (long long)T * r.n, st), what)) return g.last_err;
+    return check(launch_qgemm(r.W.L, r.W.ptr, g.d_x16, d_y, T, g.d_err, st), what);
+}
+
+int cats_gpu_qgemm(const void *w, const float *x, float *y, int T)
+{
+    const char *what = "cats_gpu_qgemm";
+    if (!ensure_init()) return g.last_err;
+    auto it = g.weights.find(w);
+    if (it == g.weights.end()) return fail(CATS_ERR_ARG, "cats_gpu_qgemm: weight not registered");
+    Reg &r = it->second;
+    if (!x || !y || T <= 0) return fail(CATS_ERR_ARG, what);
+    const size_t xb = (size_t)T * r.n * 4, yb = (size_t)T * r.d * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, xb) || grow((void **)&g.d_c, &g.cap_c, yb)) return g.last_err;
+    if (check(cudaMemcpyAsync(g.d_a, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return g.last_err;
+    if (int rc = cats_gpu_qgemm_dev(w, g.d_a, g.d_c, T, g.stream)) return rc;
+    if (check(cudaMemcpyAsync(y, g.d_c, yb, cudaMemcpyDeviceToHost, g.stream), what)) return g.last_err;
+    if (check(cudaStreamSynchronize(g.stream), what)) return g.last_err;
+    return check_device_error(what);
 }
 
 int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mode, void *stream)

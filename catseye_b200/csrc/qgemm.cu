@@ -1,0 +1,359 @@
+// qgemm.cu — batched product of a block-quantized weight with T activation
+// vectors on the 5th-generation tensor cores (tcgen05, TMEM accumulators):
+//     Y[T][d] = X[T][n] * W[d][n]^T
+// i.e. T matmul calls of the llama runtime at once (llm/catseye_llm.h:1531,
+// 844-879 for one vector), the dense contraction of a prefill or of a
+// batched decode step.  The reference has no batched form; it is defined as
+// the same sums with fp16 operands (dequantized weights, rounded activations)
+// and fp32 accumulation: relative error <= 1e-3.
+//
+// CTA: 128 weight rows (the UMMA M) x BN tokens (the UMMA N, 16..256), K in
+// slices of 64 (two 32-element blocks).
+//  * Producers (warps 0-3, one weight row per thread): read the row's two
+//    blocks from the weight's tile layout (the matvec's, so prefill and decode
+//    share one copy of the weights in HBM), dequantize to fp16 and store the
+//    row in the K-major 128-byte-swizzled form UMMA reads; copy the BN
+//    activation rows (fp16, converted once per call) with cp.async into the
+//    same form; then fence.proxy.async and arrive on the stage's full barrier.
+//  * MMA warp (warp 4, one thread): four K=16 tcgen05.mma per stage into the
+//    TMEM accumulator; tcgen05.commit releases the stage when they complete.
+//  * Epilogue: after a final commit, warp w reads TMEM lanes 32w..32w+31 (its
+//    weight rows) 16 columns at a time and writes Y (consecutive lanes are
+//    consecutive rows of Y: coalesced).
+// Every wait is bounded; TMEM is freed on every path.
+#include "qgemm.cuh"
+#include <algorithm>
+
+namespace cats {
+
+constexpr int QG_M = 128;
+constexpr int QG_K = 64;
+constexpr int QG_STAGES = 4;
+constexpr int QG_PROD = 128;                 // producer threads (4 warps)
+constexpr int QG_THREADS = QG_PROD + 32;     // + the MMA warp
+constexpr uint32_t QG_A_BYTES = QG_M * 128;  // one stage of weight rows (fp16, 64 per row)
+
+struct QgemmArgs {
+    const uint8_t *w;                 // tile layout (matvec.cuh WeightLayout)
+    int type, n, d, R, units, nseg;
+    uint32_t full_chunk;
+    unsigned long long tile_bytes;
+    const __half *x;                  // [T][n] fp16
+    float *y;                         // [T][d]
+    int T;
+    int *err;
+};
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (the canonical
+// UMMA K-major SW128 layout: SBO = 1024 B, LBO unused = 1, version 1).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr)
+{
+    return (uint64_t)((smem_addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A and B f16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N)
+{
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw128(int r, int c)
+{
+    return (uint32_t)r * 128 + (uint32_t)((c ^ (r & 7)) * 16);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Dequantize the two blocks of weight row `row` at K slice kb into 64 fp16,
+// stored swizzled at dst (the row's 128 bytes).
+template <int WT>
+__device__ __forceinline__ void stage_weight_row(const QgemmArgs &a, int row, int kb, uint8_t *dst_row_base, int r)
+{
+    uint32_t h[32];   // 64 fp16, two per word
+    if (row < a.d) {
+        const int u = 2 * kb, s = u / MV_SEG_UNITS, u0 = u % MV_SEG_UNITS;
+        const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
+        const int t = row / a.R, rr = row % a.R;
+        const uint8_t *ch = a.w + (size_t)t * a.tile_bytes + (size_t)s * a.full_chunk;
+        const uint32_t sstride = (uint32_t)round_up((size_t)us * 2, 16);
+        const uint32_t ub = WT == W_Q4_0 ? 16 : 32;
+        const uint32_t sc2 = *reinterpret_cast<const uint32_t *>(ch + (size_t)a.R * us * ub + rr * sstride + u0 * 2);
+        const float d0 = half_bits_to_float((uint16_t)(sc2 & 0xffff)), d1 = half_bits_to_float((uint16_t)(sc2 >> 16));
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            const float dd = b ? d1 : d0;
+            int8_t q[32];
+            if (WT == W_Q4_0) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + u0 + b) * 16);
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const uint32_t byte = (wv[j >> 2] >> ((j & 3) * 8)) & 0xff;
+                    q[j] = (int8_t)((int)(byte & 0xf) - 8);      // element j: low nibble
+                    q[j + 16] = (int8_t)((int)(byte >> 4) - 8);  // element j + 16: high nibble
+                }
+            } else {
+                const uint4 lo = *reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2) * us + u0 + b) * 16);
+                const uint4 hi = *reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2 + 1) * us + u0 + b) * 16);
+                const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+                for (int j = 0; j < 32; j++) q[j] = (int8_t)((wv[j >> 2] >> ((j & 3) * 8)) & 0xff);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const __half lo16 = __float2half_rn((float)q[2 * j] * dd);
+                const __half hi16 = __float2half_rn((float)q[2 * j + 1] * dd);
+                h[b * 16 + j] = (uint32_t)__half_as_ushort(lo16) | ((uint32_t)__half_as_ushort(hi16) << 16);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) h[j] = 0u;
+    }
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+        *reinterpret_cast<uint4 *>(dst_row_base + sw128(r, c)) =
+            make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+}
+
+template <int WT, int BN>
+__global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__ QgemmArgs a)
+{
+    constexpr uint32_t B_BYTES = BN * 128;
+    constexpr uint32_t STAGE = QG_A_BYTES + B_BYTES;
+    constexpr int TCOLS = BN < 32 ? 32 : BN;   // TMEM columns: a power of two >= 32
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + QG_STAGES * STAGE);
+    uint64_t *empty = full + QG_STAGES;
+    uint64_t *done = empty + QG_STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *commits = const_cast<int *>(abort_s) + 1;   // [QG_STAGES] commits issued to each empty barrier
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * QG_M, t0 = blockIdx.y * BN;
+    const int ksteps = a.n / QG_K;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < QG_STAGES; s++) {
+            mbar_init(&full[s], QG_PROD);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *abort_s = 0;
+        for (int s = 0; s < QG_STAGES; s++) commits[s] = 0;
+        fence_barrier_init();
+    }
+    if (warp == 4) {   // TMEM allocation (warp-wide)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TCOLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(QG_M, BN);
+            for (int kb = 0; kb < ksteps; kb++) {
+                const int s = kb % QG_STAGES;
+                const uint32_t ph = (uint32_t)(kb / QG_STAGES) & 1u;
+                bool ok = false;
+                for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+                    if (mbar_try_wait(&full[s], ph)) { ok = true; break; }
+                    if (*abort_s) break;
+                    if (i > 64) __nanosleep(32);
+                }
+                if (!ok) {
+                    if (!*abort_s && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_FULL);
+                    *abort_s = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + QG_A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < QG_K / 16; kk++) {
+                    const uint64_t da = umma_desc_sw128(sa + kk * 32), db = umma_desc_sw128(sb + kk * 32);
+                    const uint32_t acc = (kb | kk) != 0;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\t"
+                        "setp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+                        ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u)
+                        : "memory");
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                             ::"r"(smem_u32(&empty[s])) : "memory");
+                commits[s]++;
+            }
+            // arrives once every MMA issued above has completed (at once if none was)
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"(smem_u32(done)) : "memory");
+        }
+    } else {
+        // ---------------- producers
+        const int p = threadIdx.x;
+        for (int kb = 0; kb < ksteps; kb++) {
+            const int s = kb % QG_STAGES;
+            const uint32_t ph = (uint32_t)(kb / QG_STAGES) & 1u;
+            bool ok = false;
+            for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+                if (mbar_try_wait(&empty[s], ph ^ 1u)) { ok = true; break; }
+                if (*abort_s) break;
+                if (i > 64) __nanosleep(32);
+            }
+            if (!ok) {
+                if (!*abort_s && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_EMPTY);
+                *abort_s = 1;
+                break;
+            }
+            uint8_t *sa = smem + s * STAGE, *sb = sa + QG_A_BYTES;
+            const uint32_t sb_addr = smem_u32(sb);
+            // activation rows: BN rows x 8 chunks of 16 bytes
+            for (int i = p; i < BN * 8; i += QG_PROD) {
+                const int r = i >> 3, c = i & 7, tok = t0 + r;
+                const bool valid = tok < a.T;
+                const __half *src = a.x + (size_t)(valid ? tok : 0) * a.n + (size_t)kb * QG_K + c * 8;
+                cp_async16(sb_addr + sw128(r, c), src, valid);
+            }
+            stage_weight_row<WT>(a, m0 + p, kb, sa, p);
+            cp_async_wait_all();
+            fence_proxy_async_smem();   // generic-proxy writes before the tensor cores read them
+            mbar_arrive(&full[s]);
+        }
+        // ---------------- epilogue: TMEM lanes 32w..32w+31 are rows m0 + 32w + lane
+        bool ok = false;
+        for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+            if (mbar_try_wait(done, 0)) { ok = true; break; }
+            if (i > 64) __nanosleep(32);
+        }
+        if (!ok && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_FULL);
+        tc_fence_after();
+        if (ok && !*abort_s) {
+            const int row = m0 + warp * 32 + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                             "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                               "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+                               "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                             : "r"(taddr + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < a.d) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int tok = t0 + c0 + j;
+                        if (tok < a.T) a.y[(size_t)tok * a.d + row] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
+    }
+    if (threadIdx.x == 0) {
+        // a commit's arrive lands when its MMAs complete: wait for each empty
+        // barrier's last committed phase before retiring the barriers
+        for (int s = 0; s < QG_STAGES; s++)
+            if (commits[s] > 0) mbar_wait_bounded(&empty[s], (uint32_t)(commits[s] - 1) & 1u, nullptr, 0);
+        for (int s = 0; s < QG_STAGES; s++) {
+            mbar_inval(&full[s]);
+            mbar_inval(&empty[s]);
+        }
+        mbar_inval(done);
+    }
+}
+
+__global__ void k_f32_to_f16(const float *__restrict__ x, __half *__restrict__ y, long long n)
+{
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = __float2half_rn(x[i]);
+}
+
+cudaError_t launch_f32_to_f16(const float *x, __half *y, long long n, cudaStream_t st)
+{
+    if (n <= 0) return cudaSuccess;
+    const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 8);
+    k_f32_to_f16<<<grid, 256, 0, st>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+size_t qgemm_smem_bytes(int bn)
+{
+    // alignment slack, stages, barriers, TMEM slot, abort flag, commit counts
+    return 1024 + (size_t)QG_STAGES * (QG_A_BYTES + (size_t)bn * 128) + (2 * QG_STAGES + 1) * 8 + 8 + 4 * QG_STAGES;
+}
+
+template <int WT, int BN>
+static cudaError_t launch_t(const QgemmArgs &a, cudaStream_t st)
+{
+    const size_t smem = qgemm_smem_bytes(BN);
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm<WT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    dim3 grid(cdiv(a.d, QG_M), cdiv(a.T, BN));
+    k_qgemm<WT, BN><<<grid, QG_THREADS, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <int WT>
+static cudaError_t launch_bn(const QgemmArgs &a, cudaStream_t st)
+{
+    if (a.T > 128) return launch_t<WT, 256>(a, st);
+    if (a.T > 64) return launch_t<WT, 128>(a, st);
+    if (a.T > 32) return launch_t<WT, 64>(a, st);
+    if (a.T > 16) return launch_t<WT, 32>(a, st);
+    return launch_t<WT, 16>(a, st);
+}
+
+bool qgemm_supported(const WeightLayout &L)
+{
+    return (L.type == W_Q4_0 || L.type == W_Q8_0) && L.n % QG_K == 0 && L.units % 2 == 0;
+}
+
+cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T, int *err,
+                         cudaStream_t st)
+{
+    if (T <= 0) return cudaSuccess;
+    if (!qgemm_supported(L)) return cudaErrorInvalidValue;
+    QgemmArgs a;
+    a.w = w;
+    a.type = L.type;
+    a.n = L.n;
+    a.d = L.d;
+    a.R = L.R;
+    a.units = L.units;
+    a.nseg = L.nseg;
+    a.full_chunk = L.full_chunk;
+    a.tile_bytes = L.tile_bytes;
+    a.x = x16;
+    a.y = y;
+    a.T = T;
+    a.err = err;
+    return L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, st) : launch_bn<W_Q8_0>(a, st);
+}
+
+} // namespace cats

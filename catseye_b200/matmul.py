@@ -148,3 +148,18 @@ def linear_forward_dev(x, w, z, batch, n_in, n_out, stream=None):
     _lib.check(lib.cats_linear_forward_dev(_dp(x), _dp(w), _dp(z), batch, n_in, n_out, stream),
                "cats_linear_forward_dev")
     return z
+
+
+# ------------------------------------------------ batched product (tensor cores)
+def qgemm(w, x, T, n, d):
+    """y[T][d] = x[T][n] * W^T for a registered Q4_0/Q8_0 weight w (host arrays)."""
+    lib = _lib.init()
+    y = np.empty(T * d, np.float32)
+    _lib.check(lib.cats_gpu_qgemm(_p(w), _p(np.ascontiguousarray(x, np.float32)), _p(y), T), "cats_gpu_qgemm")
+    return y.reshape(T, d)
+
+
+def qgemm_dev(w, x, y, T, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_gpu_qgemm_dev(_p(w), _dp(x), _dp(y), T, stream), "cats_gpu_qgemm_dev")
+    return y

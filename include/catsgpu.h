@@ -95,6 +95,15 @@ void *cats_gpu_dequantize_q8_0(void *y, const void *x, int row, int n);
  * pointer to n floats (x_is_q8 = 0: quantized on the device for quantized
  * types) or to n/32 Q8 blocks (x_is_q8 = 1).  stream: cudaStream_t or NULL. */
 int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q8, void *stream);
+/* Batched product for prefill and batched decode: y[T][d] = x[T][n] * W^T
+ * for a registered Q4_0 or Q8_0 weight (n a multiple of 64), i.e. T calls of
+ * matmul (llm/catseye_llm.h:1531) at once, on the tensor cores: weights are
+ * dequantized and activations rounded to fp16, sums accumulate in fp32
+ * (normwise relative error <= 1e-3 against the exact dequantized product).
+ * The _dev form takes device pointers (d_x 16-byte aligned) and a stream;
+ * cats_gpu_qgemm takes host pointers and returns after the copy back. */
+int cats_gpu_qgemm_dev(const void *w, const float *d_x, float *d_y, int T, void *stream);
+int cats_gpu_qgemm(const void *w, const float *x, float *y, int T);
 /* quantize_q8 on device buffers; scalar_mode selects the plain-C build's
  * rounding (llm/catseye_llm.h:227-251). */
 int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mode, void *stream);

@@ -1,0 +1,86 @@
+"""Batched quantized-weight product on the tensor cores (cats_gpu_qgemm):
+y[T][d] = x[T][n] W^T against the exact product of the oracle's dequantized
+weights, in float64.  fp16 operands with fp32 accumulation: normwise relative
+error <= 1e-3, the bar for the tensor-core paths."""
+import numpy as np
+import pytest
+
+from models import rel
+from oracle.cpu import Q4_0, Q8_0
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def mm(gpu):
+    from catseye_b200 import matmul
+    return matmul
+
+
+def _case(orc, t, n, d, T, seed):
+    rng = np.random.default_rng(seed)
+    w = orc.quantize_rows(t, (rng.standard_normal((d, n)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((T, n)).astype(np.float32)
+    ref = x.astype(np.float64) @ orc.dequantize(t, w, n, d).astype(np.float64).T
+    return w, x, ref
+
+
+# (n, d, T): full 128 x 256 tiles; ragged rows and tokens; a partial last
+# 64-block segment (11008 = 5 x 2048 + 768); the smallest shapes
+SHAPES = [(4096, 4096, 512), (4096, 1000, 16), (11008, 4096, 100), (64, 128, 1), (8192, 256, 300),
+          (2048, 11008, 33), (128, 17, 7)]
+
+
+@pytest.mark.parametrize("t", [Q4_0, Q8_0])
+@pytest.mark.parametrize("n,d,T", SHAPES)
+def test_qgemm_matches_exact_product(mm, orc, t, n, d, T):
+    w, x, ref = _case(orc, t, n, d, T, n * 7 + d * 3 + T)
+    mm.register_weight(w, t, n, d)
+    try:
+        y = mm.qgemm(w, x, T, n, d)
+    finally:
+        mm.unregister_weight(w)
+    assert rel(y, ref) < TOL, rel(y, ref)
+
+
+def test_qgemm_rows_equal_matvecs(mm, orc):
+    """Each token's row of the batched product is the matvec of that token
+    (the matvec quantizes x to Q8 first, so the two agree to ~1e-3)."""
+    n, d, T = 4096, 512, 8
+    w, x, ref = _case(orc, Q4_0, n, d, T, 5)
+    mm.register_weight(w, Q4_0, n, d)
+    try:
+        y = mm.qgemm(w, x, T, n, d)
+        for i in range(T):
+            out = np.zeros(d, np.float32)
+            mm.matmul(Q4_0, out, mm.quantize(x[i]), w, n, d)
+            assert rel(y[i], out) < 2e-2
+    finally:
+        mm.unregister_weight(w)
+
+
+def test_qgemm_device_form(mm, orc):
+    import torch
+    n, d, T = 4096, 384, 64
+    w, x, ref = _case(orc, Q4_0, n, d, T, 9)
+    mm.register_weight(w, Q4_0, n, d)
+    try:
+        dx = torch.from_numpy(x).cuda()
+        dy = torch.empty((T, d), device="cuda")
+        mm.qgemm_dev(w, dx, dy, T)
+        torch.cuda.synchronize()
+        assert rel(dy.cpu().numpy(), ref) < TOL
+    finally:
+        mm.unregister_weight(w)
+
+
+def test_qgemm_refuses_f32_weights(mm):
+    from catseye_b200._lib import CatsGpuError
+    w = np.zeros((16, 64), np.float32)
+    mm.register_weight(w, 0, 64, 16)
+    try:
+        with pytest.raises(CatsGpuError):
+            mm.qgemm(w, np.zeros((2, 64), np.float32), 2, 64, 16)
+    finally:
+        mm.unregister_weight(w)

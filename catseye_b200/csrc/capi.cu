@@ -343,10 +343,8 @@ int cats_gpu_qgemm_dev(const void *w, const float *d_x, float *d_y, int T, void 
     if (!d_x || !d_y || T <= 0 || ((uintptr_t)d_x % 16)) return fail(CATS_ERR_ARG, what);
     if (!qgemm_supported(r.W.L)) return fail(CATS_ERR_UNSUPPORTED, what);
     cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
-    const size_t xb = (size_t)T * r.n * 2;
-    if (grow((void **)&g.d_x16, &g.cap_x16, xb)) return g.last_err;
-    if (check(launch_f32_to_f16(d_x, g.d_x16, (long long)T * r.n, st), what)) return g.last_err;
-    return check(launch_qgemm(r.W.L, r.W.ptr, g.d_x16, d_y, T, g.d_err, st), what);
+    if (grow((void **)&g.d_x16, &g.cap_x16, qgemm_x16_bytes(r.n, T))) return g.last_err;
+    return check(launch_qgemm(r.W.L, r.W.ptr, d_x, g.d_x16, d_y, T, g.d_err, st), what);
 }
 
 int cats_gpu_qgemm(const void *w, const float *x, float *y, int T)

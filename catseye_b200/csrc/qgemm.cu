@@ -29,6 +29,7 @@ namespace cats {
 constexpr int QG_M = 128;
 constexpr int QG_K = 64;
 constexpr int QG_STAGES = 4;
+constexpr int QG_PF = 3;                     // K slices of weight words a producer has in flight
 constexpr int QG_PROD = 128;                 // producer threads (4 warps)
 constexpr int QG_THREADS = QG_PROD + 32;     // + the MMA warp
 constexpr uint32_t QG_A_BYTES = QG_M * 128;  // one stage of weight rows (fp16, 64 per row)
@@ -38,9 +39,9 @@ struct QgemmArgs {
     int type, n, d, R, units, nseg;
     uint32_t full_chunk;
     unsigned long long tile_bytes;
-    const __half *x;                  // [T][n] fp16
+    const __half *x;                  // fp16 activations, [n/64][Tpad][64], rows pre-swizzled
     float *y;                         // [T][d]
-    int T;
+    int T, Tpad;
     int *err;
 };
 
@@ -67,54 +68,96 @@ __device__ __forceinline__ uint32_t sw128(int r, int c)
     return (uint32_t)r * 128 + (uint32_t)((c ^ (r & 7)) * 16);
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid)
+// 1-D bulk copy global -> shared completing on an mbarrier (no L2 hint: the
+// activations are read by every CTA of the column and should stay in L2).
+__device__ __forceinline__ void bulk_g2s_keep(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
 {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
 
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// The raw words of one weight row's two blocks at one K slice.
+struct RawRow {
+    uint4 w[4];     // Q4_0: w[0..1] nibbles of the two blocks; Q8_0: lo0, hi0, lo1, hi1
+    uint32_t sc;    // the two fp16 scales
+};
 
-// Dequantize the two blocks of weight row `row` at K slice kb into 64 fp16,
-// stored swizzled at dst (the row's 128 bytes).
+// Issue the loads of weight row `row`'s two blocks at K slice kb (no use yet,
+// so several slices' loads are in flight while earlier ones are dequantized).
 template <int WT>
-__device__ __forceinline__ void stage_weight_row(const QgemmArgs &a, int row, int kb, uint8_t *dst_row_base, int r)
+__device__ __forceinline__ void fetch_row(const QgemmArgs &a, int row, int kb, RawRow &r)
 {
-    uint32_t h[32];   // 64 fp16, two per word
-    if (row < a.d) {
-        const int u = 2 * kb, s = u / MV_SEG_UNITS, u0 = u % MV_SEG_UNITS;
-        const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
-        const int t = row / a.R, rr = row % a.R;
-        const uint8_t *ch = a.w + (size_t)t * a.tile_bytes + (size_t)s * a.full_chunk;
-        const uint32_t sstride = (uint32_t)round_up((size_t)us * 2, 16);
-        const uint32_t ub = WT == W_Q4_0 ? 16 : 32;
-        const uint32_t sc2 = *reinterpret_cast<const uint32_t *>(ch + (size_t)a.R * us * ub + rr * sstride + u0 * 2);
-        const float d0 = half_bits_to_float((uint16_t)(sc2 & 0xffff)), d1 = half_bits_to_float((uint16_t)(sc2 >> 16));
+    const int u = 2 * kb, s = u / MV_SEG_UNITS, u0 = u % MV_SEG_UNITS;
+    const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
+    const int t = row / a.R, rr = row % a.R;
+    const uint8_t *ch = a.w + (size_t)t * a.tile_bytes + (size_t)s * a.full_chunk;
+    const uint32_t sstride = (uint32_t)round_up((size_t)us * 2, 16);
+    const uint32_t ub = WT == W_Q4_0 ? 16 : 32;
+    r.sc = __ldg(reinterpret_cast<const unsigned int *>(ch + (size_t)a.R * us * ub + rr * sstride + u0 * 2));
+    if (WT == W_Q4_0) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + u0) * 16);
+        r.w[0] = __ldg(p);
+        r.w[1] = __ldg(p + 1);
+    } else {
+        const uint4 *lo = reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2) * us + u0) * 16);
+        const uint4 *hi = reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2 + 1) * us + u0) * 16);
+        r.w[0] = __ldg(lo);
+        r.w[1] = __ldg(hi);
+        r.w[2] = __ldg(lo + 1);
+        r.w[3] = __ldg(hi + 1);
+    }
+}
+
+// Two small non-negative integers (bits 0-10 of each 16-bit half of t) as
+// an fp16 pair: OR-ing them into the mantissa of 1024.0 gives 1024 + v
+// exactly, and subtracting `bias` (1024 + the code offset) leaves the code.
+__device__ __forceinline__ __half2 codes_to_half2(uint32_t t, __half2 bias)
+{
+    const uint32_t u = t | 0x64006400u;
+    return __hsub2(*reinterpret_cast<const __half2 *>(&u), bias);
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
+// Dequantize a fetched row into 64 fp16 stored swizzled as row r of the
+// stage's weight tile (zeros for rows past d).  Value = code * d, the fp16
+// product of two exact fp16 operands, i.e. the correctly rounded q*d.
+template <int WT>
+__device__ __forceinline__ void dequant_row(const RawRow &raw, bool valid, uint8_t *tile, int r)
+{
+    uint32_t h[32];   // 64 fp16, two per word: h[16b + e/2] holds elements e, e+1 of block b
+    if (valid) {
 #pragma unroll
         for (int b = 0; b < 2; b++) {
-            const float dd = b ? d1 : d0;
-            int8_t q[32];
+            const uint16_t sb = (uint16_t)(b ? raw.sc >> 16 : raw.sc & 0xffff);
+            const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
             if (WT == W_Q4_0) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + u0 + b) * 16);
+                // byte j holds element j (low nibble) and element j + 16 (high nibble)
+                const __half2 bias = __float2half2_rn(1032.f);
+                const uint4 w = raw.w[b];
                 const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const uint32_t byte = (wv[j >> 2] >> ((j & 3) * 8)) & 0xff;
-                    q[j] = (int8_t)((int)(byte & 0xf) - 8);      // element j: low nibble
-                    q[j + 16] = (int8_t)((int)(byte >> 4) - 8);  // element j + 16: high nibble
+                for (int i = 0; i < 4; i++) {
+                    const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140);   // bytes 4i, 4i+1 -> the two halves
+                    const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342);   // bytes 4i+2, 4i+3
+                    h[16 * b + 2 * i] = h2u(__hmul2(codes_to_half2(t01 & 0x000F000Fu, bias), d2));
+                    h[16 * b + 2 * i + 1] = h2u(__hmul2(codes_to_half2(t23 & 0x000F000Fu, bias), d2));
+                    h[16 * b + 8 + 2 * i] = h2u(__hmul2(codes_to_half2((t01 >> 4) & 0x000F000Fu, bias), d2));
+                    h[16 * b + 9 + 2 * i] = h2u(__hmul2(codes_to_half2((t23 >> 4) & 0x000F000Fu, bias), d2));
                 }
             } else {
-                const uint4 lo = *reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2) * us + u0 + b) * 16);
-                const uint4 hi = *reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2 + 1) * us + u0 + b) * 16);
+                // int8 codes: flipping the sign bit gives code + 128 in 0..255
+                const __half2 bias = __float2half2_rn(1152.f);
+                const uint4 lo = raw.w[2 * b], hi = raw.w[2 * b + 1];
                 const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
-                for (int j = 0; j < 32; j++) q[j] = (int8_t)((wv[j >> 2] >> ((j & 3) * 8)) & 0xff);
-            }
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const __half lo16 = __float2half_rn((float)q[2 * j] * dd);
-                const __half hi16 = __float2half_rn((float)q[2 * j + 1] * dd);
-                h[b * 16 + j] = (uint32_t)__half_as_ushort(lo16) | ((uint32_t)__half_as_ushort(hi16) << 16);
+                for (int i = 0; i < 8; i++) {
+                    const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140) ^ 0x00800080u;
+                    const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342) ^ 0x00800080u;
+                    h[16 * b + 2 * i] = h2u(__hmul2(codes_to_half2(t01, bias), d2));
+                    h[16 * b + 2 * i + 1] = h2u(__hmul2(codes_to_half2(t23, bias), d2));
+                }
             }
         }
     } else {
@@ -123,8 +166,7 @@ __device__ __forceinline__ void stage_weight_row(const QgemmArgs &a, int row, in
     }
 #pragma unroll
     for (int c = 0; c < 8; c++)
-        *reinterpret_cast<uint4 *>(dst_row_base + sw128(r, c)) =
-            make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+        *reinterpret_cast<uint4 *>(tile + sw128(r, c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
 }
 
 template <int WT, int BN>
@@ -209,34 +251,43 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
         }
     } else {
         // ---------------- producers
-        const int p = threadIdx.x;
-        for (int kb = 0; kb < ksteps; kb++) {
-            const int s = kb % QG_STAGES;
-            const uint32_t ph = (uint32_t)(kb / QG_STAGES) & 1u;
-            bool ok = false;
-            for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
-                if (mbar_try_wait(&empty[s], ph ^ 1u)) { ok = true; break; }
-                if (*abort_s) break;
-                if (i > 64) __nanosleep(32);
+        const int p = threadIdx.x, row = m0 + p;
+        const bool valid = row < a.d;
+        RawRow raw[QG_PF];
+#pragma unroll
+        for (int j = 0; j < QG_PF; j++)
+            if (valid && j < ksteps) fetch_row<WT>(a, row, j, raw[j]);
+        bool stop = false;
+        for (int kb0 = 0; kb0 < ksteps && !stop; kb0 += QG_PF) {
+#pragma unroll
+            for (int j = 0; j < QG_PF; j++) {
+                const int kb = kb0 + j;
+                if (kb >= ksteps || stop) break;
+                const int s = kb % QG_STAGES;
+                const uint32_t ph = (uint32_t)(kb / QG_STAGES) & 1u;
+                bool ok = false;
+                for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+                    if (mbar_try_wait(&empty[s], ph ^ 1u)) { ok = true; break; }
+                    if (*abort_s) break;
+                    if (i > 64) __nanosleep(32);
+                }
+                if (!ok) {
+                    if (!*abort_s && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_EMPTY);
+                    *abort_s = 1;
+                    stop = true;
+                    break;
+                }
+                uint8_t *sa = smem + s * STAGE, *sb = sa + QG_A_BYTES;
+                // the BN activation rows of this K slice: one bulk copy of
+                // pre-swizzled rows (the tensor cores read them through the
+                // async proxy, like the copy writes them)
+                if (p == 0) bulk_g2s_keep(sb, a.x + ((size_t)kb * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
+                dequant_row<WT>(raw[j], valid, sa, p);
+                if (valid && kb + QG_PF < ksteps) fetch_row<WT>(a, row, kb + QG_PF, raw[j]);
+                fence_proxy_async_smem();   // the generic-proxy weight writes, before the tensor cores read them
+                if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
+                else mbar_arrive(&full[s]);
             }
-            if (!ok) {
-                if (!*abort_s && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_EMPTY);
-                *abort_s = 1;
-                break;
-            }
-            uint8_t *sa = smem + s * STAGE, *sb = sa + QG_A_BYTES;
-            const uint32_t sb_addr = smem_u32(sb);
-            // activation rows: BN rows x 8 chunks of 16 bytes
-            for (int i = p; i < BN * 8; i += QG_PROD) {
-                const int r = i >> 3, c = i & 7, tok = t0 + r;
-                const bool valid = tok < a.T;
-                const __half *src = a.x + (size_t)(valid ? tok : 0) * a.n + (size_t)kb * QG_K + c * 8;
-                cp_async16(sb_addr + sw128(r, c), src, valid);
-            }
-            stage_weight_row<WT>(a, m0 + p, kb, sa, p);
-            cp_async_wait_all();
-            fence_proxy_async_smem();   // generic-proxy writes before the tensor cores read them
-            mbar_arrive(&full[s]);
         }
         // ---------------- epilogue: TMEM lanes 32w..32w+31 are rows m0 + 32w + lane
         bool ok = false;
@@ -288,18 +339,40 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     }
 }
 
-__global__ void k_f32_to_f16(const float *__restrict__ x, __half *__restrict__ y, long long n)
+// x[T][n] fp32 -> fp16 in the order the kernel's bulk copies take: K slice
+// major ([n/64][Tpad][64]), each row's eight 16-byte chunks permuted as the
+// 128-byte swizzle places them (chunk c of token t at c ^ (t & 7); a CTA's
+// first token is a multiple of 8), zeros for tokens t >= T.
+__global__ void k_x16_swizzled(const float *__restrict__ x, __half *__restrict__ y, int T, int Tpad, int n)
 {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        y[i] = __float2half_rn(x[i]);
+    const long long total = (long long)(n / QG_K) * Tpad * 8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(i & 7);
+        const long long r = i >> 3;
+        const int tok = (int)(r % Tpad), kb = (int)(r / Tpad);
+        uint32_t h[4] = {0u, 0u, 0u, 0u};
+        if (tok < T) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)tok * n + (size_t)kb * QG_K + c * 8);
+            const float4 v0 = src[0], v1 = src[1];
+            const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                h[j] = (uint32_t)__half_as_ushort(__float2half_rn(f[2 * j])) |
+                       ((uint32_t)__half_as_ushort(__float2half_rn(f[2 * j + 1])) << 16);
+        }
+        *reinterpret_cast<uint4 *>(y + (r * 8 + (c ^ (tok & 7))) * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
 }
 
-cudaError_t launch_f32_to_f16(const float *x, __half *y, long long n, cudaStream_t st)
+static int pick_bn(int T)
 {
-    if (n <= 0) return cudaSuccess;
-    const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 8);
-    k_f32_to_f16<<<grid, 256, 0, st>>>(x, y, n);
-    return cudaGetLastError();
+    return T > 128 ? 256 : T > 64 ? 128 : T > 32 ? 64 : T > 16 ? 32 : 16;
+}
+
+size_t qgemm_x16_bytes(int n, int T)
+{
+    return (size_t)n * round_up((size_t)T, (size_t)pick_bn(T)) * 2;
 }
 
 size_t qgemm_smem_bytes(int bn)
@@ -320,13 +393,15 @@ static cudaError_t launch_t(const QgemmArgs &a, cudaStream_t st)
 }
 
 template <int WT>
-static cudaError_t launch_bn(const QgemmArgs &a, cudaStream_t st)
+static cudaError_t launch_bn(const QgemmArgs &a, int bn, cudaStream_t st)
 {
-    if (a.T > 128) return launch_t<WT, 256>(a, st);
-    if (a.T > 64) return launch_t<WT, 128>(a, st);
-    if (a.T > 32) return launch_t<WT, 64>(a, st);
-    if (a.T > 16) return launch_t<WT, 32>(a, st);
-    return launch_t<WT, 16>(a, st);
+    switch (bn) {
+    case 256: return launch_t<WT, 256>(a, st);
+    case 128: return launch_t<WT, 128>(a, st);
+    case 64: return launch_t<WT, 64>(a, st);
+    case 32: return launch_t<WT, 32>(a, st);
+    default: return launch_t<WT, 16>(a, st);
+    }
 }
 
 bool qgemm_supported(const WeightLayout &L)
@@ -334,11 +409,16 @@ bool qgemm_supported(const WeightLayout &L)
     return (L.type == W_Q4_0 || L.type == W_Q8_0) && L.n % QG_K == 0 && L.units % 2 == 0;
 }
 
-cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T, int *err,
-                         cudaStream_t st)
+cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
+                         int *err, cudaStream_t st)
 {
     if (T <= 0) return cudaSuccess;
     if (!qgemm_supported(L)) return cudaErrorInvalidValue;
+    const int bn = pick_bn(T), Tpad = (int)round_up((size_t)T, (size_t)bn);
+    const long long chunks = (long long)(L.n / QG_K) * Tpad * 8;
+    k_x16_swizzled<<<(int)std::min<long long>((chunks + 255) / 256, 148LL * 16), 256, 0, st>>>(x, x16, T, Tpad, L.n);
+    cudaError_t e = cudaGetLastError();
+    if (e) return e;
     QgemmArgs a;
     a.w = w;
     a.type = L.type;
@@ -352,8 +432,9 @@ cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const __half *
     a.x = x16;
     a.y = y;
     a.T = T;
+    a.Tpad = Tpad;
     a.err = err;
-    return L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, st) : launch_bn<W_Q8_0>(a, st);
+    return L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
 }
 
 } // namespace cats

@@ -338,6 +338,24 @@ void oracle_matmul_q4_0_f32(float *xout, const float *x, const uint8_t *w, int n
     }
 }
 
+/* Q8_0 weights times fp32 activations: value = q*d (GGUF Q8_0 block), the
+ * f32-activation form of matmul_q4_0 (llm/catseye_llm.h:880-914) for Q8_0. */
+void oracle_matmul_q8_0_f32(float *xout, const float *x, const uint8_t *w, int n, int d)
+{
+    const int nb = n / 32;
+    #pragma omp parallel for schedule(static)
+    for (int i = 0; i < d; i++) {
+        const uint8_t *r = w + (size_t)i * nb * 34;
+        float wr[32];
+        double s = 0;
+        for (int b = 0; b < nb; b++) {
+            deq_q8_0(wr, r + b * 34, 32);
+            for (int j = 0; j < 32; j++) s += (double)wr[j] * x[b * 32 + j];
+        }
+        xout[i] = (float)s;
+    }
+}
+
 /* dot_q3_K_q8_K / dot_q6_K_q8_K (llm/catseye_llm.h:1200-1259, 1467-1511):
  * per super-block, sum over 16-element groups of scale*int dot, times d_w*d_x. */
 static void matmul_kquant(int type, float *xout, const int8_t *xq, const uint8_t *w, int n, int d)
@@ -384,6 +402,11 @@ static void matmul_q8mode(int type, int q8_mode, float *xout, const float *x, co
         oracle_quantize_q8_K(q, x, n);
         matmul_kquant(type, xout, q, (const uint8_t *)w, n, d);
         free(q);
+        return;
+    }
+    if (q8_mode == 2) {   /* fp32 activations: matmul_q4_0 (:880-914) and its Q8_0 counterpart */
+        if (type == OR_Q4_0) oracle_matmul_q4_0_f32(xout, x, (const uint8_t *)w, n, d);
+        else                 oracle_matmul_q8_0_f32(xout, x, (const uint8_t *)w, n, d);
         return;
     }
     int8_t *q = (int8_t *)malloc((size_t)(n / 32) * 36);

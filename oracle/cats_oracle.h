@@ -56,6 +56,7 @@ void oracle_matmul_f32(float *xout, const float *x, const float *w, int n, int d
 void oracle_matmul_q4_0_q8(float *xout, const int8_t *xq, const uint8_t *w, int n, int d);
 void oracle_matmul_q8_0_q8(float *xout, const int8_t *xq, const uint8_t *w, int n, int d);
 void oracle_matmul_q4_0_f32(float *xout, const float *x, const uint8_t *w, int n, int d);
+void oracle_matmul_q8_0_f32(float *xout, const float *x, const uint8_t *w, int n, int d);
 void oracle_matmul_q3_K_q8_K(float *xout, const int8_t *xq, const uint8_t *w, int n, int d);
 void oracle_matmul_q6_K_q8_K(float *xout, const int8_t *xq, const uint8_t *w, int n, int d);
 /* generic: quantizes x with the type's activation quantizer first (copy, not in place) */
@@ -83,7 +84,8 @@ void oracle_linear_forward(const float *x, const float *w, float *z, int batch, 
 typedef struct {
     int dim, hidden, n_layers, n_heads, n_kv_heads, vocab, seq_len;
     int wtype;          /* type of wq..w3 and of the classifier */
-    int q8_mode;        /* 0: AVX quantizer rounding, 1: scalar build rounding */
+    int q8_mode;        /* 0: AVX quantizer rounding, 1: scalar build rounding,
+                           2: fp32 activations (matmul_q4_0, :880-914; no quantize_q8) */
     const float *emb;   /* [vocab][dim] fp32 */
     const float *rms_att, *rms_ffn, *rms_final;
     const void *wq, *wk, *wv, *wo, *w1, *w2, *w3, *wcls;

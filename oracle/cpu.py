@@ -171,6 +171,8 @@ class Oracle:
 
     # --- decode step ----------------------------------------------------------
     def llm(self, model, q8_mode=0):
+        """q8_mode 0/1: quantize_q8 with the AVX / plain-C rounding before each
+        quantized matmul; 2: fp32 activations (matmul_q4_0 and its Q8_0 form)."""
         return OracleLLM(self, model, q8_mode)
 
 
@@ -228,6 +230,8 @@ class Reference:
             L.ref_llm_step.restype = _fp
             L.ref_llm_step.argtypes = [_vp, C.c_int, C.c_int]
             L.ref_llm_destroy.argtypes = [_vp]
+            if hasattr(L, "ref_llm_use_f32_activations"):   # AVX builds only (matmul_q4_0)
+                L.ref_llm_use_f32_activations.argtypes = [_vp]
         else:
             L.ref_sgemm.argtypes = [C.c_char, C.c_char, C.c_int, C.c_int, C.c_int, C.c_float,
                                     _vp, _vp, C.c_float, _vp]
@@ -299,14 +303,15 @@ class Reference:
                                     _ptr(z), batch, n_in, n_out)
         return z
 
-    def llm(self, mw):
-        return RefLLM(self, mw)
+    def llm(self, mw, f32_act=False):
+        return RefLLM(self, mw, f32_act)
 
 
 class RefLLM:
-    """cats_llama2_transformer itself, on a model bound to the given weight blobs."""
+    """cats_llama2_transformer itself, on a model bound to the given weight blobs.
+    f32_act: Q4_0 tensors bound to matmul_q4_0 with quantize_null (fp32 activations)."""
 
-    def __init__(self, ref, mw):
+    def __init__(self, ref, mw, f32_act=False):
         c = mw.cfg
         self.ref, self.mw = ref, mw
         # the reference's AVX matvecs use aligned loads: give it 256-byte aligned copies
@@ -316,6 +321,10 @@ class RefLLM:
                                         c.seq_len, c.wtype, *[_ptr(b) for b in self._blobs])
         if not self.h:
             raise ValueError(f"reference has no matmul for weight type {c.wtype}")
+        if f32_act:
+            if not hasattr(ref.lib, "ref_llm_use_f32_activations"):
+                raise ValueError("this reference build has no matmul_q4_0 (AVX builds only)")
+            ref.lib.ref_llm_use_f32_activations(self.h)
 
     def step(self, token, pos):
         p = self.ref.lib.ref_llm_step(self.h, token, pos)

@@ -124,6 +124,27 @@ float *ref_llm_step(void *h, int token, int pos)
     return cats_llama2_transformer(token, pos, &r->m);
 }
 
+#ifdef __AVX__
+/* Rebind the Q4_0 tensors to the reference's fp32-activation matmul:
+ * matmul_q4_0 (llm/catseye_llm.h:880-914) with quantize_null (:2593-2595),
+ * the binding a runtime selects to skip quantize_q8.  Returns the number of
+ * tensors rebound. */
+int ref_llm_use_f32_activations(void *h)
+{
+    ref_model *r = h;
+    int k = 0;
+    for (int i = 0; i < (int)(sizeof(r->m.tensor) / sizeof(r->m.tensor[0])); i++) {
+        cats_tensor *t = &r->m.tensor[i];
+        if (t->data && t->type == GGML_TYPE_Q4_0) {
+            t->matmul = matmul_q4_0;
+            t->quantize = gguf_quantize[GGML_TYPE_F32];
+            k++;
+        }
+    }
+    return k;
+}
+#endif
+
 void ref_llm_destroy(void *h)
 {
     ref_model *r = h;

@@ -105,11 +105,13 @@ def cnn(rc, rng):
 TINY = LlmConfig(dim=64, hidden=96, n_layers=2, n_heads=4, n_kv_heads=2, vocab=128, seq_len=32)
 
 
-def llm(ref, orc, t, name):
+def llm(ref, orc, t, name, f32_act=False):
+    """f32_act: the Q4_0 tensors bound to matmul_q4_0 with quantize_null
+    (fp32 activations), the reference's counterpart of the batched path."""
     cfg = TINY.with_type(t)
     mw = ModelWeights(cfg, 7, orc)
     toks = prompt(7, 4, cfg.vocab)
-    m = ref.llm(mw)
+    m = ref.llm(mw, f32_act)
     logits, nxt, fed = [], [], []
     for pos in range(12):
         tok = int(toks[pos]) if pos < len(toks) else nxt[-1]   # prompt forcing, then greedy
@@ -125,20 +127,28 @@ def llm(ref, orc, t, name):
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
 
 
-def main():
+def main(only=None):
+    """Writes every fixture, or only the named ones (argv)."""
     rng = np.random.default_rng(20240601)
     orc = Oracle()
     ref, refs, rc = Reference("llm"), Reference("llm_scalar"), Reference("cnn")
     assert ref.is_avx() and not refs.is_avx()
-    quant(ref, refs, orc, rng)
-    matvec(ref, refs, orc, rng)
-    cnn(rc, rng)
-    llm(ref, orc, F32, "llm_f32")
-    llm(ref, orc, Q4_0, "llm_q4_0")
+    want = (lambda n: not only or n in only)
+    # quant, matvec and cnn draw from one stream in this order
+    if want("quant") or want("matvec") or want("cnn"):
+        quant(ref, refs, orc, rng)
+        matvec(ref, refs, orc, rng)
+        cnn(rc, rng)
+    if want("llm_f32"):
+        llm(ref, orc, F32, "llm_f32")
+    if want("llm_q4_0"):
+        llm(ref, orc, Q4_0, "llm_q4_0")
+    if want("llm_q4_0_f32act"):
+        llm(ref, orc, Q4_0, "llm_q4_0_f32act", f32_act=True)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

@@ -104,6 +104,20 @@ def test_llm_decode_golden(orc, name, tol):
         assert orc.argmax(lg) == g["argmax"][pos]
 
 
+def test_llm_decode_f32_activations_golden(orc):
+    """The oracle's fp32-activation mode (q8_mode=2) against the reference's
+    Q4_0 tensors bound to matmul_q4_0 + quantize_null."""
+    g = load("llm_q4_0_f32act")
+    mw = _MW(g)
+    m = orc.llm(mw, q8_mode=2)
+    for pos, tok in enumerate(g["fed"]):
+        lg = m.step(int(tok), pos)
+        assert rel(lg, g["logits"][pos]) < 1e-5, pos
+        assert orc.argmax(lg) == g["argmax"][pos]
+    # and it is a different binding from the requantizing one
+    assert rel(g["logits"], load("llm_q4_0")["logits"]) > 1e-4
+
+
 def test_live_against_reference(orc, ref_llm):
     rng = np.random.default_rng(5)
     for n in (32, 4096, 11008):

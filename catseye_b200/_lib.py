@@ -49,6 +49,11 @@ SIGNATURES = {
     "cats_gpu_llama2_transformer": (_vp, [_i, _i, _vp, _vp]),
     "cats_gpu_llm_generate": (_i, [_vp, _i, _i, _i, _vp]),
     "cats_gpu_llm_enqueue": (_i, [_vp, _i]),
+    "cats_gpu_llm_batch_reserve": (_i, [_vp, _i, _i]),
+    "cats_gpu_llm_forward_batch": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp]),
+    "cats_gpu_llm_generate_batch": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+    "cats_gpu_llm_batch_set": (_i, [_vp, _vp, _vp, _vp, _i]),
+    "cats_gpu_llm_batch_enqueue": (_i, [_vp]),
     "cats_gpu_llm_set_engine": (_i, [_vp, _i]),
     "cats_gpu_tp_unique_id_bytes": (_sz, []),
     "cats_gpu_tp_unique_id": (_i, [_vp, _sz]),

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <vector>
 #include <mutex>
 #include <unordered_map>
 
@@ -386,6 +387,7 @@ struct cats_gpu_llm {
     LlmModel m;
     int engine = CATS_ENGINE_PERSISTENT;
     int *tok_log = nullptr;   // device: argmax ids of generate()
+    int bt_T = 0, bt_nb = 0;  // the batch set last (cats_gpu_llm_batch_set)
 };
 
 cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg)
@@ -563,6 +565,82 @@ int cats_gpu_llm_generate(cats_gpu_llm *h, int token, int pos, int steps, int *t
         check(cudaMemcpyAsync(tokens_host, h->tok_log, (size_t)steps * 4, cudaMemcpyDeviceToHost, m.stream), "generate"))
         return g.last_err;
     return cats_gpu_llm_synchronize(h);
+}
+
+// ---------------------------------------------------- batched step (batch.cu)
+static int batch_ready(cats_gpu_llm *h, const char *what)
+{
+    if (!h->m.weights_ready) return fail(CATS_ERR_ARG, what);
+    if (!batch_supported(&h->m)) return fail(CATS_ERR_UNSUPPORTED, what);
+    if (h->m.bt_cap == 0) return fail(CATS_ERR_ARG, what);   // cats_gpu_llm_batch_reserve first
+    if (h->m.c.tp_size > 1 && !h->m.comm_ctx) return fail(CATS_ERR_ARG, what);
+    return CATS_OK;
+}
+
+static int device_status(cats_gpu_llm *h, const char *what)
+{
+    int e = 0;
+    if (cudaMemcpy(&e, h->m.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return fail(CATS_ERR_CUDA, what);
+    if (e) {
+        cudaMemset(h->m.err, 0, 4);
+        return fail(CATS_ERR_TIMEOUT, what);
+    }
+    return CATS_OK;
+}
+
+int cats_gpu_llm_batch_reserve(cats_gpu_llm *h, int max_tokens, int n_seqs)
+{
+    const char *what = "cats_gpu_llm_batch_reserve";
+    if (!h || max_tokens <= 0 || n_seqs <= 0) return fail(CATS_ERR_ARG, what);
+    int rc = llm_batch_reserve(&h->m, max_tokens, n_seqs);
+    return rc ? fail(rc, what) : CATS_OK;
+}
+
+int cats_gpu_llm_batch_set(cats_gpu_llm *h, const int *tokens, const int *pos, const int *seqs, int T)
+{
+    const char *what = "cats_gpu_llm_batch_set";
+    if (!h) return fail(CATS_ERR_ARG, what);
+    if (int rc = batch_ready(h, what)) return rc;
+    int nb = 0;
+    if (int rc = llm_batch_set(&h->m, tokens, pos, seqs, T, &nb)) return fail(rc, what);
+    h->bt_T = T;
+    h->bt_nb = nb;
+    return CATS_OK;
+}
+
+int cats_gpu_llm_batch_enqueue(cats_gpu_llm *h)
+{
+    const char *what = "cats_gpu_llm_batch_enqueue";
+    if (!h || h->bt_T <= 0) return fail(CATS_ERR_ARG, what);
+    return check(llm_batch_enqueue(&h->m, h->bt_T, h->bt_nb, false, nullptr, 0), what);
+}
+
+int cats_gpu_llm_forward_batch(cats_gpu_llm *h, const int *tokens, const int *pos, const int *seqs, int T,
+                               int *next_host, float *logits_host)
+{
+    const char *what = "cats_gpu_llm_forward_batch";
+    if (!h) return fail(CATS_ERR_ARG, what);
+    if (int rc = batch_ready(h, what)) return rc;
+    if (int rc = llm_forward_batch(&h->m, tokens, pos, seqs, T, next_host, logits_host)) return fail(rc, what);
+    h->bt_T = 0;
+    return device_status(h, what);
+}
+
+int cats_gpu_llm_generate_batch(cats_gpu_llm *h, const int *tokens, const int *pos, int n, int steps,
+                                int *tokens_host)
+{
+    const char *what = "cats_gpu_llm_generate_batch";
+    if (!h || !tokens || !pos || n <= 0 || steps < 0 || n > h->m.n_seqs) return fail(CATS_ERR_ARG, what);
+    if (int rc = batch_ready(h, what)) return rc;
+    for (int i = 0; i < n; i++)
+        if (pos[i] < 0 || pos[i] + steps > h->m.c.seq_len) return fail(CATS_ERR_ARG, what);
+    std::vector<int> seqs(n);
+    for (int i = 0; i < n; i++) seqs[i] = i;
+    int nb = 0;
+    if (int rc = llm_batch_set(&h->m, tokens, pos, seqs.data(), n, &nb)) return fail(rc, what);
+    h->bt_T = 0;
+    if (int rc = llm_generate_batch(&h->m, n, steps, tokens_host)) return fail(rc, what);
+    return device_status(h, what);
 }
 
 int cats_gpu_llm_synchronize(cats_gpu_llm *h)

@@ -325,7 +325,8 @@ void llm_free(LlmModel *m)
     if (m->graph) cudaGraphDestroy(m->graph);
     m->exec = nullptr;
     m->graph = nullptr;
-    tp_release(m);   // after the graph that holds its NCCL calls
+    llm_batch_free(m);
+    tp_release(m);   // after the graphs that hold its NCCL calls
     for (auto &w : m->qkv) free_w(w);
     for (auto &w : m->wo) free_w(w);
     for (auto &w : m->w13) free_w(w);

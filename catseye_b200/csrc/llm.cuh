@@ -1,6 +1,7 @@
 // llm.cuh — device-resident llama decode step built on the matvec kernel.
 #pragma once
 #include "matvec.cuh"
+#include <cuda_fp16.h>
 #include <vector>
 
 namespace cats {
@@ -21,6 +22,11 @@ struct StepParams {
     int pos;       // position of this step
     int next;      // greedy argmax of the step's logits (written by the advance kernel)
     int steps;     // number of advance() calls (diagnostics)
+};
+
+// one token of a batched step (batch.cu): input token, position, KV sequence
+struct BatchTok {
+    int token, pos, seq, pad;
 };
 
 typedef void (*AllreduceFn)(void *ctx, float *buf, size_t count, cudaStream_t st);
@@ -58,6 +64,24 @@ struct LlmModel {
     unsigned int *dec_bar = nullptr;      // [0] grid barrier counter, [1] abort flag
     int dec_stages = 0, dec_max_splits = 32;
     uint32_t dec_slot = 0, dec_xs = 0;
+    // batched step (batch.cu): prefill and batched decode on the tensor cores
+    int n_seqs = 1;                       // KV sequences: kcache is [seq][layer][seq_len][kv_dim]
+    int bt_cap = 0;                       // tokens per batched step (0: not reserved)
+    BatchTok *bt_tok = nullptr;           // device [cap]
+    int2 *bt_blocks = nullptr;            // device [cap]: attention query blocks (first token, count)
+    float *bt_x = nullptr, *bt_delta = nullptr, *bt_y = nullptr, *bt_q = nullptr, *bt_xb = nullptr;
+    float *bt_lg = nullptr;               // classifier slices [tp][T][vocab_loc]
+    float *bt_logits = nullptr;           // [T][vocab]
+    __half *bt_x16 = nullptr;             // the fp16 operand of the products
+    int *bt_next = nullptr;               // [T] greedy argmax
+    int *bt_step = nullptr;               // generate loop: steps taken
+    int *bt_log = nullptr;                // generate loop: [steps][T] token ids
+    int bt_log_cap = 0;
+    BatchTok *bt_tok_host = nullptr;      // pinned staging
+    int2 *bt_blocks_host = nullptr;
+    cudaGraph_t bt_graph = nullptr;
+    cudaGraphExec_t bt_exec = nullptr;
+    int bt_graph_T = 0;
     // tensor parallel hooks (NCCL, tp.cu), null when tp_size == 1
     AllreduceFn allreduce = nullptr;
     ArgmaxReduceFn argmax_reduce = nullptr;
@@ -97,6 +121,26 @@ int decode_prepare(LlmModel *m);
 // in the decode step but storing into scratch.  Outputs the mean device time
 // per launch (CUDA events) and the algorithmic bytes per launch.
 cudaError_t llm_time_matvec(LlmModel *m, int kind, int reps, float *ms_per_launch, double *bytes_per_launch);
+
+// Batched step (batch.cu).  Models of Q4_0/Q8_0 weights whose products the
+// tensor-core path takes (batch_supported).  llm_batch_reserve allocates
+// room for `cap` tokens per step and `n_seqs` KV sequences (sequence 0 is the
+// one the decode engines use; a larger count reallocates the cache, keeping
+// the sequences already there).  llm_batch_set validates and uploads T
+// tokens (seqs may be null: all sequence 0); llm_batch_enqueue runs one step
+// on the model's stream (advance: every token's argmax becomes its next input
+// at pos + 1, logged into log[step][T]); llm_forward_batch is set + enqueue +
+// the argmax ids (and logits [T][vocab]) copied back; llm_generate_batch
+// replays a captured step `steps` times after llm_batch_set of one token per
+// sequence.
+bool batch_supported(const LlmModel *m);
+int llm_batch_reserve(LlmModel *m, int cap, int n_seqs);
+void llm_batch_free(LlmModel *m);
+int llm_batch_set(LlmModel *m, const int *tokens, const int *pos, const int *seqs, int T, int *nblocks);
+cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int *log, int log_cap);
+int llm_forward_batch(LlmModel *m, const int *tokens, const int *pos, const int *seqs, int T, int *next_host,
+                      float *logits_host);
+int llm_generate_batch(LlmModel *m, int T, int steps, int *tokens_host);
 
 // generate one synthetic tensor in the reference's GGUF layout (device dst)
 cudaError_t synth_tensor(uint8_t *dst, int type, int n, int d, unsigned long long seed, int tensor_id,

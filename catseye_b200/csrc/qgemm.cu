@@ -11,15 +11,18 @@
 // slices of 64 (two 32-element blocks).
 //  * Producers (warps 0-3, one weight row per thread): read the row's two
 //    blocks from the weight's tile layout (the matvec's, so prefill and decode
-//    share one copy of the weights in HBM), dequantize to fp16 and store the
-//    row in the K-major 128-byte-swizzled form UMMA reads; copy the BN
-//    activation rows (fp16, converted once per call) with cp.async into the
-//    same form; then fence.proxy.async and arrive on the stage's full barrier.
+//    share one copy of the weights in HBM) three K slices ahead, dequantize to
+//    fp16 and store the row in the K-major 128-byte-swizzled form UMMA reads.
+//    Thread 0 also brings the stage's BN activation rows in with one bulk
+//    copy: the fp16 operand is stored K-slice-major and pre-swizzled
+//    (k_x16_swizzled, or a producing kernel writing x16_index order).  Then
+//    fence.proxy.async and an arrive on the stage's full barrier.
 //  * MMA warp (warp 4, one thread): four K=16 tcgen05.mma per stage into the
 //    TMEM accumulator; tcgen05.commit releases the stage when they complete.
 //  * Epilogue: after a final commit, warp w reads TMEM lanes 32w..32w+31 (its
-//    weight rows) 16 columns at a time and writes Y (consecutive lanes are
-//    consecutive rows of Y: coalesced).
+//    weight rows) 16 columns at a time and writes Y, or adds to it
+//    (accumulate: the residual stream), consecutive lanes being consecutive
+//    rows of Y (coalesced).
 // Every wait is bounded; TMEM is freed on every path.
 #include "qgemm.cuh"
 #include <algorithm>
@@ -42,6 +45,7 @@ struct QgemmArgs {
     const __half *x;                  // fp16 activations, [n/64][Tpad][64], rows pre-swizzled
     float *y;                         // [T][d]
     int T, Tpad;
+    int accumulate;                   // y += product instead of y = product
     int *err;
 };
 
@@ -314,7 +318,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int tok = t0 + c0 + j;
-                        if (tok < a.T) a.y[(size_t)tok * a.d + row] = __uint_as_float(v[j]);
+                        if (tok < a.T) {
+                            float *yp = a.y + (size_t)tok * a.d + row;
+                            *yp = a.accumulate ? *yp + __uint_as_float(v[j]) : __uint_as_float(v[j]);
+                        }
                     }
                 }
             }
@@ -370,9 +377,14 @@ static int pick_bn(int T)
     return T > 128 ? 256 : T > 64 ? 128 : T > 32 ? 64 : T > 16 ? 32 : 16;
 }
 
+int qgemm_tpad(int T)
+{
+    return (int)round_up((size_t)std::max(T, 1), (size_t)pick_bn(T));
+}
+
 size_t qgemm_x16_bytes(int n, int T)
 {
-    return (size_t)n * round_up((size_t)T, (size_t)pick_bn(T)) * 2;
+    return (size_t)n * qgemm_tpad(T) * 2;
 }
 
 size_t qgemm_smem_bytes(int bn)
@@ -409,16 +421,21 @@ bool qgemm_supported(const WeightLayout &L)
     return (L.type == W_Q4_0 || L.type == W_Q8_0) && L.n % QG_K == 0 && L.units % 2 == 0;
 }
 
-cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
-                         int *err, cudaStream_t st)
+cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t st)
+{
+    if (T <= 0) return cudaSuccess;
+    if (n % QG_K) return cudaErrorInvalidValue;
+    const int Tpad = qgemm_tpad(T);
+    const long long chunks = (long long)(n / QG_K) * Tpad * 8;
+    k_x16_swizzled<<<(int)std::min<long long>((chunks + 255) / 256, 148LL * 16), 256, 0, st>>>(x, x16, T, Tpad, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
+                             bool accumulate, int *err, cudaStream_t st)
 {
     if (T <= 0) return cudaSuccess;
     if (!qgemm_supported(L)) return cudaErrorInvalidValue;
-    const int bn = pick_bn(T), Tpad = (int)round_up((size_t)T, (size_t)bn);
-    const long long chunks = (long long)(L.n / QG_K) * Tpad * 8;
-    k_x16_swizzled<<<(int)std::min<long long>((chunks + 255) / 256, 148LL * 16), 256, 0, st>>>(x, x16, T, Tpad, L.n);
-    cudaError_t e = cudaGetLastError();
-    if (e) return e;
     QgemmArgs a;
     a.w = w;
     a.type = L.type;
@@ -432,9 +449,21 @@ cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x
     a.x = x16;
     a.y = y;
     a.T = T;
-    a.Tpad = Tpad;
+    a.Tpad = qgemm_tpad(T);
+    a.accumulate = accumulate ? 1 : 0;
     a.err = err;
+    const int bn = pick_bn(T);
     return L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
+}
+
+cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
+                         int *err, cudaStream_t st)
+{
+    if (T <= 0) return cudaSuccess;
+    if (!qgemm_supported(L)) return cudaErrorInvalidValue;
+    cudaError_t e = launch_x16(x, x16, T, L.n, st);
+    if (e) return e;
+    return launch_qgemm_x16(L, w, x16, y, T, false, err, st);
 }
 
 } // namespace cats

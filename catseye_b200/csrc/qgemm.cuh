@@ -8,11 +8,31 @@ namespace cats {
 // Weights qgemm handles: Q4_0 / Q8_0 in the tile layout, n a multiple of 64.
 bool qgemm_supported(const WeightLayout &L);
 
-// Bytes of the fp16 activation scratch launch_qgemm needs for T tokens.
+// Token rows the fp16 operand holds for T tokens (T rounded up to the CTA's
+// token tile), and the bytes of that operand for n columns.
+int qgemm_tpad(int T);
 size_t qgemm_x16_bytes(int n, int T);
 
-// Y[T][d] = X[T][n] * W[d][n]^T with fp16 operands and fp32 accumulation.
-// x (fp32, 16-byte aligned) is converted into x16 (qgemm_x16_bytes) first.
+// The fp16 operand ("x16"): K-slice-major [n/64][Tpad][64], 16-byte chunk c
+// of token t's slice stored at chunk c ^ (t & 7) (the 128-byte swizzle the
+// tensor cores read, so one bulk copy brings a stage in).  Element k of token
+// t sits at x16_index(k, t, Tpad).  Rows t >= T are never stored from: their
+// contents only reach output columns that are not written.
+__host__ __device__ inline size_t x16_index(int k, int t, int Tpad)
+{
+    const int kb = k >> 6, c = (k >> 3) & 7;
+    return (((size_t)kb * Tpad + t) * 8 + (size_t)(c ^ (t & 7))) * 8 + (k & 7);
+}
+
+// x[T][n] fp32 (16-byte aligned rows) -> x16.
+cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t st);
+
+// Y[T][d] (=, or += when accumulate) X[T][n] * W[d][n]^T with fp16 operands
+// and fp32 accumulation, X given as x16.
+cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
+                             bool accumulate, int *err, cudaStream_t st);
+
+// The same from fp32 x (converted into the x16 scratch, qgemm_x16_bytes, first).
 cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
                          int *err, cudaStream_t st);
 

@@ -97,6 +97,56 @@ class GpuLLM:
         _lib.check(self.lib.cats_gpu_llm_generate(self.h, token, pos, steps, C.c_void_p(toks.ctypes.data)), "generate")
         return toks[:steps]
 
+    # ---- batched step on the tensor cores (prefill, batched decode)
+    def batch_reserve(self, max_tokens, n_seqs=1):
+        """Room for max_tokens per batched step and n_seqs KV sequences."""
+        _lib.check(self.lib.cats_gpu_llm_batch_reserve(self.h, max_tokens, n_seqs), "batch_reserve")
+
+    def forward_batch(self, tokens, pos, seqs=None, logits=False):
+        """T tokens through the model at once (token t at pos[t] of sequence
+        seqs[t]); returns the greedy argmax per token, and the [T][vocab]
+        logits when asked."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        T = tokens.size
+        sp = None
+        if seqs is not None:
+            seqs = np.ascontiguousarray(seqs, np.int32)
+            sp = C.c_void_p(seqs.ctypes.data)
+        nxt = np.zeros(T, np.int32)
+        lg = np.zeros((T, self.cfg.vocab), np.float32) if logits else None
+        _lib.check(self.lib.cats_gpu_llm_forward_batch(
+            self.h, C.c_void_p(tokens.ctypes.data), C.c_void_p(pos.ctypes.data), sp, T,
+            C.c_void_p(nxt.ctypes.data), C.c_void_p(lg.ctypes.data) if logits else None), "forward_batch")
+        return (nxt, lg) if logits else nxt
+
+    def generate_batch(self, tokens, pos, steps):
+        """Greedy decoding of len(tokens) sequences (sequence i from tokens[i]
+        at pos[i]), one token of each per step; returns [steps][n] ids."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        n = tokens.size
+        out = np.zeros((max(steps, 1), n), np.int32)
+        _lib.check(self.lib.cats_gpu_llm_generate_batch(self.h, C.c_void_p(tokens.ctypes.data),
+                                                        C.c_void_p(pos.ctypes.data), n, steps,
+                                                        C.c_void_p(out.ctypes.data)), "generate_batch")
+        return out[:steps]
+
+    def batch_set(self, tokens, pos, seqs=None):
+        """Upload a batch for batch_enqueue (timing)."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        sp = None
+        if seqs is not None:
+            seqs = np.ascontiguousarray(seqs, np.int32)
+            sp = C.c_void_p(seqs.ctypes.data)
+        _lib.check(self.lib.cats_gpu_llm_batch_set(self.h, C.c_void_p(tokens.ctypes.data),
+                                                   C.c_void_p(pos.ctypes.data), sp, tokens.size), "batch_set")
+
+    def batch_enqueue(self):
+        """Enqueue one batched step of the batch set last on the model's stream."""
+        _lib.check(self.lib.cats_gpu_llm_batch_enqueue(self.h), "batch_enqueue")
+
     def set_engine(self, engine):
         """ENGINE_PERSISTENT (default): one cooperative kernel runs whole tokens;
         ENGINE_GRAPH: a CUDA graph of per-phase kernels."""

@@ -170,6 +170,32 @@ int cats_gpu_llm_tp_connect(cats_gpu_llm *m, const void *id);
  * barrier; *ctas receives the grid size (host must hold 2*148*per_cta). */
 int cats_gpu_llm_trace_step(cats_gpu_llm *m, int token, int pos, unsigned long long *host, int per_cta,
                             int *ctas);
+/* Batched step on the tensor cores: prefill of a prompt, and batched decode
+ * of several sequences.  T tokens go through cats_llama2_transformer
+ * (llm/catseye_llm.h:1625-1772) together, token t at position pos[t] of KV
+ * sequence seqs[t] (seqs NULL: sequence 0, the one the single-token engines
+ * use), attending to positions 0..pos[t] of its sequence.  Every weight
+ * product is one tcgen05 GEMM over the T tokens with fp16 activations: the
+ * reference's fp32-activation binding (matmul_q4_0 with quantize_null,
+ * :880-914) up to fp16 rounding.  Q4_0/Q8_0 models whose products have
+ * n % 64 == 0 and head_size % 8 == 0 (else CATS_ERR_UNSUPPORTED).
+ * cats_gpu_llm_batch_reserve: room for max_tokens per step and n_seqs KV
+ *   sequences (more sequences reallocate the cache, keeping those present).
+ * cats_gpu_llm_forward_batch: one step; next_host (may be NULL) receives the
+ *   greedy argmax per token, logits_host (may be NULL) [T][vocab].
+ * cats_gpu_llm_generate_batch: greedy decoding of n sequences (sequence i
+ *   starts from tokens[i] at pos[i]) for `steps` steps, one token of every
+ *   sequence per step, replayed from a captured graph with no host round
+ *   trip; tokens_host (may be NULL) receives [steps][n] ids.
+ * cats_gpu_llm_batch_set / _batch_enqueue: upload a batch, then enqueue one
+ *   step of it on the model's stream (asynchronous, for timing). */
+int cats_gpu_llm_batch_reserve(cats_gpu_llm *m, int max_tokens, int n_seqs);
+int cats_gpu_llm_forward_batch(cats_gpu_llm *m, const int *tokens, const int *pos, const int *seqs, int T,
+                               int *next_host, float *logits_host);
+int cats_gpu_llm_generate_batch(cats_gpu_llm *m, const int *tokens, const int *pos, int n, int steps,
+                                int *tokens_host);
+int cats_gpu_llm_batch_set(cats_gpu_llm *m, const int *tokens, const int *pos, const int *seqs, int T);
+int cats_gpu_llm_batch_enqueue(cats_gpu_llm *m);
 /* Asynchronous form for timing: enqueue `steps` greedy steps on the model's stream. */
 int cats_gpu_llm_enqueue(cats_gpu_llm *m, int steps);
 int cats_gpu_llm_set_position(cats_gpu_llm *m, int token, int pos);

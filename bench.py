@@ -25,6 +25,19 @@ cpu_baseline : the reference's own CPU step (oracle/_ref, all cores) on a
 
 --impl reference times only that CPU reference on the same workload.
 
+--workload llama70b_q4_0_prefill512 | llama7b_q4_0_batch16 measure the
+batched step on the tensor cores (cats_gpu_llm_forward_batch): a 512-token
+prompt prefilled through the 80-layer Llama-2-70B-shape Q4_0 model in one
+step (value = prompt tok/s), or 16 sequences decoded one token each per step
+on the 7B shape (value = tok/s over all 16; the step is a CUDA graph replayed
+with the argmax fed back on the device).  roofline: the tcgen05 product
+(k_qgemm) of the largest weight (w1/w3) at the step's token count, timed on
+its own with CUDA events: tensor FLOP/s against the measured bf16 peak for
+prefill, weight bytes/s against the measured HBM copy rate for batch 16.
+e2e = the host API (token ids in, argmax ids out); cpu_baseline = the
+reference's own step on all cores (it processes a prompt or a batch one
+token at a time, so its tok/s is its decode rate).
+
 --workload sgemm_4096 | cnn_forward_b128 measure the CNN side instead: a
 4096^3 fp32 NN sgemm (cats_sgemm_dev), or the 32x32x3 CNN's four
 convolutions and two linear layers at batch 128 (cats_conv2d_forward_dev /
@@ -76,6 +89,21 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 tensor peak (TFLOP/s): the measured cuBLAS burst figure."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    return 1590.0, "fallback"
+
+
+# batched workloads: (model, weight type, tokens per step, sequences)
+BATCHED = {
+    "llama70b_q4_0_prefill512": ("LLAMA2_70B", 2, 512, 1),
+    "llama7b_q4_0_batch16": ("LLAMA2_7B", 2, 16, 16),
+}
 
 
 class Clocks:
@@ -242,6 +270,171 @@ def run_ours(args, dist, rank, ws, local):
     kbytes = wbytes * args.steps + kv_bytes
     kms = ms
     return ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg
+
+
+# -------------------------------------------- batched step (prefill, batch 16)
+def run_batched(args, dist, rank, ws, local):
+    import torch
+    from catseye_b200 import _lib, llm
+    _lib.init(local)
+    torch.cuda.set_device(local)
+    name, t, T, nseq = BATCHED[args.workload]
+    cfg = getattr(llm, name).with_type(t)
+    if args.layers:
+        from dataclasses import replace
+        cfg = replace(cfg, n_layers=args.layers)
+    m = llm.GpuLLM(cfg)
+    m.init_random(SEED)
+    stream = torch.cuda.ExternalStream(m.stream)
+    rng = np.random.default_rng(SEED + 1 + rank)
+    prefill = nseq == 1
+    if prefill:
+        m.batch_reserve(T, 1)
+        toks = rng.integers(0, cfg.vocab, T).astype(np.int32)
+        pos = np.arange(T, dtype=np.int32)
+        m.batch_set(toks, pos)
+        launch = m.batch_enqueue
+        step_tokens = T
+
+        def host_step():
+            return m.forward_batch(toks, pos)
+        h2d, d2h = 3 * 4 * T, 4 * T
+    else:
+        m.batch_reserve(max(T, nseq * PROMPT), nseq)
+        ptoks = rng.integers(0, cfg.vocab, nseq * PROMPT).astype(np.int32)
+        ppos = np.tile(np.arange(PROMPT, dtype=np.int32), nseq)
+        pseq = np.repeat(np.arange(nseq, dtype=np.int32), PROMPT)
+        nxt = m.forward_batch(ptoks, ppos, pseq)           # every sequence's prompt, one call (untimed)
+        first = nxt[PROMPT - 1::PROMPT].copy()
+        p0 = np.full(nseq, PROMPT, np.int32)
+        assert PROMPT + args.warmup + args.steps + args.e2e_steps <= cfg.seq_len
+        m.batch_set(first, p0, np.arange(nseq, dtype=np.int32))
+        step_tokens = nseq
+
+        def launch(k=1):
+            m.batch_enqueue_decode(k)
+        state = {"tok": first, "pos": p0 + args.warmup + args.steps}
+
+        def host_step():
+            state["tok"] = m.forward_batch(state["tok"], state["pos"], np.arange(nseq, dtype=np.int32))
+            state["pos"] = state["pos"] + 1
+            return state["tok"]
+        h2d, d2h = 3 * 4 * nseq, 4 * nseq
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    if prefill:
+        for _ in range(args.warmup):
+            launch()
+    else:
+        launch(args.warmup)
+    torch.cuda.synchronize()
+    m.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        if prefill:
+            for _ in range(args.steps):
+                launch()
+        else:
+            launch(args.steps)
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    m.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    clocks = clk.summary()
+    e2e_steps = max(1, min(args.e2e_steps, 4 if prefill else args.e2e_steps))
+    host_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        host_step()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    # the products timed alone at this token count (diagnostic + roofline)
+    kinds = {}
+    for k, kname in enumerate(("qkv", "wo", "w13", "w2", "cls")):
+        kms, fl, wb = m.time_product(k, T, reps=2)
+        kinds[kname] = {"us_per_launch": round(kms * 1e3, 2), "tflops": round(fl / (kms * 1e-3) / 1e12, 1),
+                        "weight_gbs": round(wb / (kms * 1e-3) / 1e9, 1), "flop": fl, "weight_bytes": wb}
+    wbytes = m.weight_bytes()
+    m.close()
+    return dict(ms=ms, e2e_s=e2e_s, e2e_steps=e2e_steps, kinds=kinds, wbytes=wbytes, clocks=clocks, cfg=cfg, T=T,
+                nseq=nseq, step_tokens=step_tokens, h2d=h2d, d2h=d2h, prefill=prefill)
+
+
+def batched_main(args):
+    name, t, T, nseq = BATCHED[args.workload]
+    prefill = nseq == 1
+    metric = f"prefill tok/s ({T}-token prompt)" if prefill else f"decode tok/s (batch {nseq})"
+    dtype = "q4_0 weights dequantized to f16 x f16 activations, f32 accumulate (tcgen05)"
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        from catseye_b200 import llm
+        cfg = getattr(llm, name).with_type(t)
+        cb = cpu_reference(cfg, "reference", samples=3)
+        cb["sample"] += "; the reference runs a prompt or a batch one token at a time, so this is its rate"
+        print(json.dumps({"impl": "reference", "metric": metric, "value": round(cb["value"], 3), "unit": "tok/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x q8 (int8 dot, f32 accumulate)",
+                          "data": "synthetic", "config": {"workload": workload_name(args)}, "cpu_baseline": cb,
+                          "e2e": {"value": round(cb["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
+    dist, rank, ws, local = dist_init()
+    r = run_batched(args, dist, rank, ws, local)
+    if rank == 0:
+        cfg, ms = r["cfg"], r["ms"]
+        tok_s = ws * r["step_tokens"] * args.steps / (ms * 1e-3)
+        w13 = r["kinds"]["w13"]
+        kms = w13["flop"] / (w13["tflops"] * 1e12) * 1e3
+        if prefill:
+            peak, peak_kind = tensor_peak()
+            achieved = w13["tflops"]
+            roof = {"bound": "tensor", "kernel": f"k_qgemm (w1/w3 product, {cfg.dim}x{2 * cfg.hidden}, T={T})",
+                    "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "traffic": None, "flop_per_launch": w13["flop"],
+                    "ms_per_launch": round(kms, 4)}
+        else:
+            peak, peak_kind = peaks()
+            achieved = w13["weight_gbs"]
+            roof = {"bound": "hbm", "kernel": f"k_qgemm (w1/w3 product, {cfg.dim}x{2 * cfg.hidden}, T={T})",
+                    "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "traffic": None, "bytes_per_launch": w13["weight_bytes"],
+                    "ms_per_launch": round(kms, 4)}
+        step_flop = 2.0 * (r["wbytes"] / 18 * 32) * r["step_tokens"]
+        launches = cfg.n_layers * 10 + (4 if prefill else 5)
+        line = {"metric": metric, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+                "config": {"workload": workload_name(args), "tokens_per_step": r["step_tokens"], "sequences": nseq,
+                           "dim": cfg.dim, "layers": cfg.n_layers, "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads,
+                           "context": cfg.seq_len, "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                           "weight_tflop_per_s": round(step_flop * args.steps / (ms * 1e-3) / 1e12, 1),
+                           "l2": f"weights {r['wbytes'] / 1e9:.1f} GB per step > 126 MB L2; no flush"},
+                "roofline": roof, "products": {k: {kk: v[kk] for kk in ("us_per_launch", "tflops", "weight_gbs")}
+                                               for k, v in r["kinds"].items()},
+                "e2e": {"value": round(ws * r["step_tokens"] * r["e2e_steps"] / r["e2e_s"], 2), "unit": "tok/s",
+                        "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+                "gpu_launches": launches * args.steps, "clocks": r["clocks"]}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference(cfg, "reference")
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
 
 
 # ------------------------------------------------ fp32 GEMM workloads (CNN side)
@@ -464,13 +657,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama7b_q4_0", choices=sorted(WORKLOADS) + ["sgemm_4096", "cnn_forward_b128"])
+    ap.add_argument("--workload", default="llama7b_q4_0",
+                    choices=sorted(WORKLOADS) + sorted(BATCHED) + ["sgemm_4096", "cnn_forward_b128"])
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload in ("sgemm_4096", "cnn_forward_b128"):
         gemm_main(args)
+        return
+    if args.workload in BATCHED:
+        batched_main(args)
         return
 
     if args.impl == "reference":

@@ -54,6 +54,8 @@ SIGNATURES = {
     "cats_gpu_llm_generate_batch": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "cats_gpu_llm_batch_set": (_i, [_vp, _vp, _vp, _vp, _i]),
     "cats_gpu_llm_batch_enqueue": (_i, [_vp]),
+    "cats_gpu_llm_batch_enqueue_decode": (_i, [_vp, _i]),
+    "cats_gpu_llm_time_product": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "cats_gpu_llm_set_engine": (_i, [_vp, _i]),
     "cats_gpu_tp_unique_id_bytes": (_sz, []),
     "cats_gpu_tp_unique_id": (_i, [_vp, _sz]),

@@ -31,6 +31,7 @@
 #include "qgemm.cuh"
 #include <algorithm>
 #include <cstring>
+#include <vector>
 
 namespace cats {
 
@@ -447,12 +448,13 @@ static void free_batch(LlmModel *m)
     m->bt_graph = nullptr;
     m->bt_graph_T = 0;
     void *dp[] = {m->bt_tok, m->bt_blocks, m->bt_x, m->bt_delta, m->bt_y, m->bt_q, m->bt_xb, m->bt_lg, m->bt_logits,
-                  m->bt_x16, m->bt_next, m->bt_step, m->bt_log};
+                  m->bt_x16, m->bt_ws, m->bt_next, m->bt_step, m->bt_log};
     for (void *p : dp) if (p) cudaFree(p);
     if (m->bt_tok_host) cudaFreeHost(m->bt_tok_host);
     if (m->bt_blocks_host) cudaFreeHost(m->bt_blocks_host);
     m->bt_tok = nullptr; m->bt_blocks = nullptr; m->bt_x = nullptr; m->bt_delta = nullptr; m->bt_y = nullptr;
     m->bt_q = nullptr; m->bt_xb = nullptr; m->bt_lg = nullptr; m->bt_logits = nullptr; m->bt_x16 = nullptr;
+    m->bt_ws = nullptr; m->bt_ws_bytes = 0;
     m->bt_next = nullptr; m->bt_step = nullptr; m->bt_log = nullptr; m->bt_log_cap = 0;
     m->bt_tok_host = nullptr; m->bt_blocks_host = nullptr;
     m->bt_cap = 0;
@@ -506,6 +508,14 @@ int llm_batch_reserve(LlmModel *m, int cap, int n_seqs)
     ok &= cudaMalloc(&m->bt_lg, (size_t)tp * cap * m->vocab_loc * 4) == cudaSuccess;
     ok &= cudaMalloc(&m->bt_logits, (size_t)cap * c.vocab * 4) == cudaSuccess;
     ok &= cudaMalloc(&m->bt_x16, qgemm_x16_bytes((int)nmax, cap)) == cudaSuccess;
+    // K-split partials: the most any product takes at any token count up to
+    // cap (every layer has layer 0's shapes)
+    size_t wsb = 0;
+    for (int T = 1; T <= cap; T++)
+        for (const DevWeight *w : {&m->qkv[0], &m->wo[0], &m->w13[0], &m->w2[0], &m->cls})
+            wsb = std::max(wsb, qgemm_workspace_bytes(w->L, T));
+    if (wsb) ok &= cudaMalloc(&m->bt_ws, wsb) == cudaSuccess;
+    m->bt_ws_bytes = ok ? wsb : 0;
     ok &= cudaMalloc(&m->bt_next, (size_t)cap * 4) == cudaSuccess;
     ok &= cudaMalloc(&m->bt_step, 4) == cudaSuccess;
     ok &= cudaMallocHost(&m->bt_tok_host, (size_t)cap * sizeof(BatchTok)) == cudaSuccess;
@@ -566,8 +576,8 @@ static cudaError_t launch_attn_batch(LlmModel *m, int l, int T, int nblocks, cud
 static cudaError_t residual_product(LlmModel *m, const DevWeight &W, int T, cudaStream_t st)
 {
     const LlmConfig &c = m->c;
-    if (c.tp_size <= 1) return launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_x, T, true, m->err, st);
-    cudaError_t e = launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_delta, T, false, m->err, st);
+    if (c.tp_size <= 1) return launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_x, T, true, m->bt_ws, m->bt_ws_bytes, m->err, st);
+    cudaError_t e = launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_delta, T, false, m->bt_ws, m->bt_ws_bytes, m->err, st);
     if (e) return e;
     m->allreduce(m->comm_ctx, m->bt_delta, (size_t)T * c.dim, st);
     const long long n = (long long)T * c.dim;
@@ -587,7 +597,8 @@ cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int
     for (int l = 0; l < c.n_layers; l++) {
         k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_att + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad);
         if ((e = cudaGetLastError())) return e;
-        if ((e = launch_qgemm_x16(m->qkv[l].L, m->qkv[l].ptr, m->bt_x16, m->bt_y, T, false, m->err, st))) return e;
+        if ((e = launch_qgemm_x16(m->qkv[l].L, m->qkv[l].ptr, m->bt_x16, m->bt_y, T, false, m->bt_ws,
+                                    m->bt_ws_bytes, m->err, st))) return e;
         const long long np = (long long)T * (m->q_dim + 2 * m->kv_dim) / 2;
         k_rope_kv<<<grid_for(np, 256), 256, 0, st>>>(m->bt_y, T, m->bt_tok, m->bt_q, m->kcache, m->vcache, seq_stride,
                                                      (size_t)l * c.seq_len * m->kv_dim, m->q_dim, m->kv_dim,
@@ -598,7 +609,8 @@ cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int
         if ((e = residual_product(m, m->wo[l], T, st))) return e;
         k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_ffn + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad);
         if ((e = cudaGetLastError())) return e;
-        if ((e = launch_qgemm_x16(m->w13[l].L, m->w13[l].ptr, m->bt_x16, m->bt_y, T, false, m->err, st))) return e;
+        if ((e = launch_qgemm_x16(m->w13[l].L, m->w13[l].ptr, m->bt_x16, m->bt_y, T, false, m->bt_ws,
+                                    m->bt_ws_bytes, m->err, st))) return e;
         const long long nh = (long long)T * (m->hidden_loc / 8);
         k_swiglu_x16<<<grid_for(nh, 256), 256, 0, st>>>(m->bt_y, T, m->hidden_loc, m->bt_x16, Tpad);
         if ((e = cudaGetLastError())) return e;
@@ -607,7 +619,7 @@ cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int
     k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_final, m->bt_x16, c.dim, Tpad);
     if ((e = cudaGetLastError())) return e;
     float *lg = m->bt_lg + (size_t)c.tp_rank * T * m->vocab_loc;
-    if ((e = launch_qgemm_x16(m->cls.L, m->cls.ptr, m->bt_x16, lg, T, false, m->err, st))) return e;
+    if ((e = launch_qgemm_x16(m->cls.L, m->cls.ptr, m->bt_x16, lg, T, false, m->bt_ws, m->bt_ws_bytes, m->err, st))) return e;
     if (c.tp_size > 1) m->allgather(m->comm_ctx, m->bt_lg, (size_t)T * m->vocab_loc, c.tp_rank, st);
     k_logits_argmax<<<T, 256, 0, st>>>(m->bt_lg, T, m->vocab_loc, c.tp_size, m->bt_logits, m->bt_next, m->err);
     if ((e = cudaGetLastError())) return e;
@@ -657,16 +669,17 @@ int llm_forward_batch(LlmModel *m, const int *tokens, const int *pos, const int 
     return cudaStreamSynchronize(m->stream) == cudaSuccess ? E_OK : E_CUDA;
 }
 
-int llm_generate_batch(LlmModel *m, int T, int steps, int *tokens_host)
+cudaError_t llm_batch_decode_enqueue(LlmModel *m, int T, int steps)
 {
-    // the batch (one token per sequence) was set by llm_batch_set; one step
-    // is captured once into a graph and replayed `steps` times
-    if (steps <= 0) return E_OK;
+    // one token per sequence (set by llm_batch_set): every attention block is
+    // one token; one step is captured once into a graph and replayed
+    if (steps <= 0) return cudaSuccess;
+    cudaError_t e;
     if (m->bt_log_cap < steps * T) {
         if (m->bt_log) cudaFree(m->bt_log);
         m->bt_log = nullptr;
         m->bt_log_cap = 0;
-        if (cudaMalloc(&m->bt_log, (size_t)steps * T * 4) != cudaSuccess) return E_NOMEM;
+        if ((e = cudaMalloc(&m->bt_log, (size_t)steps * T * 4))) return e;
         m->bt_log_cap = steps * T;
         if (m->bt_exec) { cudaGraphExecDestroy(m->bt_exec); m->bt_exec = nullptr; }
         if (m->bt_graph) { cudaGraphDestroy(m->bt_graph); m->bt_graph = nullptr; }
@@ -675,20 +688,66 @@ int llm_generate_batch(LlmModel *m, int T, int steps, int *tokens_host)
     if (m->bt_graph_T != T || !m->bt_exec) {
         if (m->bt_exec) { cudaGraphExecDestroy(m->bt_exec); m->bt_exec = nullptr; }
         if (m->bt_graph) { cudaGraphDestroy(m->bt_graph); m->bt_graph = nullptr; }
-        if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) return E_CUDA;
-        // one token per sequence: every block is one token
+        if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal))) return e;
         const cudaError_t e1 = llm_batch_enqueue(m, T, T, true, m->bt_log, m->bt_log_cap / T);
         const cudaError_t e2 = cudaStreamEndCapture(m->stream, &m->bt_graph);
-        if (e1 || e2) return E_CUDA;
-        if (cudaGraphInstantiate(&m->bt_exec, m->bt_graph, 0)) return E_CUDA;
+        if (e1) return e1;
+        if (e2) return e2;
+        if ((e = cudaGraphInstantiate(&m->bt_exec, m->bt_graph, 0))) return e;
         m->bt_graph_T = T;
     }
     for (int s = 0; s < steps; s++)
-        if (cudaGraphLaunch(m->bt_exec, m->stream)) return E_CUDA;
+        if ((e = cudaGraphLaunch(m->bt_exec, m->stream))) return e;
+    return cudaSuccess;
+}
+
+int llm_generate_batch(LlmModel *m, int T, int steps, int *tokens_host)
+{
+    if (steps <= 0) return E_OK;
+    cudaError_t e = llm_batch_decode_enqueue(m, T, steps);
+    if (e) return e == cudaErrorMemoryAllocation ? E_NOMEM : E_CUDA;
     if (tokens_host &&
         cudaMemcpyAsync(tokens_host, m->bt_log, (size_t)steps * T * 4, cudaMemcpyDeviceToHost, m->stream))
         return E_CUDA;
     return cudaStreamSynchronize(m->stream) == cudaSuccess ? E_OK : E_CUDA;
+}
+
+cudaError_t llm_time_product(LlmModel *m, int kind, int T, int reps, float *ms_per_launch, double *flop_per_launch,
+                             double *weight_bytes_per_launch)
+{
+    const LlmConfig &c = m->c;
+    if (T <= 0 || T > m->bt_cap || reps <= 0 || kind < 0 || kind > 4) return cudaErrorInvalidValue;
+    std::vector<const DevWeight *> ws;
+    for (int l = 0; l < c.n_layers && kind < 4; l++)
+        ws.push_back(kind == 0 ? &m->qkv[l] : kind == 1 ? &m->wo[l] : kind == 2 ? &m->w13[l] : &m->w2[l]);
+    if (kind == 4) ws.push_back(&m->cls);
+    float *y = kind == 4 ? m->bt_lg : m->bt_y;   // both hold [T][d] of this kind
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    auto run = [&](int passes) -> cudaError_t {
+        for (int r = 0; r < passes; r++)
+            for (auto w : ws) {
+                cudaError_t le = launch_qgemm_x16(w->L, w->ptr, m->bt_x16, y, T, false, m->bt_ws, m->bt_ws_bytes, m->err,
+                                                  m->stream);
+                if (le) return le;
+            }
+        return cudaSuccess;
+    };
+    cudaError_t e = run(1);   // warm-up
+    if (!e) e = cudaEventRecord(e0, m->stream);
+    if (!e) e = run(reps);
+    if (!e) e = cudaEventRecord(e1, m->stream);
+    if (!e) e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (!e) cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    const WeightLayout &L = ws[0]->L;
+    *ms_per_launch = ms / (float)(reps * ws.size());
+    *flop_per_launch = 2.0 * T * L.n * L.d;
+    *weight_bytes_per_launch = (double)gguf_row_bytes(L.type, L.n) * L.d;
+    return e;
 }
 
 } // namespace cats

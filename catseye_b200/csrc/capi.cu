@@ -42,6 +42,8 @@ struct Ctx {
     size_t cap_a = 0, cap_b = 0, cap_c = 0, cap_work = 0;
     __half *d_x16 = nullptr;   // fp16 activations of the batched product
     size_t cap_x16 = 0;
+    float *d_ws = nullptr;     // its K-split partials
+    size_t cap_ws = 0;
 };
 
 Ctx g;
@@ -211,11 +213,12 @@ void cats_gpu_term(void)
     cudaStreamSynchronize(g.stream);
     for (auto &kv : g.weights) if (kv.second.W.ptr) cudaFree(kv.second.W.ptr);
     g.weights.clear();
-    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err, g.d_x16};
+    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err, g.d_x16, g.d_ws};
     for (void *b : bufs) if (b) cudaFree(b);
     g.d_x = nullptr; g.d_out = nullptr; g.d_a = g.d_b = g.d_c = g.d_work = nullptr; g.d_err = nullptr;
     g.d_x16 = nullptr;
-    g.d_x_cap = g.d_out_cap = g.cap_a = g.cap_b = g.cap_c = g.cap_work = g.cap_x16 = 0;
+    g.d_ws = nullptr;
+    g.d_x_cap = g.d_out_cap = g.cap_a = g.cap_b = g.cap_c = g.cap_work = g.cap_x16 = g.cap_ws = 0;
     cudaStreamDestroy(g.stream);
     g.stream = nullptr;
     g.init = false;
@@ -345,7 +348,9 @@ int cats_gpu_qgemm_dev(const void *w, const float *d_x, float *d_y, int T, void 
     if (!qgemm_supported(r.W.L)) return fail(CATS_ERR_UNSUPPORTED, what);
     cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
     if (grow((void **)&g.d_x16, &g.cap_x16, qgemm_x16_bytes(r.n, T))) return g.last_err;
-    return check(launch_qgemm(r.W.L, r.W.ptr, d_x, g.d_x16, d_y, T, g.d_err, st), what);
+    const size_t wsb = qgemm_workspace_bytes(r.W.L, T);
+    if (wsb && grow((void **)&g.d_ws, &g.cap_ws, wsb)) return g.last_err;
+    return check(launch_qgemm(r.W.L, r.W.ptr, d_x, g.d_x16, d_y, T, g.d_ws, g.cap_ws, g.d_err, st), what);
 }
 
 int cats_gpu_qgemm(const void *w, const float *x, float *y, int T)
@@ -613,6 +618,23 @@ int cats_gpu_llm_batch_enqueue(cats_gpu_llm *h)
     const char *what = "cats_gpu_llm_batch_enqueue";
     if (!h || h->bt_T <= 0) return fail(CATS_ERR_ARG, what);
     return check(llm_batch_enqueue(&h->m, h->bt_T, h->bt_nb, false, nullptr, 0), what);
+}
+
+int cats_gpu_llm_batch_enqueue_decode(cats_gpu_llm *h, int steps)
+{
+    const char *what = "cats_gpu_llm_batch_enqueue_decode";
+    if (!h || h->bt_T <= 0 || steps < 0 || h->bt_nb != h->bt_T) return fail(CATS_ERR_ARG, what);
+    return check(llm_batch_decode_enqueue(&h->m, h->bt_T, steps), what);
+}
+
+int cats_gpu_llm_time_product(cats_gpu_llm *h, int kind, int T, int reps, float *ms_per_launch,
+                              double *flop_per_launch, double *weight_bytes_per_launch)
+{
+    const char *what = "cats_gpu_llm_time_product";
+    if (!h || !ms_per_launch || !flop_per_launch || !weight_bytes_per_launch) return fail(CATS_ERR_ARG, what);
+    if (int rc = batch_ready(h, what)) return rc;
+    return check(llm_time_product(&h->m, kind, T, reps, ms_per_launch, flop_per_launch, weight_bytes_per_launch),
+                 what);
 }
 
 int cats_gpu_llm_forward_batch(cats_gpu_llm *h, const int *tokens, const int *pos, const int *seqs, int T,

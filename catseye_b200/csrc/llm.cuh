@@ -73,6 +73,8 @@ struct LlmModel {
     float *bt_lg = nullptr;               // classifier slices [tp][T][vocab_loc]
     float *bt_logits = nullptr;           // [T][vocab]
     __half *bt_x16 = nullptr;             // the fp16 operand of the products
+    float *bt_ws = nullptr;               // K-split partials of the products
+    size_t bt_ws_bytes = 0;
     int *bt_next = nullptr;               // [T] greedy argmax
     int *bt_step = nullptr;               // generate loop: steps taken
     int *bt_log = nullptr;                // generate loop: [steps][T] token ids
@@ -141,6 +143,13 @@ cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int
 int llm_forward_batch(LlmModel *m, const int *tokens, const int *pos, const int *seqs, int T, int *next_host,
                       float *logits_host);
 int llm_generate_batch(LlmModel *m, int T, int steps, int *tokens_host);
+cudaError_t llm_batch_decode_enqueue(LlmModel *m, int T, int steps);
+// Device time of one kind of batched product (0 qkv, 1 wo, 2 w13, 3 w2,
+// 4 classifier) at T tokens: `reps` passes over every layer's weight of that
+// kind, back to back on the model's stream (CUDA events).  Reports ms per
+// launch, its 2*T*n*d FLOPs and its weight bytes (reference layout).
+cudaError_t llm_time_product(LlmModel *m, int kind, int T, int reps, float *ms_per_launch, double *flop_per_launch,
+                             double *weight_bytes_per_launch);
 
 // generate one synthetic tensor in the reference's GGUF layout (device dst)
 cudaError_t synth_tensor(uint8_t *dst, int type, int n, int d, unsigned long long seed, int tensor_id,

@@ -8,21 +8,26 @@
 // and fp32 accumulation: relative error <= 1e-3.
 //
 // CTA: 128 weight rows (the UMMA M) x BN tokens (the UMMA N, 16..256), K in
-// slices of 64 (two 32-element blocks).
-//  * Producers (warps 0-3, one weight row per thread): read the row's two
-//    blocks from the weight's tile layout (the matvec's, so prefill and decode
-//    share one copy of the weights in HBM) three K slices ahead, dequantize to
-//    fp16 and store the row in the K-major 128-byte-swizzled form UMMA reads.
-//    Thread 0 also brings the stage's BN activation rows in with one bulk
-//    copy: the fp16 operand is stored K-slice-major and pre-swizzled
-//    (k_x16_swizzled, or a producing kernel writing x16_index order).  Then
-//    fence.proxy.async and an arrive on the stage's full barrier.
-//  * MMA warp (warp 4, one thread): four K=16 tcgen05.mma per stage into the
+// slices of 64 (two 32-element blocks); grid (N tiles, M tiles, K splits),
+// N tiles fastest so the CTAs that share a weight tile run together and the
+// second reads it from L2.
+//  * Producers (warps 0-7): thread p owns block p & 1 of weight row p >> 1 in
+//    every K slice.  It loads the block's words from the weight's tile layout
+//    (the matvec's, so prefill and decode share one copy of the weights in
+//    HBM) four slices ahead into registers, dequantizes them to fp16 and
+//    stores them in the K-major 128-byte-swizzled form UMMA reads.  Thread 0
+//    also brings the stage's BN activation rows in with one bulk copy: the
+//    fp16 operand is stored K-slice-major and pre-swizzled (k_x16_swizzled,
+//    or a producing kernel writing x16_index order).  Then fence.proxy.async
+//    and an arrive on the stage's full barrier.
+//  * MMA warp (warp 8, one thread): four K=16 tcgen05.mma per stage into the
 //    TMEM accumulator; tcgen05.commit releases the stage when they complete.
-//  * Epilogue: after a final commit, warp w reads TMEM lanes 32w..32w+31 (its
-//    weight rows) 16 columns at a time and writes Y, or adds to it
-//    (accumulate: the residual stream), consecutive lanes being consecutive
-//    rows of Y (coalesced).
+//  * Epilogue: after a final commit, warps w and w + 4 read TMEM lanes
+//    32w..32w+31 (weight rows), each half of the columns, 8 at a time, and
+//    write Y or add to it (accumulate: the residual stream); consecutive lanes
+//    are consecutive rows of Y (coalesced).  With a K split each CTA writes
+//    its partial sums to a workspace and k_splitk_sum adds the splits in
+//    order (deterministic).
 // Every wait is bounded; TMEM is freed on every path.
 #include "qgemm.cuh"
 #include <algorithm>
@@ -31,11 +36,14 @@ namespace cats {
 
 constexpr int QG_M = 128;
 constexpr int QG_K = 64;
-constexpr int QG_STAGES = 4;
-constexpr int QG_PF = 3;                     // K slices of weight words a producer has in flight
-constexpr int QG_PROD = 128;                 // producer threads (4 warps)
+constexpr int QG_PF = 4;                     // K slices of weight words a producer has in flight
+constexpr int QG_PROD = 256;                 // producer threads (8 warps): one block per K slice each
 constexpr int QG_THREADS = QG_PROD + 32;     // + the MMA warp
+constexpr int QG_MMA_WARP = QG_PROD / 32;
 constexpr uint32_t QG_A_BYTES = QG_M * 128;  // one stage of weight rows (fp16, 64 per row)
+constexpr int QG_MAX_SPLITS = 16;
+
+__host__ __device__ constexpr int qg_stages(int bn) { return bn >= 256 ? 3 : 4; }
 
 struct QgemmArgs {
     const uint8_t *w;                 // tile layout (matvec.cuh WeightLayout)
@@ -44,7 +52,10 @@ struct QgemmArgs {
     unsigned long long tile_bytes;
     const __half *x;                  // fp16 activations, [n/64][Tpad][64], rows pre-swizzled
     float *y;                         // [T][d]
+    float *ws;                        // K split partials [splits][T][d] (splits > 1)
     int T, Tpad;
+    int kper;                         // K slices per split
+    int splits;
     int accumulate;                   // y += product instead of y = product
     int *err;
 };
@@ -81,35 +92,29 @@ __device__ __forceinline__ void bulk_g2s_keep(void *dst, const void *src, uint32
                  : "memory");
 }
 
-// The raw words of one weight row's two blocks at one K slice.
-struct RawRow {
-    uint4 w[4];     // Q4_0: w[0..1] nibbles of the two blocks; Q8_0: lo0, hi0, lo1, hi1
-    uint32_t sc;    // the two fp16 scales
+// The raw words of one 32-element block of a weight row.
+struct RawBlk {
+    uint4 w[2];     // Q4_0: w[0] = the 16 nibble bytes; Q8_0: w[0], w[1] = the low and high 16 codes
+    uint32_t sc;    // fp16 scale in the low half
 };
 
-// Issue the loads of weight row `row`'s two blocks at K slice kb (no use yet,
+// Issue the loads of block h of weight row `row` at K slice kb (no use yet,
 // so several slices' loads are in flight while earlier ones are dequantized).
 template <int WT>
-__device__ __forceinline__ void fetch_row(const QgemmArgs &a, int row, int kb, RawRow &r)
+__device__ __forceinline__ void fetch_blk(const QgemmArgs &a, int row, int kb, int h, RawBlk &r)
 {
-    const int u = 2 * kb, s = u / MV_SEG_UNITS, u0 = u % MV_SEG_UNITS;
+    const int u = 2 * kb + h, s = u / MV_SEG_UNITS, uu = u % MV_SEG_UNITS;
     const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
     const int t = row / a.R, rr = row % a.R;
     const uint8_t *ch = a.w + (size_t)t * a.tile_bytes + (size_t)s * a.full_chunk;
     const uint32_t sstride = (uint32_t)round_up((size_t)us * 2, 16);
     const uint32_t ub = WT == W_Q4_0 ? 16 : 32;
-    r.sc = __ldg(reinterpret_cast<const unsigned int *>(ch + (size_t)a.R * us * ub + rr * sstride + u0 * 2));
+    r.sc = __ldg(reinterpret_cast<const unsigned short *>(ch + (size_t)a.R * us * ub + rr * sstride + uu * 2));
     if (WT == W_Q4_0) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + u0) * 16);
-        r.w[0] = __ldg(p);
-        r.w[1] = __ldg(p + 1);
+        r.w[0] = __ldg(reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + uu) * 16));
     } else {
-        const uint4 *lo = reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2) * us + u0) * 16);
-        const uint4 *hi = reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2 + 1) * us + u0) * 16);
-        r.w[0] = __ldg(lo);
-        r.w[1] = __ldg(hi);
-        r.w[2] = __ldg(lo + 1);
-        r.w[3] = __ldg(hi + 1);
+        r.w[0] = __ldg(reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2) * us + uu) * 16));
+        r.w[1] = __ldg(reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2 + 1) * us + uu) * 16));
     }
 }
 
@@ -124,58 +129,57 @@ __device__ __forceinline__ __half2 codes_to_half2(uint32_t t, __half2 bias)
 
 __device__ __forceinline__ uint32_t h2u(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
 
-// Dequantize a fetched row into 64 fp16 stored swizzled as row r of the
-// stage's weight tile (zeros for rows past d).  Value = code * d, the fp16
-// product of two exact fp16 operands, i.e. the correctly rounded q*d.
+// Dequantize a fetched block into 32 fp16, stored swizzled as chunks
+// 4h .. 4h+3 of row r of the stage's weight tile (zeros for rows past d).
+// Value = code * d, the fp16 product of two exact fp16 operands, i.e. the
+// correctly rounded q*d.
 template <int WT>
-__device__ __forceinline__ void dequant_row(const RawRow &raw, bool valid, uint8_t *tile, int r)
+__device__ __forceinline__ void dequant_blk(const RawBlk &raw, bool valid, uint8_t *tile, int r, int h)
 {
-    uint32_t h[32];   // 64 fp16, two per word: h[16b + e/2] holds elements e, e+1 of block b
+    uint32_t o[16];   // 32 fp16, two per word: o[e/2] holds elements e, e+1
     if (valid) {
+        const uint16_t sb = (uint16_t)(raw.sc & 0xffff);
+        const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
+        if (WT == W_Q4_0) {
+            // byte j holds element j (low nibble) and element j + 16 (high nibble)
+            const __half2 bias = __float2half2_rn(1032.f);
+            const uint32_t wv[4] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w};
 #pragma unroll
-        for (int b = 0; b < 2; b++) {
-            const uint16_t sb = (uint16_t)(b ? raw.sc >> 16 : raw.sc & 0xffff);
-            const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
-            if (WT == W_Q4_0) {
-                // byte j holds element j (low nibble) and element j + 16 (high nibble)
-                const __half2 bias = __float2half2_rn(1032.f);
-                const uint4 w = raw.w[b];
-                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+            for (int i = 0; i < 4; i++) {
+                const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140);   // bytes 4i, 4i+1 -> the two halves
+                const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342);   // bytes 4i+2, 4i+3
+                o[2 * i] = h2u(__hmul2(codes_to_half2(t01 & 0x000F000Fu, bias), d2));
+                o[2 * i + 1] = h2u(__hmul2(codes_to_half2(t23 & 0x000F000Fu, bias), d2));
+                o[8 + 2 * i] = h2u(__hmul2(codes_to_half2((t01 >> 4) & 0x000F000Fu, bias), d2));
+                o[9 + 2 * i] = h2u(__hmul2(codes_to_half2((t23 >> 4) & 0x000F000Fu, bias), d2));
+            }
+        } else {
+            // int8 codes: flipping the sign bit gives code + 128 in 0..255
+            const __half2 bias = __float2half2_rn(1152.f);
+            const uint32_t wv[8] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w,
+                                    raw.w[1].x, raw.w[1].y, raw.w[1].z, raw.w[1].w};
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140);   // bytes 4i, 4i+1 -> the two halves
-                    const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342);   // bytes 4i+2, 4i+3
-                    h[16 * b + 2 * i] = h2u(__hmul2(codes_to_half2(t01 & 0x000F000Fu, bias), d2));
-                    h[16 * b + 2 * i + 1] = h2u(__hmul2(codes_to_half2(t23 & 0x000F000Fu, bias), d2));
-                    h[16 * b + 8 + 2 * i] = h2u(__hmul2(codes_to_half2((t01 >> 4) & 0x000F000Fu, bias), d2));
-                    h[16 * b + 9 + 2 * i] = h2u(__hmul2(codes_to_half2((t23 >> 4) & 0x000F000Fu, bias), d2));
-                }
-            } else {
-                // int8 codes: flipping the sign bit gives code + 128 in 0..255
-                const __half2 bias = __float2half2_rn(1152.f);
-                const uint4 lo = raw.w[2 * b], hi = raw.w[2 * b + 1];
-                const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140) ^ 0x00800080u;
-                    const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342) ^ 0x00800080u;
-                    h[16 * b + 2 * i] = h2u(__hmul2(codes_to_half2(t01, bias), d2));
-                    h[16 * b + 2 * i + 1] = h2u(__hmul2(codes_to_half2(t23, bias), d2));
-                }
+            for (int i = 0; i < 8; i++) {
+                const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140) ^ 0x00800080u;
+                const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342) ^ 0x00800080u;
+                o[2 * i] = h2u(__hmul2(codes_to_half2(t01, bias), d2));
+                o[2 * i + 1] = h2u(__hmul2(codes_to_half2(t23, bias), d2));
             }
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; j++) h[j] = 0u;
+        for (int j = 0; j < 16; j++) o[j] = 0u;
     }
 #pragma unroll
-    for (int c = 0; c < 8; c++)
-        *reinterpret_cast<uint4 *>(tile + sw128(r, c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+    for (int c = 0; c < 4; c++)
+        *reinterpret_cast<uint4 *>(tile + sw128(r, 4 * h + c)) =
+            make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 
 template <int WT, int BN>
 __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__ QgemmArgs a)
 {
+    constexpr int ST = qg_stages(BN);
     constexpr uint32_t B_BYTES = BN * 128;
     constexpr uint32_t STAGE = QG_A_BYTES + B_BYTES;
     constexpr int TCOLS = BN < 32 ? 32 : BN;   // TMEM columns: a power of two >= 32
@@ -183,28 +187,29 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     // 1024-byte alignment for the swizzled tiles
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + QG_STAGES * STAGE);
-    uint64_t *empty = full + QG_STAGES;
-    uint64_t *done = empty + QG_STAGES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + ST * STAGE);
+    uint64_t *empty = full + ST;
+    uint64_t *done = empty + ST;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    int *commits = const_cast<int *>(abort_s) + 1;   // [QG_STAGES] commits issued to each empty barrier
+    int *commits = const_cast<int *>(abort_s) + 1;   // [ST] commits issued to each empty barrier
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * QG_M, t0 = blockIdx.y * BN;
+    const int t0 = blockIdx.x * BN, m0 = blockIdx.y * QG_M, z = blockIdx.z;
     const int ksteps = a.n / QG_K;
+    const int kbeg = z * a.kper, nk = max(0, min(ksteps, kbeg + a.kper) - kbeg);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < QG_STAGES; s++) {
+        for (int s = 0; s < ST; s++) {
             mbar_init(&full[s], QG_PROD);
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
         *abort_s = 0;
-        for (int s = 0; s < QG_STAGES; s++) commits[s] = 0;
+        for (int s = 0; s < ST; s++) commits[s] = 0;
         fence_barrier_init();
     }
-    if (warp == 4) {   // TMEM allocation (warp-wide)
+    if (warp == QG_MMA_WARP) {   // TMEM allocation (warp-wide)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TCOLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -214,13 +219,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == QG_MMA_WARP) {
         // ---------------- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(QG_M, BN);
-            for (int kb = 0; kb < ksteps; kb++) {
-                const int s = kb % QG_STAGES;
-                const uint32_t ph = (uint32_t)(kb / QG_STAGES) & 1u;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % ST;
+                const uint32_t ph = (uint32_t)(kb / ST) & 1u;
                 bool ok = false;
                 for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
                     if (mbar_try_wait(&full[s], ph)) { ok = true; break; }
@@ -254,21 +259,21 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
                          ::"r"(smem_u32(done)) : "memory");
         }
     } else {
-        // ---------------- producers
-        const int p = threadIdx.x, row = m0 + p;
+        // ---------------- producers: thread p owns block p & 1 of row p >> 1
+        const int p = threadIdx.x, r = p >> 1, h = p & 1, row = m0 + r;
         const bool valid = row < a.d;
-        RawRow raw[QG_PF];
+        RawBlk rb[QG_PF];
 #pragma unroll
         for (int j = 0; j < QG_PF; j++)
-            if (valid && j < ksteps) fetch_row<WT>(a, row, j, raw[j]);
+            if (valid && j < nk) fetch_blk<WT>(a, row, kbeg + j, h, rb[j]);
         bool stop = false;
-        for (int kb0 = 0; kb0 < ksteps && !stop; kb0 += QG_PF) {
+        for (int kb0 = 0; kb0 < nk && !stop; kb0 += QG_PF) {
 #pragma unroll
             for (int j = 0; j < QG_PF; j++) {
                 const int kb = kb0 + j;
-                if (kb >= ksteps || stop) break;
-                const int s = kb % QG_STAGES;
-                const uint32_t ph = (uint32_t)(kb / QG_STAGES) & 1u;
+                if (kb >= nk || stop) break;
+                const int s = kb % ST;
+                const uint32_t ph = (uint32_t)(kb / ST) & 1u;
                 bool ok = false;
                 for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
                     if (mbar_try_wait(&empty[s], ph ^ 1u)) { ok = true; break; }
@@ -285,15 +290,17 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
                 // the BN activation rows of this K slice: one bulk copy of
                 // pre-swizzled rows (the tensor cores read them through the
                 // async proxy, like the copy writes them)
-                if (p == 0) bulk_g2s_keep(sb, a.x + ((size_t)kb * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
-                dequant_row<WT>(raw[j], valid, sa, p);
-                if (valid && kb + QG_PF < ksteps) fetch_row<WT>(a, row, kb + QG_PF, raw[j]);
+                if (p == 0)
+                    bulk_g2s_keep(sb, a.x + ((size_t)(kbeg + kb) * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
+                dequant_blk<WT>(rb[j], valid, sa, r, h);
+                if (valid && kb + QG_PF < nk) fetch_blk<WT>(a, row, kbeg + kb + QG_PF, h, rb[j]);
                 fence_proxy_async_smem();   // the generic-proxy weight writes, before the tensor cores read them
                 if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
                 else mbar_arrive(&full[s]);
             }
         }
-        // ---------------- epilogue: TMEM lanes 32w..32w+31 are rows m0 + 32w + lane
+        // ---------------- epilogue: TMEM lanes 32q..32q+31 are rows m0 + 32q + lane;
+        // warps q and q + 4 take the two halves of the columns
         bool ok = false;
         for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
             if (mbar_try_wait(done, 0)) { ok = true; break; }
@@ -301,26 +308,27 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
         }
         if (!ok && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_FULL);
         tc_fence_after();
-        if (ok && !*abort_s) {
-            const int row = m0 + warp * 32 + lane;
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+        if (ok && !*abort_s && nk > 0) {
+            const int q = warp & 3, half = warp >> 2;
+            const int orow = m0 + q * 32 + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+            float *out = a.splits > 1 ? a.ws + (size_t)z * a.T * a.d : a.y;
+            const bool acc = a.splits == 1 && a.accumulate;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t v[16];
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-                             "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+            for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 8) {
+                uint32_t v[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                               "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-                               "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                               "=r"(v[7])
                              : "r"(taddr + (uint32_t)c0));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (row < a.d) {
+                if (orow < a.d) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
+                    for (int j = 0; j < 8; j++) {
                         const int tok = t0 + c0 + j;
                         if (tok < a.T) {
-                            float *yp = a.y + (size_t)tok * a.d + row;
-                            *yp = a.accumulate ? *yp + __uint_as_float(v[j]) : __uint_as_float(v[j]);
+                            float *yp = out + (size_t)tok * a.d + orow;
+                            *yp = acc ? *yp + __uint_as_float(v[j]) : __uint_as_float(v[j]);
                         }
                     }
                 }
@@ -329,16 +337,16 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == QG_MMA_WARP) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
     }
     if (threadIdx.x == 0) {
         // a commit's arrive lands when its MMAs complete: wait for each empty
         // barrier's last committed phase before retiring the barriers
-        for (int s = 0; s < QG_STAGES; s++)
+        for (int s = 0; s < ST; s++)
             if (commits[s] > 0) mbar_wait_bounded(&empty[s], (uint32_t)(commits[s] - 1) & 1u, nullptr, 0);
-        for (int s = 0; s < QG_STAGES; s++) {
+        for (int s = 0; s < ST; s++) {
             mbar_inval(&full[s]);
             mbar_inval(&empty[s]);
         }
@@ -346,29 +354,39 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     }
 }
 
+// y (=, or +=) the sum of the K splits' partials, in split order.
+__global__ void k_splitk_sum(const float *__restrict__ ws, int splits, long long count, float *__restrict__ y,
+                             int accumulate)
+{
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count;
+         i += (long long)gridDim.x * blockDim.x) {
+        float p = 0.f;
+        for (int z = 0; z < splits; z++) p += ws[(size_t)z * count + i];
+        y[i] = accumulate ? y[i] + p : p;
+    }
+}
+
 // x[T][n] fp32 -> fp16 in the order the kernel's bulk copies take: K slice
 // major ([n/64][Tpad][64]), each row's eight 16-byte chunks permuted as the
 // 128-byte swizzle places them (chunk c of token t at c ^ (t & 7); a CTA's
-// first token is a multiple of 8), zeros for tokens t >= T.
+// first token is a multiple of 8).  Rows t >= T are left as they are.
 __global__ void k_x16_swizzled(const float *__restrict__ x, __half *__restrict__ y, int T, int Tpad, int n)
 {
-    const long long total = (long long)(n / QG_K) * Tpad * 8;
+    const long long total = (long long)(n / QG_K) * T * 8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const int c = (int)(i & 7);
         const long long r = i >> 3;
-        const int tok = (int)(r % Tpad), kb = (int)(r / Tpad);
-        uint32_t h[4] = {0u, 0u, 0u, 0u};
-        if (tok < T) {
-            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)tok * n + (size_t)kb * QG_K + c * 8);
-            const float4 v0 = src[0], v1 = src[1];
-            const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const int tok = (int)(r % T), kb = (int)(r / T);
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)tok * n + (size_t)kb * QG_K + c * 8);
+        const float4 v0 = src[0], v1 = src[1];
+        const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t h[4];
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                h[j] = (uint32_t)__half_as_ushort(__float2half_rn(f[2 * j])) |
-                       ((uint32_t)__half_as_ushort(__float2half_rn(f[2 * j + 1])) << 16);
-        }
-        *reinterpret_cast<uint4 *>(y + (r * 8 + (c ^ (tok & 7))) * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+        for (int j = 0; j < 4; j++)
+            h[j] = (uint32_t)__half_as_ushort(__float2half_rn(f[2 * j])) |
+                   ((uint32_t)__half_as_ushort(__float2half_rn(f[2 * j + 1])) << 16);
+        *reinterpret_cast<uint4 *>(y + x16_index(kb * QG_K + c * 8, tok, Tpad)) = make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
@@ -390,17 +408,85 @@ size_t qgemm_x16_bytes(int n, int T)
 size_t qgemm_smem_bytes(int bn)
 {
     // alignment slack, stages, barriers, TMEM slot, abort flag, commit counts
-    return 1024 + (size_t)QG_STAGES * (QG_A_BYTES + (size_t)bn * 128) + (2 * QG_STAGES + 1) * 8 + 8 + 4 * QG_STAGES;
+    const int st = qg_stages(bn);
+    return 1024 + (size_t)st * (QG_A_BYTES + (size_t)bn * 128) + (2 * st + 1) * 8 + 8 + 4 * st;
+}
+
+template <int WT, int BN>
+static cudaError_t prepare_t(int *per_sm)
+{
+    const size_t smem = qgemm_smem_bytes(BN);
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm<WT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_qgemm<WT, BN>, QG_THREADS, smem);
+}
+
+template <int WT>
+static cudaError_t prepare_bn(int bn, int *per_sm)
+{
+    switch (bn) {
+    case 256: return prepare_t<WT, 256>(per_sm);
+    case 128: return prepare_t<WT, 128>(per_sm);
+    case 64: return prepare_t<WT, 64>(per_sm);
+    case 32: return prepare_t<WT, 32>(per_sm);
+    default: return prepare_t<WT, 16>(per_sm);
+    }
+}
+
+// CTAs of one kernel instance resident per SM (shared memory and registers),
+// queried once per device and instance; the dynamic shared-memory limit is
+// raised on the way.
+static int resident_per_sm(int type, int bn)
+{
+    static int cache[2][5][8] = {};   // [type][bn][device], 0 = not queried
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int ti = type == W_Q4_0 ? 0 : 1;
+    const int bi = bn == 256 ? 0 : bn == 128 ? 1 : bn == 64 ? 2 : bn == 32 ? 3 : 4;
+    int &c = cache[ti][bi][dev & 7];
+    if (c == 0) {
+        int n = 0;
+        const cudaError_t e = type == W_Q4_0 ? prepare_bn<W_Q4_0>(bn, &n) : prepare_bn<W_Q8_0>(bn, &n);
+        c = (e == cudaSuccess && n > 0) ? n : 1;
+    }
+    return c;
+}
+
+// K splits for a product: when the (N tile, M tile) grid leaves SMs idle or
+// ends in a partial wave, splitting K gives every SM work.  The estimate
+// weighs waves of K slices against the partials' extra traffic.
+static int pick_splits(int type, int n, int d, int T)
+{
+    const int bn = pick_bn(T);
+    const int ksteps = n / QG_K;
+    const long long tiles = (long long)cdiv(d, QG_M) * cdiv(T, bn);
+    const long long slots = 148LL * resident_per_sm(type, bn);
+    const double t_k = 0.4e-6 * std::max(bn, 64) / 256.0 + 0.05e-6;   // seconds per K slice of one CTA
+    int best = 1;
+    double best_t = 1e30;
+    for (int s = 1; s <= QG_MAX_SPLITS && (s == 1 || ksteps / s >= 4); s++) {
+        const int kper = cdiv(ksteps, s);
+        if (cdiv(ksteps, kper) != s) continue;   // every split gets work
+        const double waves = (double)((tiles * s + slots - 1) / slots);
+        const double t = waves * kper * t_k + (s > 1 ? 8.0 * s * T * (double)d / 5e12 : 0.0);
+        if (t < best_t * 0.97) { best_t = t; best = s; }
+    }
+    return best;
+}
+
+size_t qgemm_workspace_bytes(const WeightLayout &L, int T)
+{
+    if (T <= 0 || !qgemm_supported(L)) return 0;
+    const int s = pick_splits(L.type, L.n, L.d, T);
+    return s > 1 ? (size_t)s * T * L.d * 4 : 0;
 }
 
 template <int WT, int BN>
 static cudaError_t launch_t(const QgemmArgs &a, cudaStream_t st)
 {
-    const size_t smem = qgemm_smem_bytes(BN);
-    cudaError_t e = cudaFuncSetAttribute(k_qgemm<WT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e) return e;
-    dim3 grid(cdiv(a.d, QG_M), cdiv(a.T, BN));
-    k_qgemm<WT, BN><<<grid, QG_THREADS, smem, st>>>(a);
+    resident_per_sm(WT, BN);   // raises the kernel's shared-memory limit once
+    dim3 grid(cdiv(a.T, BN), cdiv(a.d, QG_M), a.splits);
+    k_qgemm<WT, BN><<<grid, QG_THREADS, qgemm_smem_bytes(BN), st>>>(a);
     return cudaGetLastError();
 }
 
@@ -426,13 +512,13 @@ cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t s
     if (T <= 0) return cudaSuccess;
     if (n % QG_K) return cudaErrorInvalidValue;
     const int Tpad = qgemm_tpad(T);
-    const long long chunks = (long long)(n / QG_K) * Tpad * 8;
+    const long long chunks = (long long)(n / QG_K) * T * 8;
     k_x16_swizzled<<<(int)std::min<long long>((chunks + 255) / 256, 148LL * 16), 256, 0, st>>>(x, x16, T, Tpad, n);
     return cudaGetLastError();
 }
 
 cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
-                             bool accumulate, int *err, cudaStream_t st)
+                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st)
 {
     if (T <= 0) return cudaSuccess;
     if (!qgemm_supported(L)) return cudaErrorInvalidValue;
@@ -452,18 +538,29 @@ cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __ha
     a.Tpad = qgemm_tpad(T);
     a.accumulate = accumulate ? 1 : 0;
     a.err = err;
+    const int ksteps = L.n / QG_K;
+    int splits = pick_splits(L.type, L.n, L.d, T);
+    if (splits > 1 && (!ws || ws_bytes < (size_t)splits * T * L.d * 4)) splits = 1;   // no room: one pass over K
+    a.splits = splits;
+    a.kper = cdiv(ksteps, splits);
+    a.ws = ws;
     const int bn = pick_bn(T);
-    return L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
+    cudaError_t e = L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
+    if (e || splits == 1) return e;
+    const long long count = (long long)T * L.d;
+    k_splitk_sum<<<(int)std::min<long long>((count + 255) / 256, 148LL * 8), 256, 0, st>>>(ws, splits, count, y,
+                                                                                          a.accumulate);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
-                         int *err, cudaStream_t st)
+                         float *ws, size_t ws_bytes, int *err, cudaStream_t st)
 {
     if (T <= 0) return cudaSuccess;
     if (!qgemm_supported(L)) return cudaErrorInvalidValue;
     cudaError_t e = launch_x16(x, x16, T, L.n, st);
     if (e) return e;
-    return launch_qgemm_x16(L, w, x16, y, T, false, err, st);
+    return launch_qgemm_x16(L, w, x16, y, T, false, ws, ws_bytes, err, st);
 }
 
 } // namespace cats

@@ -27,14 +27,20 @@ __host__ __device__ inline size_t x16_index(int k, int t, int Tpad)
 // x[T][n] fp32 (16-byte aligned rows) -> x16.
 cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t st);
 
+// Bytes of the K-split workspace a product of L at T tokens uses (0 when it
+// runs as one pass over K).  Deterministic in (L, T) on a given GPU.
+size_t qgemm_workspace_bytes(const WeightLayout &L, int T);
+
 // Y[T][d] (=, or += when accumulate) X[T][n] * W[d][n]^T with fp16 operands
-// and fp32 accumulation, X given as x16.
+// and fp32 accumulation, X given as x16.  ws (ws_bytes) holds the K-split
+// partials; with less room than qgemm_workspace_bytes the product runs as
+// one pass over K.
 cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
-                             bool accumulate, int *err, cudaStream_t st);
+                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st);
 
 // The same from fp32 x (converted into the x16 scratch, qgemm_x16_bytes, first).
 cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
-                         int *err, cudaStream_t st);
+                         float *ws, size_t ws_bytes, int *err, cudaStream_t st);
 
 size_t qgemm_smem_bytes(int bn);
 

@@ -147,6 +147,18 @@ class GpuLLM:
         """Enqueue one batched step of the batch set last on the model's stream."""
         _lib.check(self.lib.cats_gpu_llm_batch_enqueue(self.h), "batch_enqueue")
 
+    def batch_enqueue_decode(self, steps):
+        """Enqueue `steps` greedy steps of the batch set last (one token per sequence)."""
+        _lib.check(self.lib.cats_gpu_llm_batch_enqueue_decode(self.h, steps), "batch_enqueue_decode")
+
+    def time_product(self, kind, T, reps=2):
+        """(ms, FLOPs, weight bytes) per launch of one batched product kind at
+        T tokens: 0 qkv, 1 wo, 2 w13, 3 w2, 4 classifier."""
+        ms, fl, wb = C.c_float(), C.c_double(), C.c_double()
+        _lib.check(self.lib.cats_gpu_llm_time_product(self.h, kind, T, reps, C.byref(ms), C.byref(fl), C.byref(wb)),
+                   "time_product")
+        return ms.value, fl.value, wb.value
+
     def set_engine(self, engine):
         """ENGINE_PERSISTENT (default): one cooperative kernel runs whole tokens;
         ENGINE_GRAPH: a CUDA graph of per-phase kernels."""

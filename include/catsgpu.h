@@ -188,7 +188,12 @@ int cats_gpu_llm_trace_step(cats_gpu_llm *m, int token, int pos, unsigned long l
  *   sequence per step, replayed from a captured graph with no host round
  *   trip; tokens_host (may be NULL) receives [steps][n] ids.
  * cats_gpu_llm_batch_set / _batch_enqueue: upload a batch, then enqueue one
- *   step of it on the model's stream (asynchronous, for timing). */
+ *   step of it on the model's stream (asynchronous, for timing).
+ * cats_gpu_llm_batch_enqueue_decode: `steps` greedy steps from a batch of
+ *   one token per sequence set last (the loop of _generate_batch, enqueued).
+ * cats_gpu_llm_time_product: device time of one kind of batched product
+ *   (0 qkv, 1 wo, 2 w13, 3 w2, 4 classifier) at T tokens, `reps` passes over
+ *   the layers back to back: ms, FLOPs (2*T*n*d) and weight bytes per launch. */
 int cats_gpu_llm_batch_reserve(cats_gpu_llm *m, int max_tokens, int n_seqs);
 int cats_gpu_llm_forward_batch(cats_gpu_llm *m, const int *tokens, const int *pos, const int *seqs, int T,
                                int *next_host, float *logits_host);
@@ -196,6 +201,9 @@ int cats_gpu_llm_generate_batch(cats_gpu_llm *m, const int *tokens, const int *p
                                 int *tokens_host);
 int cats_gpu_llm_batch_set(cats_gpu_llm *m, const int *tokens, const int *pos, const int *seqs, int T);
 int cats_gpu_llm_batch_enqueue(cats_gpu_llm *m);
+int cats_gpu_llm_batch_enqueue_decode(cats_gpu_llm *m, int steps);
+int cats_gpu_llm_time_product(cats_gpu_llm *m, int kind, int T, int reps, float *ms_per_launch,
+                              double *flop_per_launch, double *weight_bytes_per_launch);
 /* Asynchronous form for timing: enqueue `steps` greedy steps on the model's stream. */
 int cats_gpu_llm_enqueue(cats_gpu_llm *m, int steps);
 int cats_gpu_llm_set_position(cats_gpu_llm *m, int token, int pos);

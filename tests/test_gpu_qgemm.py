@@ -27,9 +27,11 @@ def _case(orc, t, n, d, T, seed):
 
 
 # (n, d, T): full 128 x 256 tiles; ragged rows and tokens; a partial last
-# 64-block segment (11008 = 5 x 2048 + 768); the smallest shapes
+# 64-block segment (11008 = 5 x 2048 + 768); the smallest shapes; grids small
+# enough that K is split across CTAs (long K, few rows: 16 splits; the 7B w2
+# shape at batch 16)
 SHAPES = [(4096, 4096, 512), (4096, 1000, 16), (11008, 4096, 100), (64, 128, 1), (8192, 256, 300),
-          (2048, 11008, 33), (128, 17, 7)]
+          (2048, 11008, 33), (128, 17, 7), (28672, 256, 16), (11008, 4096, 16)]
 
 
 @pytest.mark.parametrize("t", [Q4_0, Q8_0])

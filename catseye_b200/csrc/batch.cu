@@ -12,7 +12,7 @@
 // reference's fp32-activation binding (matmul_q4_0 with quantize_null,
 // :880-914, :2593-2595) up to fp16 rounding of the operands.
 //
-// Per layer (the x16 operand is qgemm's swizzled fp16 layout, x16_index):
+// Per layer (the x16 operand is qgemm's swizzled fp16 layout, x16_chunk):
 //   k_rmsnorm_x16     rmsnorm(x) -> x16                               (:1655, 684-698)
 //   qgemm [wq;wk;wv]  -> y
 //   k_rope_kv         RoPE on q and k; k and v into the cache          (:1657-1674, 1597-1620)
@@ -54,11 +54,6 @@ __global__ void k_embed(const BatchTok *__restrict__ bt, const float *__restrict
     for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = ok ? __ldg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-__device__ __forceinline__ uint32_t pack_half2(float a, float b)
-{
-    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
-}
-
 // rmsnorm (llm/catseye_llm.h:684-698: ss = mean(x^2) + 1e-5, o = w * (x / sqrt(ss)))
 // of token t's row, written as fp16 into the x16 operand.  One CTA per token.
 __global__ void __launch_bounds__(256) k_rmsnorm_x16(const float *__restrict__ x, const float *__restrict__ w,
@@ -84,15 +79,13 @@ __global__ void __launch_bounds__(256) k_rmsnorm_x16(const float *__restrict__ x
     tot = tot / (float)n + 1e-5f;
     const float sc = 1.f / sqrtf(tot);
     const float4 *wr = reinterpret_cast<const float4 *>(w);
-    for (int c = tid; c < n / 8; c += blockDim.x) {
-        const float4 a0 = xr[2 * c], a1 = xr[2 * c + 1];
-        const float4 w0 = __ldg(wr + 2 * c), w1 = __ldg(wr + 2 * c + 1);
-        uint4 h;
-        h.x = pack_half2(w0.x * (sc * a0.x), w0.y * (sc * a0.y));
-        h.y = pack_half2(w0.z * (sc * a0.z), w0.w * (sc * a0.w));
-        h.z = pack_half2(w1.x * (sc * a1.x), w1.y * (sc * a1.y));
-        h.w = pack_half2(w1.z * (sc * a1.z), w1.w * (sc * a1.w));
-        *reinterpret_cast<uint4 *>(x16 + x16_index(8 * c, t, Tpad)) = h;
+    for (int ci = tid; ci < n / 8; ci += blockDim.x) {
+        const int kb = ci >> 3, c = ci & 7, o4 = (kb * 64 + x16_src_off(c)) / 4;
+        const float4 a0 = xr[o4], a1 = xr[o4 + 4];
+        const float4 w0 = __ldg(wr + o4), w1 = __ldg(wr + o4 + 4);
+        const float4 r0 = make_float4(w0.x * (sc * a0.x), w0.y * (sc * a0.y), w0.z * (sc * a0.z), w0.w * (sc * a0.w));
+        const float4 r1 = make_float4(w1.x * (sc * a1.x), w1.y * (sc * a1.y), w1.z * (sc * a1.z), w1.w * (sc * a1.w));
+        *reinterpret_cast<uint4 *>(x16 + x16_chunk(kb, c, t, Tpad)) = x16_pack(r0, r1);
     }
 }
 
@@ -132,21 +125,22 @@ __global__ void k_swiglu_x16(const float *__restrict__ y, int T, int hidden, __h
     const int cpr = hidden / 8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * cpr;
          i += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / cpr), k = 8 * (int)(i % cpr);
-        const float4 *src = reinterpret_cast<const float4 *>(y + (size_t)t * 2 * hidden + 2 * k);
+        const int t = (int)(i / cpr), ci = (int)(i % cpr), kb = ci >> 3, c = ci & 7;
+        const int e0 = kb * 64 + x16_src_off(c);
+        const float4 *row = reinterpret_cast<const float4 *>(y + (size_t)t * 2 * hidden);
         float h[8];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const float4 v = src[j];
-            h[2 * j] = v.x * (1.f / (1.f + expf(-v.x))) * v.y;
-            h[2 * j + 1] = v.z * (1.f / (1.f + expf(-v.z))) * v.w;
+        for (int run = 0; run < 2; run++) {
+            const float4 *src = row + (2 * (e0 + 16 * run)) / 4;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float4 v = src[j];
+                h[4 * run + 2 * j] = v.x * (1.f / (1.f + expf(-v.x))) * v.y;
+                h[4 * run + 2 * j + 1] = v.z * (1.f / (1.f + expf(-v.z))) * v.w;
+            }
         }
-        uint4 o;
-        o.x = pack_half2(h[0], h[1]);
-        o.y = pack_half2(h[2], h[3]);
-        o.z = pack_half2(h[4], h[5]);
-        o.w = pack_half2(h[6], h[7]);
-        *reinterpret_cast<uint4 *>(x16 + x16_index(k, t, Tpad)) = o;
+        *reinterpret_cast<uint4 *>(x16 + x16_chunk(kb, c, t, Tpad)) =
+            x16_pack(make_float4(h[0], h[1], h[2], h[3]), make_float4(h[4], h[5], h[6], h[7]));
     }
 }
 

@@ -12,14 +12,15 @@
 // N tiles fastest so the CTAs that share a weight tile run together and the
 // second reads it from L2.
 //  * Producers (warps 0-7): thread p owns block p & 1 of weight row p >> 1 in
-//    every K slice.  It loads the block's words from the weight's tile layout
-//    (the matvec's, so prefill and decode share one copy of the weights in
-//    HBM) four slices ahead into registers, dequantizes them to fp16 and
+//    every K slice.  It walks the block's words through the weight's tile
+//    layout (the matvec's, so prefill and decode share one copy of the
+//    weights in HBM) with a cursor, four slices ahead into registers,
+//    dequantizes them to fp16 in the x16 element order (qgemm.cuh) and
 //    stores them in the K-major 128-byte-swizzled form UMMA reads.  Thread 0
 //    also brings the stage's BN activation rows in with one bulk copy: the
 //    fp16 operand is stored K-slice-major and pre-swizzled (k_x16_swizzled,
-//    or a producing kernel writing x16_index order).  Then fence.proxy.async
-//    and an arrive on the stage's full barrier.
+//    or a producing kernel writing x16_chunk order).  Then fence.proxy.async
+//    and one arrive per warp on the stage's full barrier.
 //  * MMA warp (warp 8, one thread): four K=16 tcgen05.mma per stage into the
 //    TMEM accumulator; tcgen05.commit releases the stage when they complete.
 //  * Epilogue: after a final commit, warps w and w + 4 read TMEM lanes
@@ -98,10 +99,18 @@ struct RawBlk {
     uint32_t sc;    // fp16 scale in the low half
 };
 
-// Issue the loads of block h of weight row `row` at K slice kb (no use yet,
-// so several slices' loads are in flight while earlier ones are dequantized).
+// Where the next block a producer thread loads sits in the tile layout: its
+// code words, its scale, the distance from the low to the high Q8_0 plane,
+// and the K slices left in the current 64-unit segment.  Within a segment a
+// row's next block (two units on) is 32 bytes further, its scale 4 bytes.
+struct BlkCursor {
+    const uint8_t *codes, *scale;
+    uint32_t hi_off;
+    int left;
+};
+
 template <int WT>
-__device__ __forceinline__ void fetch_blk(const QgemmArgs &a, int row, int kb, int h, RawBlk &r)
+__device__ __forceinline__ void cursor_at(const QgemmArgs &a, int row, int h, int kb, BlkCursor &c)
 {
     const int u = 2 * kb + h, s = u / MV_SEG_UNITS, uu = u % MV_SEG_UNITS;
     const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
@@ -109,71 +118,80 @@ __device__ __forceinline__ void fetch_blk(const QgemmArgs &a, int row, int kb, i
     const uint8_t *ch = a.w + (size_t)t * a.tile_bytes + (size_t)s * a.full_chunk;
     const uint32_t sstride = (uint32_t)round_up((size_t)us * 2, 16);
     const uint32_t ub = WT == W_Q4_0 ? 16 : 32;
-    r.sc = __ldg(reinterpret_cast<const unsigned short *>(ch + (size_t)a.R * us * ub + rr * sstride + uu * 2));
-    if (WT == W_Q4_0) {
-        r.w[0] = __ldg(reinterpret_cast<const uint4 *>(ch + ((size_t)rr * us + uu) * 16));
-    } else {
-        r.w[0] = __ldg(reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2) * us + uu) * 16));
-        r.w[1] = __ldg(reinterpret_cast<const uint4 *>(ch + ((size_t)(rr * 2 + 1) * us + uu) * 16));
-    }
+    c.scale = ch + (size_t)a.R * us * ub + rr * sstride + uu * 2;
+    c.codes = ch + ((size_t)(WT == W_Q4_0 ? rr : 2 * rr) * us + uu) * 16;
+    c.hi_off = (uint32_t)us * 16;
+    c.left = us / 2 - (uu >> 1);
 }
 
-// Two small non-negative integers (bits 0-10 of each 16-bit half of t) as
-// an fp16 pair: OR-ing them into the mantissa of 1024.0 gives 1024 + v
-// exactly, and subtracting `bias` (1024 + the code offset) leaves the code.
-__device__ __forceinline__ __half2 codes_to_half2(uint32_t t, __half2 bias)
+// Issue the loads of the cursor's block, then step the cursor one K slice
+// (the loads are not used yet, so several slices are in flight at once).
+template <int WT>
+__device__ __forceinline__ void fetch_next(const QgemmArgs &a, int row, int h, int kb_next, BlkCursor &c, RawBlk &r)
 {
-    const uint32_t u = t | 0x64006400u;
-    return __hsub2(*reinterpret_cast<const __half2 *>(&u), bias);
+    r.sc = __ldg(reinterpret_cast<const unsigned short *>(c.scale));
+    r.w[0] = __ldg(reinterpret_cast<const uint4 *>(c.codes));
+    if (WT == W_Q8_0) r.w[1] = __ldg(reinterpret_cast<const uint4 *>(c.codes + c.hi_off));
+    if (--c.left > 0) {
+        c.codes += 32;
+        c.scale += 4;
+    } else if (2 * kb_next < a.units) {
+        cursor_at<WT>(a, row, h, kb_next, c);   // the next segment
+    }
 }
 
 __device__ __forceinline__ uint32_t h2u(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+__device__ __forceinline__ __half2 u2h(uint32_t v) { return *reinterpret_cast<__half2 *>(&v); }
 
-// Dequantize a fetched block into 32 fp16, stored swizzled as chunks
-// 4h .. 4h+3 of row r of the stage's weight tile (zeros for rows past d).
-// Value = code * d, the fp16 product of two exact fp16 operands, i.e. the
-// correctly rounded q*d.
+// Dequantize a fetched block into 32 fp16 in the x16 element order and
+// store them as chunks 4h .. 4h+3 of the stage's weight-tile row (byte
+// offsets `off`).  Value = code * d, computed as (code pair in fp16, exact)
+// times d: the correctly rounded q*d.
+//  Q4_0: byte j holds element j (low nibble) and j + 16 (high nibble).  For
+//  word i (bytes 4i..4i+3), masking bits 0-3 and 16-19 and OR-ing in the
+//  exponent of 1024 gives (1024 + e[4i], 1024 + e[4i+2]) exactly; bits 4-7
+//  and 20-23 give 1024 + 16 e[4i+16], 1024 + 16 e[4i+18], scaled back by
+//  an fma with 1/16 (exact); the word shifted by 8 gives the odd elements.
+//  Q8_0: the int8 codes of bytes (4i, 4i+2) and (4i+1, 4i+3) of each plane
+//  with the sign bit flipped are code + 128, exact as 1024 + that.
 template <int WT>
-__device__ __forceinline__ void dequant_blk(const RawBlk &raw, bool valid, uint8_t *tile, int r, int h)
+__device__ __forceinline__ void dequant_store(const RawBlk &raw, uint8_t *tile, const uint32_t (&off)[4])
 {
-    uint32_t o[16];   // 32 fp16, two per word: o[e/2] holds elements e, e+1
-    if (valid) {
-        const uint16_t sb = (uint16_t)(raw.sc & 0xffff);
-        const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
-        if (WT == W_Q4_0) {
-            // byte j holds element j (low nibble) and element j + 16 (high nibble)
-            const __half2 bias = __float2half2_rn(1032.f);
-            const uint32_t wv[4] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w};
+    const uint16_t sb = (uint16_t)(raw.sc & 0xffff);
+    const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
+    if (WT == W_Q4_0) {
+        const __half2 lo_bias = __float2half2_rn(1032.f);      // 1024 + the code offset 8
+        const __half2 sixteenth = __float2half2_rn(0.0625f);
+        const __half2 hi_bias = __float2half2_rn(-72.f);       // -(64 + 8)
+        const uint32_t wv[4] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w};
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140);   // bytes 4i, 4i+1 -> the two halves
-                const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342);   // bytes 4i+2, 4i+3
-                o[2 * i] = h2u(__hmul2(codes_to_half2(t01 & 0x000F000Fu, bias), d2));
-                o[2 * i + 1] = h2u(__hmul2(codes_to_half2(t23 & 0x000F000Fu, bias), d2));
-                o[8 + 2 * i] = h2u(__hmul2(codes_to_half2((t01 >> 4) & 0x000F000Fu, bias), d2));
-                o[9 + 2 * i] = h2u(__hmul2(codes_to_half2((t23 >> 4) & 0x000F000Fu, bias), d2));
-            }
-        } else {
-            // int8 codes: flipping the sign bit gives code + 128 in 0..255
-            const __half2 bias = __float2half2_rn(1152.f);
-            const uint32_t wv[8] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w,
-                                    raw.w[1].x, raw.w[1].y, raw.w[1].z, raw.w[1].w};
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const uint32_t t01 = __byte_perm(wv[i], 0, 0x4140) ^ 0x00800080u;
-                const uint32_t t23 = __byte_perm(wv[i], 0, 0x4342) ^ 0x00800080u;
-                o[2 * i] = h2u(__hmul2(codes_to_half2(t01, bias), d2));
-                o[2 * i + 1] = h2u(__hmul2(codes_to_half2(t23, bias), d2));
-            }
+        for (int i = 0; i < 4; i++) {
+            const uint32_t w = wv[i], w8 = w >> 8;
+            const uint32_t l02 = (w & 0x000F000Fu) | 0x64006400u, l13 = (w8 & 0x000F000Fu) | 0x64006400u;
+            const uint32_t g02 = (w & 0x00F000F0u) | 0x64006400u, g13 = (w8 & 0x00F000F0u) | 0x64006400u;
+            const uint4 o = make_uint4(h2u(__hmul2(__hsub2(u2h(l02), lo_bias), d2)),
+                                       h2u(__hmul2(__hsub2(u2h(l13), lo_bias), d2)),
+                                       h2u(__hmul2(__hfma2(u2h(g02), sixteenth, hi_bias), d2)),
+                                       h2u(__hmul2(__hfma2(u2h(g13), sixteenth, hi_bias), d2)));
+            *reinterpret_cast<uint4 *>(tile + off[i]) = o;
         }
     } else {
+        const __half2 bias = __float2half2_rn(1152.f);          // 1024 + 128
+        const uint32_t lo[4] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w};
+        const uint32_t hi[4] = {raw.w[1].x, raw.w[1].y, raw.w[1].z, raw.w[1].w};
 #pragma unroll
-        for (int j = 0; j < 16; j++) o[j] = 0u;
+        for (int i = 0; i < 4; i++) {
+            const uint32_t a02 = (__byte_perm(lo[i], 0, 0x4240) ^ 0x00800080u) | 0x64006400u;
+            const uint32_t a13 = (__byte_perm(lo[i], 0, 0x4341) ^ 0x00800080u) | 0x64006400u;
+            const uint32_t b02 = (__byte_perm(hi[i], 0, 0x4240) ^ 0x00800080u) | 0x64006400u;
+            const uint32_t b13 = (__byte_perm(hi[i], 0, 0x4341) ^ 0x00800080u) | 0x64006400u;
+            const uint4 o = make_uint4(h2u(__hmul2(__hsub2(u2h(a02), bias), d2)),
+                                       h2u(__hmul2(__hsub2(u2h(a13), bias), d2)),
+                                       h2u(__hmul2(__hsub2(u2h(b02), bias), d2)),
+                                       h2u(__hmul2(__hsub2(u2h(b13), bias), d2)));
+            *reinterpret_cast<uint4 *>(tile + off[i]) = o;
+        }
     }
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-        *reinterpret_cast<uint4 *>(tile + sw128(r, 4 * h + c)) =
-            make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 
 template <int WT, int BN>
@@ -201,7 +219,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; s++) {
-            mbar_init(&full[s], QG_PROD);
+            mbar_init(&full[s], QG_PROD / 32);   // one arrive per producer warp
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
@@ -261,19 +279,24 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     } else {
         // ---------------- producers: thread p owns block p & 1 of row p >> 1
         const int p = threadIdx.x, r = p >> 1, h = p & 1, row = m0 + r;
-        const bool valid = row < a.d;
+        const bool valid = row < a.d;   // rows past d are left unwritten: they reach only unstored outputs
+        uint32_t off[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) off[i] = sw128(r, 4 * h + i);
+        BlkCursor cur;
         RawBlk rb[QG_PF];
+        if (valid && nk > 0) cursor_at<WT>(a, row, h, kbeg, cur);
 #pragma unroll
         for (int j = 0; j < QG_PF; j++)
-            if (valid && j < nk) fetch_blk<WT>(a, row, kbeg + j, h, rb[j]);
+            if (valid && j < nk) fetch_next<WT>(a, row, h, kbeg + j + 1, cur, rb[j]);
+        int s = 0;
+        uint32_t ph = 0;
         bool stop = false;
         for (int kb0 = 0; kb0 < nk && !stop; kb0 += QG_PF) {
 #pragma unroll
             for (int j = 0; j < QG_PF; j++) {
                 const int kb = kb0 + j;
                 if (kb >= nk || stop) break;
-                const int s = kb % ST;
-                const uint32_t ph = (uint32_t)(kb / ST) & 1u;
                 bool ok = false;
                 for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
                     if (mbar_try_wait(&empty[s], ph ^ 1u)) { ok = true; break; }
@@ -292,11 +315,17 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
                 // async proxy, like the copy writes them)
                 if (p == 0)
                     bulk_g2s_keep(sb, a.x + ((size_t)(kbeg + kb) * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
-                dequant_blk<WT>(rb[j], valid, sa, r, h);
-                if (valid && kb + QG_PF < nk) fetch_blk<WT>(a, row, kbeg + kb + QG_PF, h, rb[j]);
+                if (valid) {
+                    dequant_store<WT>(rb[j], sa, off);
+                    if (kb + QG_PF < nk) fetch_next<WT>(a, row, h, kbeg + kb + QG_PF + 1, cur, rb[j]);
+                }
                 fence_proxy_async_smem();   // the generic-proxy weight writes, before the tensor cores read them
-                if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
-                else mbar_arrive(&full[s]);
+                __syncwarp();
+                if (lane == 0) {
+                    if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
+                    else mbar_arrive(&full[s]);
+                }
+                if (++s == ST) { s = 0; ph ^= 1u; }
             }
         }
         // ---------------- epilogue: TMEM lanes 32q..32q+31 are rows m0 + 32q + lane;
@@ -367,9 +396,10 @@ __global__ void k_splitk_sum(const float *__restrict__ ws, int splits, long long
 }
 
 // x[T][n] fp32 -> fp16 in the order the kernel's bulk copies take: K slice
-// major ([n/64][Tpad][64]), each row's eight 16-byte chunks permuted as the
-// 128-byte swizzle places them (chunk c of token t at c ^ (t & 7); a CTA's
-// first token is a multiple of 8).  Rows t >= T are left as they are.
+// major ([n/64][Tpad][64]), each row's eight 16-byte chunks in the x16
+// element order and permuted as the 128-byte swizzle places them (chunk c of
+// token t at c ^ (t & 7); a CTA's first token is a multiple of 8).  Rows
+// t >= T are left as they are.
 __global__ void k_x16_swizzled(const float *__restrict__ x, __half *__restrict__ y, int T, int Tpad, int n)
 {
     const long long total = (long long)(n / QG_K) * T * 8;
@@ -378,15 +408,8 @@ __global__ void k_x16_swizzled(const float *__restrict__ x, __half *__restrict__
         const int c = (int)(i & 7);
         const long long r = i >> 3;
         const int tok = (int)(r % T), kb = (int)(r / T);
-        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)tok * n + (size_t)kb * QG_K + c * 8);
-        const float4 v0 = src[0], v1 = src[1];
-        const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint32_t h[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-            h[j] = (uint32_t)__half_as_ushort(__float2half_rn(f[2 * j])) |
-                   ((uint32_t)__half_as_ushort(__float2half_rn(f[2 * j + 1])) << 16);
-        *reinterpret_cast<uint4 *>(y + x16_index(kb * QG_K + c * 8, tok, Tpad)) = make_uint4(h[0], h[1], h[2], h[3]);
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)tok * n + (size_t)kb * QG_K + x16_src_off(c));
+        *reinterpret_cast<uint4 *>(y + x16_chunk(kb, c, tok, Tpad)) = x16_pack(src[0], src[4]);
     }
 }
 

@@ -13,16 +13,34 @@ bool qgemm_supported(const WeightLayout &L);
 int qgemm_tpad(int T);
 size_t qgemm_x16_bytes(int n, int T);
 
-// The fp16 operand ("x16"): K-slice-major [n/64][Tpad][64], 16-byte chunk c
-// of token t's slice stored at chunk c ^ (t & 7) (the 128-byte swizzle the
-// tensor cores read, so one bulk copy brings a stage in).  Element k of token
-// t sits at x16_index(k, t, Tpad).  Rows t >= T are never stored from: their
-// contents only reach output columns that are not written.
-__host__ __device__ inline size_t x16_index(int k, int t, int Tpad)
+// The fp16 operand ("x16"): K-slice-major [n/64][Tpad][64] with token t's
+// eight 16-byte chunks of a slice stored at chunk c ^ (t & 7) (the 128-byte
+// swizzle the tensor cores read, so one bulk copy brings a stage in).
+// Chunk c holds, of the slice's 32-element block b = c >> 2 and i = c & 3,
+// the elements 4i, 4i+2, 4i+1, 4i+3, 4i+16, 4i+18, 4i+17, 4i+19: the order
+// in which the dequantization extracts a block's codes (the nibbles of
+// bytes 4i..4i+3 of a Q4_0 block), so weights and activations share one
+// permutation of K and the sums are unchanged.  Rows t >= T are never
+// stored from: their contents only reach output columns that are not written.
+__host__ __device__ inline size_t x16_chunk(int kb, int c, int t, int Tpad)
 {
-    const int kb = k >> 6, c = (k >> 3) & 7;
-    return (((size_t)kb * Tpad + t) * 8 + (size_t)(c ^ (t & 7))) * 8 + (k & 7);
+    return (((size_t)kb * Tpad + t) * 8 + (size_t)(c ^ (t & 7))) * 8;   // in halves
 }
+
+#ifdef __CUDACC__
+// Pack chunk c's eight elements, given a = elements 4i..4i+3 and b =
+// elements 4i+16..4i+19 of its block (i = c & 3), as the x16 order places them.
+__device__ __forceinline__ uint4 x16_pack(float4 a, float4 b)
+{
+    auto h2 = [](float lo, float hi) {
+        return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+    };
+    return make_uint4(h2(a.x, a.z), h2(a.y, a.w), h2(b.x, b.z), h2(b.y, b.w));
+}
+
+// Offset (elements) of chunk c's two source runs within its 64-wide slice.
+__host__ __device__ inline int x16_src_off(int c) { return (c >> 2) * 32 + (c & 3) * 4; }
+#endif
 
 // x[T][n] fp32 (16-byte aligned rows) -> x16.
 cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t st);

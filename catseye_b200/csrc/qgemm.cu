@@ -37,7 +37,9 @@ namespace cats {
 
 constexpr int QG_M = 128;
 constexpr int QG_K = 64;
-constexpr int QG_PF = 4;                     // K slices of weight words a producer has in flight
+// K slices of weight words a producer has in flight: deeper for small token
+// tiles, where the weight stream, not the tensor cores, sets the pace
+__host__ __device__ constexpr int qg_prefetch(int bn) { return bn <= 32 ? 8 : 4; }
 constexpr int QG_PROD = 256;                 // producer threads (8 warps): one block per K slice each
 constexpr int QG_THREADS = QG_PROD + 32;     // + the MMA warp
 constexpr int QG_MMA_WARP = QG_PROD / 32;
@@ -198,6 +200,7 @@ template <int WT, int BN>
 __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__ QgemmArgs a)
 {
     constexpr int ST = qg_stages(BN);
+    constexpr int QG_PF = qg_prefetch(BN);
     constexpr uint32_t B_BYTES = BN * 128;
     constexpr uint32_t STAGE = QG_A_BYTES + B_BYTES;
     constexpr int TCOLS = BN < 32 ? 32 : BN;   // TMEM columns: a power of two >= 32

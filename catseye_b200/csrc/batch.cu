@@ -408,6 +408,212 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_batch(const __grid_constant
     }
 }
 
+// ------------------------------------------------- attention on the tensor cores
+// The same causal attention for query blocks of head size 128 (prefill),
+// flash-attention style on the tensor cores (mma.sync m16n8k16, fp16
+// operands, fp32 accumulation): warp w takes block rows 16w..16w+15; per
+// chunk of MA_KC cache positions (staged as fp32 in shared memory by
+// cp.async, double-buffered) S = Q K^T / sqrt(128) with the causal mask, an
+// online softmax on the accumulators, then O += P V with P taken straight
+// from the S accumulators.  The rounding of q, k, p and v to fp16 adds
+// ~1e-4 relative to the attention output.
+constexpr int MA_HS = 128;
+constexpr int MA_KC = 32;
+constexpr int MA_THREADS = 128;
+constexpr int MA_SK = MA_HS + 8;   // K row stride (floats): 64-bit fragment loads conflict-free
+constexpr int MA_SV = MA_HS + 4;   // V row stride (floats): 32-bit fragment loads conflict-free
+
+__host__ __device__ constexpr size_t ma_smem_bytes() { return (size_t)2 * MA_KC * (MA_SK + MA_SV) * 4; }
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi)
+{
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+__global__ void __launch_bounds__(MA_THREADS) k_attn_mma(const __grid_constant__ AttnBatchArgs a)
+{
+    extern __shared__ __align__(16) float msm[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, cq = lane & 3;   // mma fragment coordinates
+    const int2 blk = a.blocks[blockIdx.x];
+    const int kvh = blockIdx.y;
+    const int nq = blk.y * a.kv_mul;
+    const int seq = a.tok[blk.x].seq;
+    const bool seq_ok = seq >= 0 && seq < a.n_seqs;
+    int maxpos = -1;
+    for (int r = 0; r < nq; r += a.kv_mul) maxpos = max(maxpos, a.tok[blk.x + r / a.kv_mul].pos);
+    maxpos = seq_ok ? min(maxpos, a.seq_len - 1) : -1;
+    const float *kbase = a.kc + (size_t)(seq_ok ? seq : 0) * a.seq_stride + a.layer_off + (size_t)kvh * MA_HS;
+    const float *vbase = a.vc + (size_t)(seq_ok ? seq : 0) * a.seq_stride + a.layer_off + (size_t)kvh * MA_HS;
+
+    // this thread's two block rows, g and g + 8 of the warp's 16
+    int lim[2], tokr[2], headr[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int r = 16 * warp + g + 8 * i;
+        lim[i] = -1;
+        tokr[i] = -1;
+        headr[i] = 0;
+        if (r < nq && seq_ok) {
+            tokr[i] = blk.x + r / a.kv_mul;
+            headr[i] = kvh * a.kv_mul + r % a.kv_mul;
+            const int p = a.tok[tokr[i]].pos;
+            lim[i] = (p >= 0 && p < a.seq_len) ? p : -1;
+        }
+    }
+    // Q fragments (A operand) for the 8 k-tiles of the head dimension
+    uint32_t qf[8][4];
+#pragma unroll
+    for (int kt = 0; kt < 8; kt++) {
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {        // columns 2c.. and 2c+8..
+#pragma unroll
+            for (int i = 0; i < 2; i++) {       // rows g, g + 8
+                float2 v = make_float2(0.f, 0.f);
+                if (tokr[i] >= 0)
+                    v = *reinterpret_cast<const float2 *>(a.q + (size_t)tokr[i] * a.q_dim + headr[i] * MA_HS +
+                                                         16 * kt + 8 * hh + 2 * cq);
+                qf[kt][2 * hh + i] = pack_f16x2(v.x, v.y);
+            }
+        }
+    }
+    const float scale = 1.f / sqrtf((float)MA_HS);
+    float o[16][4];
+#pragma unroll
+    for (int nt = 0; nt < 16; nt++) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+    const int nchunks = maxpos >= 0 ? maxpos / MA_KC + 1 : 0;
+    auto stage = [&](int ch, int buf) {
+        float *ks = msm + (size_t)buf * MA_KC * (MA_SK + MA_SV);
+        float *vs = ks + MA_KC * MA_SK;
+        const int p0 = ch * MA_KC;
+        // 2 x KC rows of 128 floats = KC * 64 16-byte pieces; rows past maxpos
+        // are zeros (their probabilities are 0, and 0 * stale data could be NaN)
+        for (int e = tid; e < MA_KC * 64; e += MA_THREADS) {
+            const int j = e >> 6, piece = e & 63, isv = piece >> 5, c4 = piece & 31;
+            float *dst = isv ? vs + j * MA_SV + 4 * c4 : ks + j * MA_SK + 4 * c4;
+            if (p0 + j > maxpos) {
+                *reinterpret_cast<float4 *>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+                continue;
+            }
+            cp_async16(dst, (isv ? vbase : kbase) + (size_t)(p0 + j) * a.kv_dim + 4 * c4);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (nchunks > 0) stage(0, 0);
+    for (int ch = 0; ch < nchunks; ch++) {
+        const int buf = ch & 1, p0 = ch * MA_KC;
+        if (ch + 1 < nchunks) {
+            stage(ch + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const float *ks = msm + (size_t)buf * MA_KC * (MA_SK + MA_SV);
+        const float *vs = ks + MA_KC * MA_SK;
+        // S = Q K^T over the chunk's 4 n-tiles of 8 positions
+        float sacc[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; nt++) {
+            sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+            const float *kr = ks + (8 * nt + g) * MA_SK + 2 * cq;
+#pragma unroll
+            for (int kt = 0; kt < 8; kt++) {
+                const float2 b0 = *reinterpret_cast<const float2 *>(kr + 16 * kt);
+                const float2 b1 = *reinterpret_cast<const float2 *>(kr + 16 * kt + 8);
+                mma_16816(sacc[nt], qf[kt][0], qf[kt][1], qf[kt][2], qf[kt][3], pack_f16x2(b0.x, b0.y),
+                          pack_f16x2(b1.x, b1.y));
+            }
+        }
+        // mask, scale, online softmax (rows g and g + 8: accumulator halves 0-1 and 2-3)
+        float alpha[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int p = p0 + 8 * nt + 2 * cq + e;
+                    float v = sacc[nt][2 * i + e] * scale;
+                    v = p <= lim[i] ? v : -INFINITY;
+                    sacc[nt][2 * i + e] = v;
+                    mx = fmaxf(mx, v);
+                }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(mrow[i], mx);
+            alpha[i] = mrow[i] == -INFINITY ? 0.f : expf(mrow[i] - mn);
+            float sum = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const float v = sacc[nt][2 * i + e];
+                    const float pv = v == -INFINITY ? 0.f : expf(v - mn);
+                    sacc[nt][2 * i + e] = pv;
+                    sum += pv;
+                }
+            lrow[i] = lrow[i] * alpha[i] + sum;   // this thread's columns; the quad is summed at the end
+            mrow[i] = mn;
+        }
+#pragma unroll
+        for (int nt = 0; nt < 16; nt++) {
+            o[nt][0] *= alpha[0];
+            o[nt][1] *= alpha[0];
+            o[nt][2] *= alpha[1];
+            o[nt][3] *= alpha[1];
+        }
+        // O += P V: P's A fragments are the S accumulators of n-tiles 2kt, 2kt+1
+#pragma unroll
+        for (int kt = 0; kt < 2; kt++) {
+            const uint32_t a0 = pack_f16x2(sacc[2 * kt][0], sacc[2 * kt][1]);
+            const uint32_t a1 = pack_f16x2(sacc[2 * kt][2], sacc[2 * kt][3]);
+            const uint32_t a2 = pack_f16x2(sacc[2 * kt + 1][0], sacc[2 * kt + 1][1]);
+            const uint32_t a3 = pack_f16x2(sacc[2 * kt + 1][2], sacc[2 * kt + 1][3]);
+            const float *vr = vs + (16 * kt + 2 * cq) * MA_SV + g;
+#pragma unroll
+            for (int nt = 0; nt < 16; nt++) {
+                const float *v = vr + 8 * nt;
+                mma_16816(o[nt], a0, a1, a2, a3, pack_f16x2(v[0], v[MA_SV]),
+                          pack_f16x2(v[8 * MA_SV], v[9 * MA_SV]));
+            }
+        }
+        __syncthreads();   // this buffer is restaged two chunks on
+    }
+    // normalise and store rows g, g + 8
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        float l = lrow[i];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        if (tokr[i] < 0) continue;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        float *dst = a.xb + (size_t)tokr[i] * a.q_dim + headr[i] * MA_HS + 2 * cq;
+#pragma unroll
+        for (int nt = 0; nt < 16; nt++)
+            *reinterpret_cast<float2 *>(dst + 8 * nt) = make_float2(o[nt][2 * i] * inv, o[nt][2 * i + 1] * inv);
+    }
+}
+
 // ------------------------------------------------------------------- host
 static int grid_for(long long items, int block)
 {
@@ -539,7 +745,7 @@ static int make_blocks(const LlmModel *m, const BatchTok *tok, int T, int2 *bloc
     return nb;
 }
 
-static cudaError_t launch_attn_batch(LlmModel *m, int l, int T, int nblocks, cudaStream_t st)
+static cudaError_t launch_attn_batch(LlmModel *m, int l, int nblocks, int max_rows, cudaStream_t st)
 {
     AttnBatchArgs a;
     const LlmConfig &c = m->c;
@@ -557,10 +763,17 @@ static cudaError_t launch_attn_batch(LlmModel *m, int l, int T, int nblocks, cud
     a.kv_mul = c.n_heads / c.n_kv_heads;
     a.seq_len = c.seq_len;
     a.n_seqs = m->n_seqs;
+    // blocks of 16 query rows or more (prefill) go to the tensor cores
+    if (a.hs == MA_HS && max_rows >= 16) {
+        const size_t smem = ma_smem_bytes();
+        cudaError_t e = cudaFuncSetAttribute(k_attn_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e) return e;
+        k_attn_mma<<<dim3(nblocks, m->kv_heads_loc), MA_THREADS, smem, st>>>(a);
+        return cudaGetLastError();
+    }
     const size_t smem = attn_smem_floats(a.hs) * 4;
     cudaError_t e = cudaFuncSetAttribute(k_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
-    (void)T;
     k_attn_batch<<<dim3(nblocks, m->kv_heads_loc), AT_THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }
@@ -598,7 +811,7 @@ cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int
                                                      (size_t)l * c.seq_len * m->kv_dim, m->q_dim, m->kv_dim,
                                                      m->head_size, c.seq_len, m->n_seqs, m->err);
         if ((e = cudaGetLastError())) return e;
-        if ((e = launch_attn_batch(m, l, T, nblocks, st))) return e;
+        if ((e = launch_attn_batch(m, l, nblocks, m->bt_max_rows, st))) return e;
         if ((e = launch_x16(m->bt_xb, m->bt_x16, T, m->q_dim, st))) return e;
         if ((e = residual_product(m, m->wo[l], T, st))) return e;
         k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_ffn + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad);
@@ -639,6 +852,9 @@ int llm_batch_set(LlmModel *m, const int *tokens, const int *pos, const int *seq
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) return E_CUDA;
     for (int t = 0; t < T; t++) m->bt_tok_host[t] = BatchTok{tokens[t], pos[t], seqs ? seqs[t] : 0, 0};
     const int nb = make_blocks(m, m->bt_tok_host, T, m->bt_blocks_host);
+    int most = 0;
+    for (int b = 0; b < nb; b++) most = std::max(most, m->bt_blocks_host[b].y);
+    m->bt_max_rows = most * (c.n_heads / c.n_kv_heads);
     if (cudaMemcpyAsync(m->bt_tok, m->bt_tok_host, (size_t)T * sizeof(BatchTok), cudaMemcpyHostToDevice, m->stream) ||
         cudaMemcpyAsync(m->bt_blocks, m->bt_blocks_host, (size_t)nb * sizeof(int2), cudaMemcpyHostToDevice,
                         m->stream) ||

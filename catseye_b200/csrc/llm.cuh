@@ -69,6 +69,7 @@ struct LlmModel {
     int bt_cap = 0;                       // tokens per batched step (0: not reserved)
     BatchTok *bt_tok = nullptr;           // device [cap]
     int2 *bt_blocks = nullptr;            // device [cap]: attention query blocks (first token, count)
+    int bt_max_rows = 0;                  // query rows of the largest block of the batch set last
     float *bt_x = nullptr, *bt_delta = nullptr, *bt_y = nullptr, *bt_q = nullptr, *bt_xb = nullptr;
     float *bt_lg = nullptr;               // classifier slices [tp][T][vocab_loc]
     float *bt_logits = nullptr;           // [T][vocab]

@@ -37,6 +37,13 @@ SIGNATURES = {
     "cats_gpu_quantize_q8": (None, [_vp, _vp, _i]),
     "cats_gpu_dequantize_q4_0": (_vp, [_vp, _vp, _i, _i]),
     "cats_gpu_dequantize_q8_0": (_vp, [_vp, _vp, _i, _i]),
+    "cats_gpu_matmul_q4_0_f32": (None, [_vp, _vp, _vp, _i, _i]),
+    "cats_gpu_matmul_q8_0_f32": (None, [_vp, _vp, _vp, _i, _i]),
+    "cats_gpu_matmul_q3_K_q8_K": (None, [_vp, _vp, _vp, _i, _i]),
+    "cats_gpu_matmul_q6_K_q8_K": (None, [_vp, _vp, _vp, _i, _i]),
+    "cats_gpu_quantize_q8_K": (None, [_vp, _vp, _i]),
+    "cats_gpu_dequantize_q3_K": (_vp, [_vp, _vp, _i, _i]),
+    "cats_gpu_dequantize_q6_K": (_vp, [_vp, _vp, _i, _i]),
     "cats_gpu_matvec_dev": (_i, [_vp, _vp, _vp, _i, _vp]),
     "cats_gpu_quantize_q8_dev": (_i, [_vp, _vp, _i, _i, _vp]),
     "cats_gpu_qgemm_dev": (_i, [_vp, _vp, _vp, _i, _vp]),

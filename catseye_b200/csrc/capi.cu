@@ -6,6 +6,7 @@
 // void drop-in signatures cannot return.
 #include "../../include/catsgpu.h"
 #include "conv.cuh"
+#include "kquant.cuh"
 #include "llm.cuh"
 #include "qgemm.cuh"
 #include "sgemm.cuh"
@@ -111,12 +112,13 @@ int check_device_error(const char *what)
 }
 
 bool type_ok(int t) { return t == CATS_TYPE_F32 || t == CATS_TYPE_Q4_0 || t == CATS_TYPE_Q8_0; }
+bool kquant(int t) { return t == CATS_TYPE_Q3_K || t == CATS_TYPE_Q6_K; }
 
 int validate_shape(int type, int n, int d)
 {
     if (n <= 0 || d <= 0) return CATS_ERR_ARG;
-    if (!type_ok(type)) return CATS_ERR_UNSUPPORTED;
-    if (type == CATS_TYPE_F32 ? (n % 4) : (n % 32)) return CATS_ERR_ARG;
+    if (!type_ok(type) && !kquant(type)) return CATS_ERR_UNSUPPORTED;
+    if (type == CATS_TYPE_F32 ? (n % 4) : kquant(type) ? (n % 256) : (n % 32)) return CATS_ERR_ARG;
     return CATS_OK;
 }
 
@@ -152,22 +154,30 @@ MatvecArgs args_for(const Reg &r)
     return a;
 }
 
-void matmul_host(int type, float *xout, void *x, void *w, int n, int d, const char *what)
+// x_f32: fp32 activations against quantized weights (the matmul_q4_0 binding)
+void matmul_host(int type, float *xout, void *x, void *w, int n, int d, const char *what, bool x_f32 = false)
 {
     if (!ensure_init()) return;
     if (!xout || !x || !w) { fail(CATS_ERR_ARG, what); return; }
     if (int rc = validate_shape(type, n, d)) { fail(rc, what); return; }
     Reg *r = lookup(w, type, n, d);
     if (!r) return;
-    const size_t xb = type == CATS_TYPE_F32 ? (size_t)n * 4 : (size_t)(n / 32) * 36;
+    const size_t xb = (type == CATS_TYPE_F32 || x_f32) ? (size_t)n * 4
+                      : kquant(type)                  ? (size_t)(n / 256) * 260
+                                                      : (size_t)(n / 32) * 36;
     if (grow(&g.d_x, &g.d_x_cap, xb) || grow((void **)&g.d_out, &g.d_out_cap, (size_t)d * 4)) return;
     if (check(cudaMemcpyAsync(g.d_x, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
-    MatvecArgs a = args_for(*r);
-    a.xmode = type == CATS_TYPE_F32 ? XM_F32 : XM_Q8_RAW;
-    a.x = g.d_x;
-    a.epi = EPI_STORE;
-    a.out = g.d_out;
-    if (check(launch_matvec(a, r->W.L.rpw, type, g.stream, false), what)) return;
+    if (kquant(type)) {
+        if (check(launch_matvec_kquant(type, g.d_out, (const uint8_t *)g.d_x, r->W.ptr, n, d, g.stream), what))
+            return;
+    } else {
+        MatvecArgs a = args_for(*r);
+        a.xmode = (type == CATS_TYPE_F32 || x_f32) ? XM_F32 : XM_Q8_RAW;
+        a.x = g.d_x;
+        a.epi = EPI_STORE;
+        a.out = g.d_out;
+        if (check(launch_matvec(a, r->W.L.rpw, type, g.stream, false), what)) return;
+    }
     if (check(cudaMemcpyAsync(xout, g.d_out, (size_t)d * 4, cudaMemcpyDeviceToHost, g.stream), what)) return;
     if (check(cudaStreamSynchronize(g.stream), what)) return;
     check_device_error(what);
@@ -247,10 +257,22 @@ int cats_gpu_register_weight(const void *w, int type, int n, int d)
         cats_gpu_unregister_weight(w);
     }
     const size_t bytes = gguf_row_bytes(type, n) * d;
-    uint8_t *stg = nullptr;
-    if (cudaMalloc(&stg, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
     Reg r;
     r.type = type; r.n = n; r.d = d;
+    if (kquant(type)) {
+        // K-quant weights keep the reference's row layout on the device
+        r.W.L.type = type;
+        r.W.L.n = n;
+        r.W.L.d = d;
+        r.W.L.total_bytes = bytes;
+        if (cudaMalloc(&r.W.ptr, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
+        int rc = check(cudaMemcpy(r.W.ptr, w, bytes, cudaMemcpyHostToDevice), "cats_gpu_register_weight");
+        if (rc) { cudaFree(r.W.ptr); return rc; }
+        g.weights[w] = r;
+        return CATS_OK;
+    }
+    uint8_t *stg = nullptr;
+    if (cudaMalloc(&stg, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
     // two rows per warp halves the activation reads per weight byte; use it
     // when there are enough 16-row tiles to give every SM two or more
     r.W.L = make_layout(type, n, d, d >= 2 * 16 * matvec_num_sms() ? 2 : 1);
@@ -287,6 +309,28 @@ void cats_gpu_matmul_q4_0_q8(float *xout, void *x, void *w, int n, int d)
 void cats_gpu_matmul_q8_0_q8(float *xout, void *x, void *w, int n, int d)
 { matmul_host(CATS_TYPE_Q8_0, xout, x, w, n, d, "cats_gpu_matmul_q8_0_q8"); }
 
+void cats_gpu_matmul_q4_0_f32(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_Q4_0, xout, x, w, n, d, "cats_gpu_matmul_q4_0_f32", true); }
+void cats_gpu_matmul_q8_0_f32(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_Q8_0, xout, x, w, n, d, "cats_gpu_matmul_q8_0_f32", true); }
+void cats_gpu_matmul_q3_K_q8_K(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_Q3_K, xout, x, w, n, d, "cats_gpu_matmul_q3_K_q8_K"); }
+void cats_gpu_matmul_q6_K_q8_K(float *xout, void *x, void *w, int n, int d)
+{ matmul_host(CATS_TYPE_Q6_K, xout, x, w, n, d, "cats_gpu_matmul_q6_K_q8_K"); }
+
+void cats_gpu_quantize_q8_K(int8_t *q, float *x, int n)
+{
+    const char *what = "cats_gpu_quantize_q8_K";
+    if (!ensure_init()) return;
+    if (!q || !x || n <= 0 || n % 256) { fail(CATS_ERR_ARG, what); return; }
+    const size_t xb = (size_t)n * 4, qb = (size_t)(n / 256) * 260;
+    if (grow(&g.d_x, &g.d_x_cap, xb) || grow((void **)&g.d_out, &g.d_out_cap, qb)) return;
+    if (check(cudaMemcpyAsync(g.d_x, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(launch_quantize_q8_K((uint8_t *)g.d_out, (const float *)g.d_x, n, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(q, g.d_out, qb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
 void cats_gpu_quantize_q8(int8_t *q, float *x, int n)
 {
     const char *what = "cats_gpu_quantize_q8";
@@ -303,12 +347,15 @@ void cats_gpu_quantize_q8(int8_t *q, float *x, int n)
 static void *dequant_host(int type, void *y, const void *x, int row, int n, const char *what)
 {
     if (!ensure_init()) return 0;
-    if (!y || !x || row < 0 || n <= 0 || n % 32) { fail(CATS_ERR_ARG, what); return 0; }
+    if (!y || !x || row < 0 || n <= 0 || n % (kquant(type) ? 256 : 32)) { fail(CATS_ERR_ARG, what); return 0; }
     const size_t rb = gguf_row_bytes(type, n);
     if (grow(&g.d_x, &g.d_x_cap, rb) || grow((void **)&g.d_out, &g.d_out_cap, (size_t)n * 4)) return 0;
     const uint8_t *src = static_cast<const uint8_t *>(x) + (size_t)row * rb;
     if (check(cudaMemcpyAsync(g.d_x, src, rb, cudaMemcpyHostToDevice, g.stream), what)) return 0;
-    if (check(launch_dequantize(type, g.d_out, (const uint8_t *)g.d_x, n, 1, g.stream), what)) return 0;
+    if (check(kquant(type) ? launch_dequantize_kquant(type, g.d_out, (const uint8_t *)g.d_x, n, 1, g.stream)
+                           : launch_dequantize(type, g.d_out, (const uint8_t *)g.d_x, n, 1, g.stream),
+              what))
+        return 0;
     if (check(cudaMemcpyAsync(y, g.d_out, (size_t)n * 4, cudaMemcpyDeviceToHost, g.stream), what)) return 0;
     check(cudaStreamSynchronize(g.stream), what);
     return 0;
@@ -318,6 +365,10 @@ void *cats_gpu_dequantize_q4_0(void *y, const void *x, int row, int n)
 { return dequant_host(CATS_TYPE_Q4_0, y, x, row, n, "cats_gpu_dequantize_q4_0"); }
 void *cats_gpu_dequantize_q8_0(void *y, const void *x, int row, int n)
 { return dequant_host(CATS_TYPE_Q8_0, y, x, row, n, "cats_gpu_dequantize_q8_0"); }
+void *cats_gpu_dequantize_q3_K(void *y, const void *x, int row, int n)
+{ return dequant_host(CATS_TYPE_Q3_K, y, x, row, n, "cats_gpu_dequantize_q3_K"); }
+void *cats_gpu_dequantize_q6_K(void *y, const void *x, int row, int n)
+{ return dequant_host(CATS_TYPE_Q6_K, y, x, row, n, "cats_gpu_dequantize_q6_K"); }
 
 int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q8, void *stream)
 {
@@ -327,10 +378,22 @@ int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q
     if (it == g.weights.end()) return fail(CATS_ERR_ARG, "cats_gpu_matvec_dev: weight not registered");
     if (!d_out || !d_x || ((uintptr_t)d_x % 16)) return fail(CATS_ERR_ARG, what);
     Reg &r = it->second;
+    if (x_is_q8 < 0 || x_is_q8 > 2) return fail(CATS_ERR_ARG, what);
     if (x_is_q8 && r.type == CATS_TYPE_F32) return fail(CATS_ERR_ARG, "cats_gpu_matvec_dev: F32 weight with Q8 input");
     cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    if (kquant(r.type)) {
+        if (x_is_q8 == 2) return fail(CATS_ERR_UNSUPPORTED, what);
+        const uint8_t *xq = static_cast<const uint8_t *>(d_x);
+        if (!x_is_q8) {   // quantize_q8_K into the library's scratch first
+            if (grow((void **)&g.d_out, &g.d_out_cap, (size_t)(r.n / 256) * 260)) return g.last_err;
+            if (check(launch_quantize_q8_K((uint8_t *)g.d_out, static_cast<const float *>(d_x), r.n, st), what))
+                return g.last_err;
+            xq = (const uint8_t *)g.d_out;
+        }
+        return check(launch_matvec_kquant(r.type, d_out, xq, r.W.ptr, r.n, r.d, st), what);
+    }
     MatvecArgs a = args_for(r);
-    a.xmode = r.type == CATS_TYPE_F32 ? XM_F32 : (x_is_q8 ? XM_Q8_RAW : XM_Q8_FROM_F32);
+    a.xmode = (r.type == CATS_TYPE_F32 || x_is_q8 == 2) ? XM_F32 : (x_is_q8 ? XM_Q8_RAW : XM_Q8_FROM_F32);
     a.x = d_x;
     a.epi = EPI_STORE;
     a.out = d_out;
@@ -382,8 +445,11 @@ int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mo
 int cats_gpu_dequantize_dev(int type, float *d_y, const void *d_w, int n, int rows, void *stream)
 {
     if (!ensure_init()) return g.last_err;
-    if (!d_y || !d_w || n <= 0 || n % 32 || rows <= 0 || !type_ok(type)) return fail(CATS_ERR_ARG, "cats_gpu_dequantize_dev");
-    return check(launch_dequantize(type, d_y, (const uint8_t *)d_w, n, rows, stream ? (cudaStream_t)stream : g.stream),
+    if (!d_y || !d_w || n <= 0 || rows <= 0 || (!type_ok(type) && !kquant(type)) || n % (kquant(type) ? 256 : 32))
+        return fail(CATS_ERR_ARG, "cats_gpu_dequantize_dev");
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    return check(kquant(type) ? launch_dequantize_kquant(type, d_y, (const uint8_t *)d_w, n, rows, st)
+                              : launch_dequantize(type, d_y, (const uint8_t *)d_w, n, rows, st),
                  "cats_gpu_dequantize_dev");
 }
 

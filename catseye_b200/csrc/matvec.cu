@@ -174,7 +174,7 @@ __host__ __device__ inline SmemPlan smem_plan(const MatvecArgs &a, int type)
     p.ring_off = 384;
     p.stage_stride = (uint32_t)round_up(a.full_chunk, 128);
     p.xs_off = p.ring_off + p.stage_stride * a.stages;
-    if (type == W_F32) p.xs_bytes = (uint32_t)round_up((size_t)a.n * 4, 128);
+    if (type == W_F32 || a.xmode == XM_F32) p.xs_bytes = (uint32_t)round_up((size_t)a.n * 4, 128);
     else p.xs_bytes = (uint32_t)round_up((size_t)a.units * 40, 128);   // lo16 + hi16 + (d, sum)
     p.total = p.xs_off + p.xs_bytes;
     return p;
@@ -217,7 +217,7 @@ __device__ __forceinline__ void mv_produce(const MatvecArgs &a, const SmemPlan &
 
 // Consumer warps: stage the activation, dot every chunk of this CTA's tiles,
 // run the epilogue.
-template <int WT, int RPW>
+template <int WT, int RPW, bool XF>
 __device__ __forceinline__ void mv_consume(const MatvecArgs &a, const SmemPlan &sp, uint8_t *smem, uint64_t *full,
                                            uint64_t *empty, float *red)
 {
@@ -232,8 +232,8 @@ __device__ __forceinline__ void mv_consume(const MatvecArgs &a, const SmemPlan &
         stage_q8_raw(static_cast<const uint8_t *>(a.x), a.n, xs, threadIdx.x, NC);
     } else {
         const float *src = static_cast<const float *>(a.x) + (a.x_row ? (size_t)(*a.x_row) * a.n : 0);
-        stage_act<WT>(Float4Src{reinterpret_cast<const float4 *>(src), false}, a.n, a.norm_w,
-                      blockIdx.x == 0 ? a.x_writeback : nullptr, xs, red, threadIdx.x, NC);
+        stage_act<XF ? (int)W_F32 : WT>(Float4Src{reinterpret_cast<const float4 *>(src), false}, a.n, a.norm_w,
+                                        blockIdx.x == 0 ? a.x_writeback : nullptr, xs, red, threadIdx.x, NC);
     }
     pdl_launch_dependents();
 
@@ -251,7 +251,7 @@ __device__ __forceinline__ void mv_consume(const MatvecArgs &a, const SmemPlan &
         for (int s = 0; s < a.nseg; s++) {
             if (!mbar_wait_bounded(&full[stage], phase, a.err, CATS_DEVERR_MBAR_FULL)) { ok = false; break; }
             const int us = min(MV_SEG_UNITS, a.units - MV_SEG_UNITS * s);
-            consume_chunk<WT, RPW>(ring + (size_t)stage * sp.stage_stride, us, s, warp, lane, a.units, xs, acc);
+            consume_chunk<WT, RPW, XF>(ring + (size_t)stage * sp.stage_stride, us, s, warp, lane, a.units, xs, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
             if (++stage == stages) { stage = 0; phase ^= 1; }
@@ -311,7 +311,7 @@ __device__ __forceinline__ void mv_consume(const MatvecArgs &a, const SmemPlan &
     }
 }
 
-template <int WT, int RPW>
+template <int WT, int RPW, bool XF>
 __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant__ MatvecArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_matvec(const __grid_constant_
     if (warp == MV_CONSUMER_WARPS) {
         if (lane == 0) mv_produce(a, sp, smem, full, empty);
     } else {
-        mv_consume<WT, RPW>(a, sp, smem, full, empty, red);
+        mv_consume<WT, RPW, XF>(a, sp, smem, full, empty, red);
     }
     // No thread returns early: once all copies have landed and every arrive
     // is done, retire the mbarriers so the next kernel on this SM may use
@@ -359,13 +359,14 @@ int matvec_num_sms()
     return sms;
 }
 
-template <int WT, int RPW>
+template <int WT, int RPW, bool XF>
 static cudaError_t launch_t(const MatvecArgs &a, cudaStream_t st, bool pdl, int grid_override)
 {
     const size_t smem = matvec_smem_bytes(a, WT);
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_matvec<WT, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_matvec<WT, RPW, XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -380,17 +381,27 @@ static cudaError_t launch_t(const MatvecArgs &a, cudaStream_t st, bool pdl, int 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_matvec<WT, RPW>, a);
+    return cudaLaunchKernelEx(&cfg, k_matvec<WT, RPW, XF>, a);
+}
+
+template <int WT, bool XF>
+static cudaError_t launch_rpw(const MatvecArgs &a, int rpw, cudaStream_t st, bool pdl, int grid_override)
+{
+    return rpw == 2 ? launch_t<WT, 2, XF>(a, st, pdl, grid_override) : launch_t<WT, 1, XF>(a, st, pdl, grid_override);
 }
 
 cudaError_t launch_matvec(const MatvecArgs &a, int rpw, int type, cudaStream_t st, bool pdl, int grid_override)
 {
     if (a.stages < 2 || a.stages > 8) return cudaErrorInvalidValue;
     if (matvec_smem_bytes(a, type) > 227 * 1024) return cudaErrorInvalidValue;
+    // fp32 activations with quantized weights: the matmul_q4_0 binding (dequantize, fp32 dot)
+    const bool xf = type != W_F32 && a.xmode == XM_F32;
     switch (type) {
-    case W_F32: return rpw == 2 ? launch_t<W_F32, 2>(a, st, pdl, grid_override) : launch_t<W_F32, 1>(a, st, pdl, grid_override);
-    case W_Q4_0: return rpw == 2 ? launch_t<W_Q4_0, 2>(a, st, pdl, grid_override) : launch_t<W_Q4_0, 1>(a, st, pdl, grid_override);
-    case W_Q8_0: return rpw == 2 ? launch_t<W_Q8_0, 2>(a, st, pdl, grid_override) : launch_t<W_Q8_0, 1>(a, st, pdl, grid_override);
+    case W_F32: return launch_rpw<W_F32, false>(a, rpw, st, pdl, grid_override);
+    case W_Q4_0: return xf ? launch_rpw<W_Q4_0, true>(a, rpw, st, pdl, grid_override)
+                           : launch_rpw<W_Q4_0, false>(a, rpw, st, pdl, grid_override);
+    case W_Q8_0: return xf ? launch_rpw<W_Q8_0, true>(a, rpw, st, pdl, grid_override)
+                           : launch_rpw<W_Q8_0, false>(a, rpw, st, pdl, grid_override);
     }
     return cudaErrorInvalidValue;
 }

@@ -48,7 +48,8 @@ size_t gguf_row_bytes(int type, int n);
 enum XMode : int {
     XM_Q8_RAW = 0,       // x is n/32 reference Q8 blocks {int8 q[32]; float d} (36 B)
     XM_Q8_FROM_F32 = 1,  // x is fp32: optional rmsnorm, then quantize_q8 (AVX rounding) in smem
-    XM_F32 = 2,          // x is fp32: optional rmsnorm, staged as fp32 (F32 weights)
+    XM_F32 = 2,          // x is fp32: optional rmsnorm, staged as fp32 (F32 weights, or quantized
+                         // weights dequantized in registers: the matmul_q4_0 binding)
 };
 
 // Epilogues

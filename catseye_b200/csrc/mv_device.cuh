@@ -160,7 +160,10 @@ __device__ __forceinline__ void stage_q8_raw(const uint8_t *xq, int n, uint8_t *
 // lane.  Q4_0: the low nibbles are dotted as bytes; the high nibbles are
 // dotted in place (w & 0xF0F0F0F0, each code times 16) and the sum shifted
 // down by 4, which is exact.
-template <int WT, int RPW>
+// XF (fp32 activations staged as floats, quantized weights): each weight is
+// dequantized in registers, (code - offset) * d exactly, and multiplied
+// with x in fp32, as matmul_q4_0 (llm/catseye_llm.h:880-914) does.
+template <int WT, int RPW, bool XF = false>
 __device__ __forceinline__ void consume_chunk(const uint8_t *ch, int us, int s, int warp, int lane, int units,
                                               const uint8_t *xs, float (&acc)[RPW])
 {
@@ -184,6 +187,50 @@ __device__ __forceinline__ void consume_chunk(const uint8_t *ch, int us, int s, 
                 acc[r] = fmaf(wv.y, xv.y, acc[r]);
                 acc[r] = fmaf(wv.z, xv.z, acc[r]);
                 acc[r] = fmaf(wv.w, xv.w, acc[r]);
+            }
+            continue;
+        }
+        if (XF) {
+            const float4 *xv = reinterpret_cast<const float4 *>(xs) + (size_t)u * 8;   // the unit's 32 floats
+            float xf[32];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float4 v = xv[k];
+                xf[4 * k] = v.x;
+                xf[4 * k + 1] = v.y;
+                xf[4 * k + 2] = v.z;
+                xf[4 * k + 3] = v.w;
+            }
+#pragma unroll
+            for (int r = 0; r < RPW; r++) {
+                const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(srow + r * sstride + h * 64));
+                uint32_t cw[8];
+                if (WT == W_Q4_0) {
+                    const uint4 wq = *reinterpret_cast<const uint4 *>(wrow + r * rstride + h * 512);
+                    cw[0] = wq.x; cw[1] = wq.y; cw[2] = wq.z; cw[3] = wq.w;
+                } else {
+                    const uint8_t *wp = ch + ((size_t)(warp * RPW + r) * 2 * us + j) * 16;
+                    const uint4 wl = *reinterpret_cast<const uint4 *>(wp);
+                    const uint4 wh = *reinterpret_cast<const uint4 *>(wp + (size_t)us * 16);
+                    cw[0] = wl.x; cw[1] = wl.y; cw[2] = wl.z; cw[3] = wl.w;
+                    cw[4] = wh.x; cw[5] = wh.y; cw[6] = wh.z; cw[7] = wh.w;
+                }
+                float a = acc[r];
+#pragma unroll
+                for (int k = 0; k < 16; k++) {
+                    const uint32_t byte = (cw[k >> 2] >> (8 * (k & 3))) & 0xffu;
+                    float w0, w1;   // elements k and k + 16
+                    if (WT == W_Q4_0) {
+                        w0 = (float)((int)(byte & 0xf) - 8) * dw;
+                        w1 = (float)((int)(byte >> 4) - 8) * dw;
+                    } else {
+                        w0 = (float)(int8_t)byte * dw;
+                        w1 = (float)(int8_t)((cw[4 + (k >> 2)] >> (8 * (k & 3))) & 0xffu) * dw;
+                    }
+                    a = fmaf(w0, xf[k], a);
+                    a = fmaf(w1, xf[k + 16], a);
+                }
+                acc[r] = a;
             }
             continue;
         }

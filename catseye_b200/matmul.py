@@ -2,8 +2,9 @@
 
 The names and argument meanings follow the reference:
   matmul(xout, x, w, n, d)         llm/catseye_llm.h:1519-1533 (gguf_matmul[] :2583)
-  quantize(q, x, n)                quantize_q8, :155-225
-  dequantize(y, w, row, n)         _dequantize_q4_0, :483-486
+  matmul_f32act(...)               matmul_q4_0 (fp32 x, quantize_null), :880-914
+  quantize(q, x, n)                quantize_q8, :155-225; quantize_q8_K :262-296
+  dequantize(y, w, row, n)         _dequantize_q4_0, :483-486; Q3_K / Q6_K :349-426
   sgemm(ta, tb, m, n, k, ...)      sgemm_ocl, sgemm_ocl2.h:208 / gemm_rnn|rnt|rtn, catseye.h:78-129
 Inputs are numpy arrays (host memory, copied per call like the reference's
 GPU backends) or torch CUDA tensors for the device-pointer forms.
@@ -14,15 +15,18 @@ import numpy as np
 
 from . import _lib
 
-F32, Q4_0, Q8_0 = 0, 2, 8
+F32, Q4_0, Q8_0, Q3_K, Q6_K = 0, 2, 8, 11, 14
 
 # the type-indexed tables of the reference (gguf_matmul / gguf_quantize / gguf_dequantize)
-_MATMUL = {F32: "cats_gpu_matmul_f32", Q4_0: "cats_gpu_matmul_q4_0_q8", Q8_0: "cats_gpu_matmul_q8_0_q8"}
-_DEQUANT = {Q4_0: "cats_gpu_dequantize_q4_0", Q8_0: "cats_gpu_dequantize_q8_0"}
+_MATMUL = {F32: "cats_gpu_matmul_f32", Q4_0: "cats_gpu_matmul_q4_0_q8", Q8_0: "cats_gpu_matmul_q8_0_q8",
+           Q3_K: "cats_gpu_matmul_q3_K_q8_K", Q6_K: "cats_gpu_matmul_q6_K_q8_K"}
+_MATMUL_F32ACT = {Q4_0: "cats_gpu_matmul_q4_0_f32", Q8_0: "cats_gpu_matmul_q8_0_f32"}
+_DEQUANT = {Q4_0: "cats_gpu_dequantize_q4_0", Q8_0: "cats_gpu_dequantize_q8_0", Q3_K: "cats_gpu_dequantize_q3_K",
+            Q6_K: "cats_gpu_dequantize_q6_K"}
 
 
 def row_bytes(t, n):
-    return {F32: n * 4, Q4_0: n // 32 * 18, Q8_0: n // 32 * 34}[t]
+    return {F32: n * 4, Q4_0: n // 32 * 18, Q8_0: n // 32 * 34, Q3_K: n // 256 * 110, Q6_K: n // 256 * 210}[t]
 
 
 def _p(a):
@@ -44,10 +48,28 @@ def unregister_weight(w):
 
 
 def matmul(t, xout, x, w, n, d):
-    """xout[:d] = W x; x is fp32 (F32) or Q8 blocks (quantized types) as quantize() made them."""
+    """xout[:d] = W x; x is fp32 (F32), Q8 blocks (Q4_0, Q8_0) or Q8_K blocks
+    (Q3_K, Q6_K) as quantize() / quantize_q8_K() made them."""
     lib = _lib.init()
     _lib.call_void(getattr(lib, _MATMUL[t]), _p(xout), _p(x), _p(w), n, d, what=_MATMUL[t])
     return xout
+
+
+def matmul_f32act(t, xout, x, w, n, d):
+    """xout[:d] = W x with fp32 x against Q4_0 / Q8_0 weights (matmul_q4_0)."""
+    lib = _lib.init()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    _lib.call_void(getattr(lib, _MATMUL_F32ACT[t]), _p(xout), _p(x), _p(w), n, d, what=_MATMUL_F32ACT[t])
+    return xout
+
+
+def quantize_q8_K(x):
+    """quantize_q8_K of fp32 x -> n/256 blocks of 260 bytes (int8 array)."""
+    lib = _lib.init()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.zeros(x.size // 256 * 260, dtype=np.int8)
+    _lib.call_void(lib.cats_gpu_quantize_q8_K, _p(q), _p(x), x.size, what="quantize_q8_K")
+    return q
 
 
 def quantize(x):

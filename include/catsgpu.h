@@ -33,6 +33,8 @@ extern "C" {
 #define CATS_TYPE_F32  0
 #define CATS_TYPE_Q4_0 2
 #define CATS_TYPE_Q8_0 8
+#define CATS_TYPE_Q3_K 11
+#define CATS_TYPE_Q6_K 14
 
 /* status codes */
 #define CATS_OK             0
@@ -88,12 +90,31 @@ void cats_gpu_quantize_q8(int8_t *q, float *x, int n);
  * matrix -> n floats.  Returns 0 like the reference. */
 void *cats_gpu_dequantize_q4_0(void *y, const void *x, int row, int n);
 void *cats_gpu_dequantize_q8_0(void *y, const void *x, int row, int n);
+/* matmul_q4_0 (llm/catseye_llm.h:880-914, MATMUL_FUNC :1530): Q4_0 weights
+ * against fp32 x (the binding with quantize_null, :2593-2595): each weight
+ * dequantized, products and sums in fp32.  cats_gpu_matmul_q8_0_f32 is the
+ * same for Q8_0 weights (no reference counterpart). */
+void cats_gpu_matmul_q4_0_f32(float *xout, void *x, void *w, int n, int d);
+void cats_gpu_matmul_q8_0_f32(float *xout, void *x, void *w, int n, int d);
+/* K-quants (256-element super-blocks; n % 256 == 0): matmul_q3_K_q8_K and
+ * matmul_q6_K_q8_K (:1532-1533; dots :1057-1261, 1332-1511) with x as
+ * quantize_q8_K made it (n/256 blocks of {int8 q[256]; float d}, 260 B);
+ * quantize_q8_K (:262-296, in place like the reference); _dequantize_q3_K /
+ * _dequantize_q6_K (:349-426, bound in gguf_dequantize[] :2602-2607). */
+void cats_gpu_matmul_q3_K_q8_K(float *xout, void *x, void *w, int n, int d);
+void cats_gpu_matmul_q6_K_q8_K(float *xout, void *x, void *w, int n, int d);
+void cats_gpu_quantize_q8_K(int8_t *q, float *x, int n);
+void *cats_gpu_dequantize_q3_K(void *y, const void *x, int row, int n);
+void *cats_gpu_dequantize_q6_K(void *y, const void *x, int row, int n);
 
 /* -------------------------------------- LLM device-pointer entry points */
 
 /* d_out[d] = W x for a registered weight w (host key); d_x is a device
  * pointer to n floats (x_is_q8 = 0: quantized on the device for quantized
- * types) or to n/32 Q8 blocks (x_is_q8 = 1).  stream: cudaStream_t or NULL. */
+ * types, quantize_q8 or quantize_q8_K as the type takes) or to the quantized
+ * blocks (x_is_q8 = 1: Q8 or Q8_K); x_is_q8 = 2 takes n floats as they are
+ * against Q4_0/Q8_0 weights (the matmul_q4_0 binding).  stream:
+ * cudaStream_t or NULL. */
 int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q8, void *stream);
 /* Batched product for prefill and batched decode: y[T][d] = x[T][n] * W^T
  * for a registered Q4_0 or Q8_0 weight (n a multiple of 64), i.e. T calls of

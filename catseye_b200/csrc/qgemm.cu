@@ -14,7 +14,7 @@
 //  * Producers (warps 0-7): thread p owns block p & 1 of weight row p >> 1 in
 //    every K slice.  It walks the block's words through the weight's tile
 //    layout (the matvec's, so prefill and decode share one copy of the
-//    weights in HBM) with a cursor, four slices ahead into registers,
+//    weights in HBM) with a cursor, 8 (Q4_0) or 4 (Q8_0) slices ahead,
 //    dequantizes them to fp16 in the x16 element order (qgemm.cuh) and
 //    stores them in the K-major 128-byte-swizzled form UMMA reads.  Thread 0
 //    also brings the stage's BN activation rows in with one bulk copy: the
@@ -37,9 +37,8 @@ namespace cats {
 
 constexpr int QG_M = 128;
 constexpr int QG_K = 64;
-// K slices of weight words a producer has in flight: deeper for small token
-// tiles, where the weight stream, not the tensor cores, sets the pace
-__host__ __device__ constexpr int qg_prefetch(int bn) { return bn <= 32 ? 8 : 4; }
+// K slices of weight words a producer has in flight: 8 of Q4_0 (5 registers
+// a slice) or 4 of Q8_0 (9 registers), the same bytes either way
 constexpr int QG_PROD = 256;                 // producer threads (8 warps): one block per K slice each
 constexpr int QG_THREADS = QG_PROD + 32;     // + the MMA warp
 constexpr int QG_MMA_WARP = QG_PROD / 32;
@@ -200,7 +199,7 @@ template <int WT, int BN>
 __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__ QgemmArgs a)
 {
     constexpr int ST = qg_stages(BN);
-    constexpr int QG_PF = qg_prefetch(BN);
+    constexpr int QG_PF = WT == W_Q8_0 ? 4 : 8;
     constexpr uint32_t B_BYTES = BN * 128;
     constexpr uint32_t STAGE = QG_A_BYTES + B_BYTES;
     constexpr int TCOLS = BN < 32 ? 32 : BN;   // TMEM columns: a power of two >= 32

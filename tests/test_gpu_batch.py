@@ -171,3 +171,31 @@ def test_batch_refuses_bad_input(llm, orc):
     with pytest.raises(CatsGpuError):
         f.batch_reserve(4, 1)
     f.close()
+
+
+@pytest.mark.parametrize("engine", [0, 1])
+def test_prefill_then_single_token_decode(llm, orc, engine):
+    """A prompt prefilled by one batched step is continued by the single-token
+    engines (persistent kernel, graph): the oracle runs the prompt in its
+    fp32-activation mode and the next steps with quantize_q8, as the two
+    device paths do.  The decode steps carry the Q8 rounding-flip amplitude
+    of the single-token tests (2e-3 on these small models)."""
+    cfg = _tiny(llm, Q4_0)
+    mw = ModelWeights(cfg, 31, orc)
+    toks = prompt(31, 8, cfg.vocab)
+    m = llm.GpuLLM(cfg)
+    m.set_engine(engine)
+    m.set_weights(mw)
+    m.batch_reserve(8, 1)
+    nxt, lg = m.forward_batch(toks, np.arange(8), logits=True)
+    r = orc.llm(mw, q8_mode=2)
+    for p, tok in enumerate(toks):
+        assert rel(lg[p], r.step(int(tok), p)) < TOL
+    r.s.q8_mode = 0                      # the decode steps quantize their activations
+    tok = int(nxt[-1])
+    for p in range(8, 12):
+        got = m.step(tok, p).copy()
+        ref = r.step(tok, p)
+        assert rel(got, ref) < 2e-3, p
+        tok = int(np.argmax(got))
+    m.close()

@@ -1,7 +1,7 @@
 """Benchmark: batch-1 decode of the Llama-2-7B-shape Q4_0 model on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload llama7b_q4_0|llama7b_q8_0|stories_f32] [--layers L]
+                    [--workload llama7b_q4_0|llama7b_q8_0|llama70b_q4_0|stories_f32] [--layers L]
 
 --layers L keeps the workload's shapes with L layers (a small case for
 profiling; the workload name then carries the layer count).
@@ -65,6 +65,7 @@ sys.path.insert(0, ROOT)
 WORKLOADS = {
     "llama7b_q4_0": ("LLAMA2_7B", 2),
     "llama7b_q8_0": ("LLAMA2_7B", 8),
+    "llama70b_q4_0": ("LLAMA2_70B", 2),
     "stories_f32": ("STORIES_F32", 0),
 }
 PROMPT = 8

@@ -178,8 +178,11 @@ def test_prefill_then_single_token_decode(llm, orc, engine):
     """A prompt prefilled by one batched step is continued by the single-token
     engines (persistent kernel, graph): the oracle runs the prompt in its
     fp32-activation mode and the next steps with quantize_q8, as the two
-    device paths do.  The decode steps carry the Q8 rounding-flip amplitude
-    of the single-token tests (2e-3 on these small models)."""
+    device paths do.  The prefilled cache differs from the oracle's by the
+    fp16 rounding (~5e-4), enough to flip a few Q8 activation codes in the
+    decode steps: their bar is the flip amplitude of the single-token tests
+    (3e-2; measured 0.8-1.1e-2).  A model whose cache never saw the prompt
+    lands far outside it, so the bar still shows the cache is the one read."""
     cfg = _tiny(llm, Q4_0)
     mw = ModelWeights(cfg, 31, orc)
     toks = prompt(31, 8, cfg.vocab)
@@ -188,14 +191,24 @@ def test_prefill_then_single_token_decode(llm, orc, engine):
     m.set_weights(mw)
     m.batch_reserve(8, 1)
     nxt, lg = m.forward_batch(toks, np.arange(8), logits=True)
+    cold = llm.GpuLLM(cfg)               # same weights, empty cache
+    cold.set_engine(engine)
+    cold.set_weights(mw)
     r = orc.llm(mw, q8_mode=2)
-    for p, tok in enumerate(toks):
-        assert rel(lg[p], r.step(int(tok), p)) < TOL
+    pre = [rel(lg[p], r.step(int(tok), p)) for p, tok in enumerate(toks)]
     r.s.q8_mode = 0                      # the decode steps quantize their activations
     tok = int(nxt[-1])
+    dec, unprimed = [], []
     for p in range(8, 12):
         got = m.step(tok, p).copy()
         ref = r.step(tok, p)
-        assert rel(got, ref) < 2e-3, p
+        dec.append(rel(got, ref))
+        unprimed.append(rel(cold.step(tok, p).copy(), ref))
         tok = int(np.argmax(got))
+    print("prefill", ["%.1e" % e for e in pre], "decode", ["%.1e" % e for e in dec],
+          "empty cache", ["%.1e" % e for e in unprimed])
+    assert max(pre) < TOL
+    assert max(dec) < 3e-2
+    assert min(unprimed) > 3 * 3e-2
     m.close()
+    cold.close()

@@ -225,3 +225,23 @@ def test_llama7b_full_size_q4_0(llm, orc):
         if pos == 0:
             assert int(np.argmax(lg)) == int(np.argmax(la))
     m.close()
+
+
+@pytest.mark.parametrize("engine", ENGINES)
+def test_llama70b_shape_one_layer_q4_0(llm, orc, engine):
+    """70B shapes at batch 1 (dim 8192, 64 query heads over 8 kv heads,
+    hidden 28672 staged in several passes, 32000-row classifier) for one
+    layer, against the oracle on the downloaded device-generated tensors.
+    One layer leaves little room for Q8 rounding flips to grow: the bar is
+    the reference's own AVX/plain-C spread, at least 1e-2."""
+    from dataclasses import replace
+    cfg = replace(llm.LLAMA2_70B, n_layers=1, seq_len=16, wtype=Q4_0)
+    m = llm.GpuLLM(cfg)
+    m.set_engine(engine)
+    m.init_random(71)
+    w = _synth_weights(llm, cfg, 71)
+    avx, plain = orc.llm(w, 0), orc.llm(w, 1)
+    for pos, tok in enumerate([2, 31000, 77, 5]):
+        lg, la, lp = m.step(tok, pos), avx.step(tok, pos), plain.step(tok, pos)
+        assert rel(lg, la) < max(1e-2, 2 * rel(lp, la)), pos
+    m.close()

@@ -446,6 +446,85 @@ __device__ __forceinline__ void attention_phase(const DecodeArgs &a, int l, int 
     }
 }
 
+// Attention for short contexts, one CTA per query head: the CTA's 16 warps
+// take four timesteps each per pass (64 per pass), each with its own online
+// softmax, and merge in shared memory (scratch: the staged-activation area,
+// free between the qkv and wo phases).  No partials go through global memory,
+// so the chain is the q/K/V loads, the dots and one CTA barrier.
+constexpr int DEC_LOCAL_ATTN_MAX_T = 256;
+
+__host__ __device__ inline uint32_t local_attn_scratch_bytes(int hs)
+{
+    return (uint32_t)DEC_WARPS * (hs + 4) * 4;
+}
+
+__device__ __forceinline__ void attention_local(const DecodeArgs &a, const Smem &sm, int l, int pos)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int h = blockIdx.x;
+    if (h >= a.heads) return;   // the whole CTA: no head, nothing to do
+    const int hs = a.head_size, P = hs + 4;
+    const bool mine = lane * 4 < hs;
+    const int T = pos + 1;
+    const float rs = sqrtf((float)hs);
+    const float *kc = a.kcache + (size_t)l * a.seq_len * a.kv_dim;
+    const float *vc = a.vcache + (size_t)l * a.seq_len * a.kv_dim;
+    const int kvo = (h / a.kv_mul) * hs + lane * 4;
+    constexpr int U = 4;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 qv = mine ? __ldcg(reinterpret_cast<const float4 *>(a.q + h * hs) + lane) : z4;
+    float4 acc = z4;
+    float m = -INFINITY, lsum = 0.f;
+    for (int tb = warp * U; tb < T; tb += DEC_WARPS * U) {
+        float4 kr[U], vr[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int t = min(tb + u, T - 1);   // clamped rows are loaded but not used
+            kr[u] = mine ? __ldcg(reinterpret_cast<const float4 *>(kc + (size_t)t * a.kv_dim + kvo)) : z4;
+            vr[u] = mine ? __ldcg(reinterpret_cast<const float4 *>(vc + (size_t)t * a.kv_dim + kvo)) : z4;
+        }
+        float dot[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) dot[u] = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
+#pragma unroll
+        for (int u = 0; u < U; u++) dot[u] = warp_sum(dot[u]);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (tb + u >= T) break;
+            const float sc = __fdiv_rn(dot[u], rs);
+            const float mn = fmaxf(m, sc);
+            const float corr = expf(m - mn);
+            const float p = expf(sc - mn);
+            lsum = lsum * corr + p;
+            acc.x = acc.x * corr + p * vr[u].x;
+            acc.y = acc.y * corr + p * vr[u].y;
+            acc.z = acc.z * corr + p * vr[u].z;
+            acc.w = acc.w * corr + p * vr[u].w;
+            m = mn;
+        }
+    }
+    // each warp's (max, sum, weighted V) into shared memory, then thread i < hs
+    // merges dimension i over the warps (:1706-1722)
+    float *scr = reinterpret_cast<float *>(sm.xs);
+    float *mine_p = scr + (size_t)warp * P;
+    if (lane == 0) { mine_p[0] = m; mine_p[1] = lsum; }
+    if (mine) reinterpret_cast<float4 *>(mine_p + 4)[lane] = acc;
+    named_bar_sync(1, DEC_NC);
+    if (tid < hs) {
+        float M = -INFINITY;
+        for (int w = 0; w < DEC_WARPS; w++) M = fmaxf(M, scr[w * P]);
+        float L = 0.f, v = 0.f;
+        for (int w = 0; w < DEC_WARPS; w++) {
+            const float mw = scr[w * P];
+            if (mw == -INFINITY) continue;
+            const float e = expf(mw - M);
+            L += e * scr[w * P + 1];
+            v += e * scr[w * P + 4 + tid];
+        }
+        a.xb[h * hs + tid] = v / L;
+    }
+}
+
 // Producer of group g's ring (lane g of the producer warp): streams the
 // chunks of the group's tiles (tile 2p + g of every pair p of every weight,
 // step after step) into the group's ring, in the order the group takes them.
@@ -527,7 +606,12 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             float xr[2];
             residual_first(a, wl[1], xr);   // x is final until the wo epilogue
-            attention_phase(a, l, pos);
+            // short contexts: one CTA per head, merged in shared memory
+            if (pos < DEC_LOCAL_ATTN_MAX_T && a.heads <= (int)gridDim.x &&
+                a.xs_bytes >= local_attn_scratch_bytes(a.head_size))
+                attention_local(a, sm, l, pos);
+            else
+                attention_phase(a, l, pos);
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);

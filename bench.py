@@ -631,16 +631,23 @@ def gemm_main(args):
     ms, e2e_s, e2e_steps, flops, launches, h2d, d2h, cfg, clocks = run_gemm(args, dist, rank, ws, local)
     if rank == 0:
         gfs = ws * flops * args.steps / (ms * 1e-3) / 1e9
-        peak = fp32_peak()
         achieved = flops * args.steps / (ms * 1e-3) / 1e12
         cfg["parallelism"] = f"replicas{ws}" if ws > 1 else "single"
+        if args.workload == "sgemm_4096":
+            # 3xTF32 on tcgen05: three tf32 products per fp32 product, tf32 at half the bf16 rate
+            bf16, bf16_kind = tensor_peak()
+            peak = bf16 / 2 / 3
+            roof = {"bound": "tensor", "kernel": "k_sgemm_tc (3xTF32, tcgen05 kind::tf32)",
+                    "peak_kind": f"{bf16_kind} / 2 (tf32 rate) / 3 (products per fp32 product)"}
+        else:
+            peak = fp32_peak()
+            roof = {"bound": "fp32-simt", "kernel": "k_conv_fwd + k_sgemm_tc",
+                    "peak_kind": "nominal (148 SMs x 128 FMA/clock x 2 x max SM clock)"}
         line = {"metric": metric, "value": round(gfs, 1), "unit": "GFLOP/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-                "roofline": {"bound": "fp32-simt", "kernel": "k_sgemm" if args.workload == "sgemm_4096"
-                             else "k_conv_fwd + k_sgemm", "achieved": round(achieved, 2), "peak": round(peak, 1),
-                             "peak_kind": "nominal (148 SMs x 128 FMA/clock x 2 x max SM clock)", "unit": "TFLOP/s",
-                             "frac": round(achieved / peak, 4), "traffic": None},
+                "roofline": dict(roof, achieved=round(achieved, 2), peak=round(peak, 1), unit="TFLOP/s",
+                                 frac=round(achieved / peak, 4), traffic=None),
                 "e2e": {"value": round(ws * flops * e2e_steps / e2e_s / 1e9, 1), "unit": "GFLOP/s",
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
                 "gpu_launches": launches * args.steps, "clocks": clocks}

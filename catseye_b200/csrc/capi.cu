@@ -814,7 +814,7 @@ int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const flo
         return fail(CATS_ERR_ARG, what);
     SgemmPlan p = sgemm_plan(m, n, k, matvec_num_sms());
     if (p.work_floats && grow((void **)&g.d_work, &g.cap_work, p.work_floats * 4)) return g.last_err;
-    return check(launch_sgemm(p, at, bt, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, g.d_work,
+    return check(launch_sgemm(p, at, bt, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, g.d_work, g.d_err,
                               stream ? (cudaStream_t)stream : g.stream),
                  what);
 }

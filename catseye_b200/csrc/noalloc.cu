@@ -73,6 +73,6 @@ extern "C" int cats_sgemm_dev_noalloc(char ta, char tb, int m, int n, int k, flo
     // Each split writes every element of its partial slab before the reduce
     // reads it, so nothing left in the array by an earlier call is ever used.
     const cudaError_t e = launch_sgemm(p, at, bt, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc,
-                                       g_scratch_addr[dev], static_cast<cudaStream_t>(stream));
+                                       g_scratch_addr[dev], nullptr, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? CATS_OK : capi_fail(CATS_ERR_CUDA, what);
 }

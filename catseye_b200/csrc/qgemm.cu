@@ -31,6 +31,7 @@
 //    order (deterministic).
 // Every wait is bounded; TMEM is freed on every path.
 #include "qgemm.cuh"
+#include "tc.cuh"
 #include <algorithm>
 
 namespace cats {
@@ -61,38 +62,6 @@ struct QgemmArgs {
     int accumulate;                   // y += product instead of y = product
     int *err;
 };
-
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-// K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (the canonical
-// UMMA K-major SW128 layout: SBO = 1024 B, LBO unused = 1, version 1).
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr)
-{
-    return (uint64_t)((smem_addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// kind::f16 instruction descriptor: D f32, A and B f16, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N)
-{
-    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile
-__device__ __forceinline__ uint32_t sw128(int r, int c)
-{
-    return (uint32_t)r * 128 + (uint32_t)((c ^ (r & 7)) * 16);
-}
-
-// 1-D bulk copy global -> shared completing on an mbarrier (no L2 hint: the
-// activations are read by every CTA of the column and should stay in L2).
-__device__ __forceinline__ void bulk_g2s_keep(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
 
 // The raw words of one 32-element block of a weight row.
 struct RawBlk {
@@ -242,7 +211,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     if (warp == QG_MMA_WARP) {
         // ---------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16(QG_M, BN);
+            const uint32_t idesc = umma_idesc(0, QG_M, BN);
             for (int kb = 0; kb < nk; kb++) {
                 const int s = kb % ST;
                 const uint32_t ph = (uint32_t)(kb / ST) & 1u;

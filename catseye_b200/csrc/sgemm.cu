@@ -189,7 +189,8 @@ SgemmPlan sgemm_plan(int M, int N, int K, int num_sms)
         int s = std::min(cdiv(num_sms * 2, tiles), K / 256);
         p.splits = std::max(1, std::min(s, 32));
     }
-    p.k_per_split = (int)round_up((size_t)cdiv(K, p.splits), BK);
+    // whole 32-deep slices, the tensor-core kernel's unit (a multiple of BK)
+    p.k_per_split = (int)round_up((size_t)cdiv(K, p.splits), 32);
     p.splits = cdiv(K, p.k_per_split);
     p.work_floats = p.splits > 1 ? (size_t)p.splits * M * N : 0;
     return p;
@@ -205,19 +206,28 @@ static cudaError_t launch_t(const SgemmPlan &p, bool vec, int M, int N, int K, f
     else k_sgemm<TA, TB, false><<<grid, NT, 0, st>>>(M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, p.k_per_split, wk);
     cudaError_t e = cudaGetLastError();
     if (e || p.splits == 1) return e;
+    return launch_splitk_reduce(M, N, p.splits, alpha, work, beta, C, ldc, st);
+}
+
+cudaError_t launch_splitk_reduce(int M, int N, int splits, float alpha, const float *work, float beta, float *C,
+                                 int ldc, cudaStream_t st)
+{
     const size_t MN = (size_t)M * N;
     int rg = (int)std::min<size_t>((MN + 255) / 256, 148 * 8);
-    k_splitk_reduce<<<rg, 256, 0, st>>>(M, N, p.splits, alpha, work, beta, C, ldc);
+    k_splitk_reduce<<<rg, 256, 0, st>>>(M, N, splits, alpha, work, beta, C, ldc);
     return cudaGetLastError();
 }
 
 cudaError_t launch_sgemm(const SgemmPlan &p, bool ta, bool tb, int M, int N, int K, float alpha, const float *A, int lda,
-                         const float *B, int ldb, float beta, float *C, int ldc, float *work, cudaStream_t st)
+                         const float *B, int ldb, float beta, float *C, int ldc, float *work, int *err,
+                         cudaStream_t st)
 {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (K <= 0) {   // C = beta*C
         return launch_t<false, false>(p, false, M, N, 0, alpha, A, lda, B, ldb, beta, C, ldc, work, st);
     }
+    if (sgemm_tc_usable(ta, tb, M, N, K, A, lda, B, ldb))
+        return launch_sgemm_tc(p, ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, work, err, st);
     const bool aligned = ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0) && lda % 4 == 0 && ldb % 4 == 0;
     // the vector path needs the contiguous extent of each loaded row to be a multiple of 4
     const bool vec = aligned && (ta ? M % 4 == 0 : K % 4 == 0) && (tb ? K % 4 == 0 : N % 4 == 0);

@@ -12,9 +12,23 @@ struct SgemmPlan {
 SgemmPlan sgemm_plan(int M, int N, int K, int num_sms);
 
 // C[M][N] (leading dim ldc) = alpha * op(A) * op(B) + beta * C.  `work` must hold
-// plan.work_floats floats when plan.splits > 1.
+// plan.work_floats floats when plan.splits > 1.  Shapes the tensor cores can
+// take (sgemm_tc_usable) run as 3xTF32 on tcgen05 (sgemm_tc.cu), the rest on
+// the CUDA cores.  `err` (may be null) receives CATS_DEVERR_* bits when a
+// tensor-core wait times out; the tiles of such a CTA are written as NaN.
 cudaError_t launch_sgemm(const SgemmPlan &p, bool ta, bool tb, int M, int N, int K, float alpha, const float *A,
-                         int lda, const float *B, int ldb, float beta, float *C, int ldc, float *work,
+                         int lda, const float *B, int ldb, float beta, float *C, int ldc, float *work, int *err,
                          cudaStream_t st);
+
+// C = alpha * sum of the plan's K-split partial slabs + beta * C
+cudaError_t launch_splitk_reduce(int M, int N, int splits, float alpha, const float *work, float beta, float *C,
+                                 int ldc, cudaStream_t st);
+
+// tensor-core (3xTF32) path
+bool sgemm_tc_usable(bool ta, bool tb, int M, int N, int K, const float *A, int lda, const float *B, int ldb);
+size_t sgemm_tc_smem_bytes();
+cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, int K, float alpha, const float *A,
+                            int lda, const float *B, int ldb, float beta, float *C, int ldc, float *work, int *err,
+                            cudaStream_t st);
 
 } // namespace cats

@@ -47,6 +47,46 @@ def test_sgemm_shapes(mm, orc, ta, tb, M, N, K):
         assert rel(c, orc.sgemm(ta, tb, M, N, K, alpha, A, B, beta, C0)) < TOL, (alpha, beta)
 
 
+# Shapes the tensor-core (3xTF32) kernel takes: M*N*K >= 2^24 with the
+# contiguous extents a multiple of 4.  Ragged edges in every dimension, K
+# tails shorter than one 32-deep slice, K splits (few output tiles, long K),
+# a single output row block, and a long-K product whose error budget is the
+# tightest.
+TC_SHAPES = [(300, 260, 1000), (196, 4100, 36), (4, 4096, 1024), (1024, 1024, 8192), (132, 516, 2052),
+             (128, 128, 4096), (2048, 64, 1536)]
+
+
+@pytest.mark.parametrize("ta,tb", [("N", "N"), ("N", "T"), ("T", "N"), ("T", "T")])
+@pytest.mark.parametrize("M,N,K", TC_SHAPES)
+def test_sgemm_tensor_core_shapes(mm, orc, ta, tb, M, N, K):
+    rng = np.random.default_rng(M * 7919 + N * 31 + K)
+    A = rng.uniform(-1, 1, M * K).astype(np.float32)
+    B = rng.uniform(-1, 1, K * N).astype(np.float32)
+    C0 = rng.uniform(-1, 1, M * N).astype(np.float32)
+    for alpha, beta in ((1.0, 0.0), (0.5, 0.25)):
+        c = C0.copy()
+        mm.sgemm(ta, tb, M, N, K, alpha, A, B, beta, c)
+        assert np.isfinite(c).all()
+        assert rel(c, orc.sgemm(ta, tb, M, N, K, alpha, A, B, beta, C0)) < TOL, (alpha, beta)
+
+
+def test_sgemm_tensor_core_wide_range(mm):
+    """3xTF32 keeps fp32 accuracy where plain TF32 (10-bit mantissa) would not:
+    operands spread over 2^-20..2^20, checked element-wise in float64."""
+    rng = np.random.default_rng(12)
+    M, N, K = 256, 384, 512
+    A = (rng.uniform(-1, 1, M * K) * 2.0 ** rng.integers(-20, 20, M * K)).astype(np.float32)
+    B = (rng.uniform(-1, 1, K * N) * 2.0 ** rng.integers(-20, 20, K * N)).astype(np.float32)
+    c = np.zeros(M * N, np.float32)
+    mm.sgemm("N", "N", M, N, K, 1.0, A, B, 0.0, c)
+    want = A.reshape(M, K).astype(np.float64) @ B.reshape(K, N).astype(np.float64)
+    mag = np.abs(A.reshape(M, K)).astype(np.float64) @ np.abs(B.reshape(K, N)).astype(np.float64)
+    # |error| against the sum of |a||b|: each 3xTF32 product is within
+    # 3 * 2^-22 of a*b and fp32 accumulation adds ~sqrt(K) * 2^-24, while one
+    # tf32 rounding (2^-11) of the dominant terms would show as ~2^-12
+    assert float(np.max(np.abs(c.reshape(M, N) - want) / mag)) < 2.0 ** -16
+
+
 def test_beta_zero_ignores_nan_in_c(mm, orc):
     rng = np.random.default_rng(4)
     A = rng.uniform(-1, 1, 40 * 30).astype(np.float32)
@@ -54,6 +94,12 @@ def test_beta_zero_ignores_nan_in_c(mm, orc):
     c = np.full(40 * 20, np.nan, np.float32)
     mm.sgemm("N", "N", 40, 20, 30, 1.0, A, B, 0.0, c)
     assert rel(c, orc.sgemm("N", "N", 40, 20, 30, 1.0, A, B, 0.0, np.zeros(800, np.float32))) < TOL
+    M, N, K = 256, 256, 512   # the same on the tensor-core path
+    A = rng.uniform(-1, 1, M * K).astype(np.float32)
+    B = rng.uniform(-1, 1, K * N).astype(np.float32)
+    c = np.full(M * N, np.nan, np.float32)
+    mm.sgemm("N", "N", M, N, K, 1.0, A, B, 0.0, c)
+    assert rel(c, orc.sgemm("N", "N", M, N, K, 1.0, A, B, 0.0, np.zeros(M * N, np.float32))) < TOL
 
 
 def test_sgemm_dev_leading_dimensions(mm, orc):

@@ -24,10 +24,11 @@
 // coalesced.  CTA: 128 (n) x 128 (m) outputs, K in slices of 32 (one 128-byte
 // swizzled row of fp32).
 //  * Producers (warps 0-7): each slice's A and B^T tiles from global memory,
-//    two slices ahead in registers, split into hi and lo and stored K-major and
-//    swizzled.  K-contiguous operands (A of NN/NT, B of NT) are read a float4
-//    along k per thread; the others (A of TN, B of NN) with a lane per k, so
-//    the transposing 4-byte shared stores fill whole 128-byte rows.  TC_ST
+//    two slices ahead in registers, split into hi and lo and stored 128-byte
+//    swizzled in the operand's own major order: K-contiguous operands (A of
+//    NN/NT, B of NT) K-major, the others (A of TN, B of NN) MN-major, which the
+//    tensor cores read directly (instruction descriptor bits 15/16), so every
+//    global load is a coalesced row and every shared store a 16-byte chunk.  TC_ST
 //    slices into chunk c + 1 they add chunk c's accumulator into the running
 //    sum (the MMA warp is then busy with the stages already filled).
 //  * MMA warp (warp 8, one thread): per slice and K=8 step, B^T_hi.A_hi into
@@ -99,9 +100,10 @@ __device__ __forceinline__ void split4(float4 v, uint4 &hi, uint4 &lo)
 }
 
 // One operand tile of a slice: 128 rows (m or n) x 32 k.  K_CONTIG: the
-// operand is stored row-major along k (X[row][k], ld), else along rows
-// (X[k][row], ld).  Thread t loads 4 float4: K_CONTIG as f = t + 256 i ->
-// (row f / 8, k 4 (f % 8)); else (k t % 32, rows 4 (t / 32 + 8 i) ..).
+// operand is stored row-major along k (X[row][k], ld) and thread t loads
+// f = t + 256 i -> (row f / 8, k 4 (f % 8)): 8 lanes per 128-byte row.  Else
+// it is stored along rows (X[k][row], ld) and warp w loads k = w + 8 i, rows
+// 4 lane .. 4 lane + 3: one 512-byte row of the tile per warp instruction.
 template <bool K_CONTIG>
 __device__ __forceinline__ void load_tile(const float *__restrict__ X, int ld, int rows, int K, int r0, int k0,
                                           float4 (&v)[4])
@@ -114,12 +116,27 @@ __device__ __forceinline__ void load_tile(const float *__restrict__ X, int ld, i
             const int f = t + TC_PROD * i, r = r0 + f / 8, k = k0 + 4 * (f % 8);
             if (r < rows && k < K) v[i] = *reinterpret_cast<const float4 *>(X + (size_t)r * ld + k);
         } else {
-            const int k = k0 + (t & 31), r = r0 + 4 * ((t >> 5) + 8 * i);
+            const int k = k0 + (t >> 5) + 8 * i, r = r0 + 4 * (t & 31);
             if (k < K && r < rows) v[i] = *reinterpret_cast<const float4 *>(X + (size_t)k * ld + r);
         }
     }
 }
 
+// Byte offset of the 16 bytes holding rows r..r+3 (r a multiple of 4) at
+// column k in an MN-major tile of 128 rows x 32 k, in the tensor cores'
+// MN-major tf32 layout "128-byte swizzle, 32-byte atomicity" (layout type 1;
+// the only MN-major layout they take for 32-bit operands): atoms of 4 k-rows
+// x 32 rows (512 bytes; k-row kr at kr * 128, its 32-byte chunk c of 8 rows
+// at (c ^ kr) * 32), the four row atoms 512 bytes apart (the descriptor's
+// leading offset) and the eight k atoms 2048 bytes apart (its stride offset).
+__device__ __forceinline__ uint32_t mn_sw128(int r, int k)
+{
+    const int kr = k & 3, c = (r >> 3) & 3;
+    return (uint32_t)((k >> 2) * 2048 + (r >> 5) * 512 + kr * 128 + ((c ^ kr) * 32) + (r & 4) * 4);
+}
+
+// Split a thread's loaded values into hi and lo and store them in the
+// tile's layout: K-major for K_CONTIG operands, MN-major for the others.
 template <bool K_CONTIG>
 __device__ __forceinline__ void store_tile(uint8_t *hi_t, uint8_t *lo_t, const float4 (&v)[4])
 {
@@ -128,21 +145,25 @@ __device__ __forceinline__ void store_tile(uint8_t *hi_t, uint8_t *lo_t, const f
     for (int i = 0; i < 4; i++) {
         uint4 h, l;
         split4(v[i], h, l);
+        uint32_t off;
         if (K_CONTIG) {
-            const int f = t + TC_PROD * i, r = f / 8, c = f % 8;
-            *reinterpret_cast<uint4 *>(hi_t + sw128(r, c)) = h;
-            *reinterpret_cast<uint4 *>(lo_t + sw128(r, c)) = l;
+            const int f = t + TC_PROD * i;
+            off = sw128(f / 8, f % 8);
         } else {
-            // lane = k: four rows r..r+3 at column k (chunk k / 4, word k % 4)
-            const int k = t & 31, r = 4 * ((t >> 5) + 8 * i), c = k >> 2, w = (k & 3) * 4;
-            const uint32_t hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                *reinterpret_cast<uint32_t *>(hi_t + sw128(r + j, c) + w) = hv[j];
-                *reinterpret_cast<uint32_t *>(lo_t + sw128(r + j, c) + w) = lv[j];
-            }
+            off = mn_sw128(4 * (t & 31), (t >> 5) + 8 * i);
         }
+        *reinterpret_cast<uint4 *>(hi_t + off) = h;
+        *reinterpret_cast<uint4 *>(lo_t + off) = l;
     }
+}
+
+// UMMA shared-memory descriptor of that MN-major tile (version 1, layout
+// type 1 = 128-byte swizzle with 32-byte atomicity): leading offset 512 bytes
+// between 32-row atoms, stride offset 2048 bytes between 4-k atoms.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr)
+{
+    return (uint64_t)((smem_addr >> 4) & 0x3FFF) | ((uint64_t)(512 >> 4) << 16) | ((uint64_t)(2048 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)1 << 61);
 }
 
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8])
@@ -276,7 +297,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
 
     if (warp == TC_MMA_WARP) {
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc(2, TC_N, TC_M);
+            // MMA A = the B^T tile (MN-major when B is not transposed), MMA B = the A tile (MN-major when A is)
+            const uint32_t idesc = umma_idesc(2, TC_N, TC_M) | (TB ? 0u : 1u << 15) | (TA ? 1u << 16 : 0u);
             for (int kb = 0; kb < nk; kb++) {
                 const int s = kb % TC_ST, c = kb / TC_CH, b = c & 1;
                 const bool chunk_start = kb % TC_CH == 0;
@@ -295,9 +317,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
                 const uint32_t d_chunk = tmem + (uint32_t)(b * 128), d_corr = tmem + TC_COL_CORR;
 #pragma unroll
                 for (int kk = 0; kk < TC_K / 8; kk++) {
-                    const uint32_t o = kk * 32;
-                    const uint64_t d_bh = umma_desc_sw128(bh + o), d_bl = umma_desc_sw128(bl + o);
-                    const uint64_t d_ah = umma_desc_sw128(ah + o), d_al = umma_desc_sw128(al + o);
+                    // a K=8 step is 32 bytes into a K-major tile's rows, two 2048-byte k atoms of an MN-major one
+                    const uint64_t d_bh = TB ? umma_desc_sw128(bh + kk * 32) : umma_desc_mn_sw128(bh + kk * 4096);
+                    const uint64_t d_bl = TB ? umma_desc_sw128(bl + kk * 32) : umma_desc_mn_sw128(bl + kk * 4096);
+                    const uint64_t d_ah = TA ? umma_desc_mn_sw128(ah + kk * 4096) : umma_desc_sw128(ah + kk * 32);
+                    const uint64_t d_al = TA ? umma_desc_mn_sw128(al + kk * 4096) : umma_desc_sw128(al + kk * 32);
                     umma_tf32(d_chunk, d_bh, d_ah, idesc, !(chunk_start && kk == 0));
                     umma_tf32(d_corr, d_bh, d_al, idesc, !(kb == 0 && kk == 0));
                     umma_tf32(d_corr, d_bl, d_ah, idesc, 1u);

@@ -180,7 +180,10 @@ SgemmPlan sgemm_plan(int M, int N, int K, int num_sms)
     SgemmPlan p;
     p.tiles_m = cdiv(M, BM);
     p.tiles_n = cdiv(N, BN);
-    const int tiles = p.tiles_m * p.tiles_n;
+    // the tensor-core kernel (products of 2^24 multiply-adds and more) has
+    // 128 x sgemm_tc_tile_m(M) output tiles: the K split is sized for those
+    const bool tc = (double)M * N * K >= 16.0 * 1024 * 1024;
+    const int tiles = tc ? cdiv(M, sgemm_tc_tile_m(M)) * cdiv(N, 128) : p.tiles_m * p.tiles_n;
     p.splits = 1;
     if (K <= 0) { p.k_per_split = BK; return p; }
     // split K when the output tiles cannot fill the SMs and K is long enough

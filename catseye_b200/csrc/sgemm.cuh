@@ -27,6 +27,7 @@ cudaError_t launch_splitk_reduce(int M, int N, int splits, float alpha, const fl
 // tensor-core (3xTF32) path
 bool sgemm_tc_usable(bool ta, bool tb, int M, int N, int K, const float *A, int lda, const float *B, int ldb);
 size_t sgemm_tc_smem_bytes();
+int sgemm_tc_tile_m(int M);   // m rows per tensor-core CTA: 256, or 128 when M <= 128
 cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, int K, float alpha, const float *A,
                             int lda, const float *B, int ldb, float beta, float *C, int ldc, float *work, int *err,
                             cudaStream_t st);

@@ -84,20 +84,20 @@ struct TcBars {
     int commits[3], chunk_commits;
 };
 
-__device__ __forceinline__ uint32_t to_tf32(float x)
-{
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+// Round an fp32 bit pattern to tf32 (10 stored mantissa bits), to nearest
+// with ties away from zero: add half of the last kept place to the 13 dropped
+// bits and clear them (a carry moves into the exponent, as rounding up
+// should).  Two integer operations.  A NaN may come out as a zero or another
+// NaN, but x - hi is then NaN, so the product still is.
+__device__ __forceinline__ uint32_t tf32_rna(uint32_t b) { return (b + 0x1000u) & 0xFFFFE000u; }
 
-// hi and lo of four floats
+// hi and lo of four floats: hi = tf32(x), lo = tf32(x - hi)
 __device__ __forceinline__ void split4(float4 v, uint4 &hi, uint4 &lo)
 {
-    hi.x = to_tf32(v.x); lo.x = to_tf32(v.x - __uint_as_float(hi.x));
-    hi.y = to_tf32(v.y); lo.y = to_tf32(v.y - __uint_as_float(hi.y));
-    hi.z = to_tf32(v.z); lo.z = to_tf32(v.z - __uint_as_float(hi.z));
-    hi.w = to_tf32(v.w); lo.w = to_tf32(v.w - __uint_as_float(hi.w));
+    hi.x = tf32_rna(__float_as_uint(v.x)); lo.x = tf32_rna(__float_as_uint(v.x - __uint_as_float(hi.x)));
+    hi.y = tf32_rna(__float_as_uint(v.y)); lo.y = tf32_rna(__float_as_uint(v.y - __uint_as_float(hi.y)));
+    hi.z = tf32_rna(__float_as_uint(v.z)); lo.z = tf32_rna(__float_as_uint(v.z - __uint_as_float(hi.z)));
+    hi.w = tf32_rna(__float_as_uint(v.w)); lo.w = tf32_rna(__float_as_uint(v.w - __uint_as_float(hi.w)));
 }
 
 // One operand tile of a slice: ROWS rows (m or n) x 32 k, ROWS / 32 float4

@@ -62,7 +62,7 @@ extern "C" int cats_sgemm_dev_noalloc(char ta, char tb, int m, int n, int k, flo
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
         return capi_fail(CATS_ERR_CUDA, "cats_sgemm_dev_noalloc: no current device");
     if (int rc = scratch_setup(dev)) return rc;
-    const SgemmPlan p = sgemm_plan(m, n, k, g_scratch_sms[dev]);
+    const SgemmPlan p = sgemm_plan(m, n, k, g_scratch_sms[dev], CATS_SGEMM_NOALLOC_SCRATCH_FLOATS);
     if (p.work_floats > (size_t)CATS_SGEMM_NOALLOC_SCRATCH_FLOATS) {
         char msg[160];
         snprintf(msg, sizeof msg,

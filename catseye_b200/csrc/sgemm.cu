@@ -175,7 +175,7 @@ __global__ void k_splitk_reduce(int M, int N, int splits, float alpha, const flo
     }
 }
 
-SgemmPlan sgemm_plan(int M, int N, int K, int num_sms)
+SgemmPlan sgemm_plan(int M, int N, int K, int num_sms, size_t max_work_floats)
 {
     SgemmPlan p;
     p.tiles_m = cdiv(M, BM);
@@ -196,6 +196,21 @@ SgemmPlan sgemm_plan(int M, int N, int K, int num_sms)
     p.k_per_split = (int)round_up((size_t)cdiv(K, p.splits), 32);
     p.splits = cdiv(K, p.k_per_split);
     p.work_floats = p.splits > 1 ? (size_t)p.splits * M * N : 0;
+    // Tensor-core tiles beyond the last full wave: when they would occupy at
+    // most half of the SMs, split each into 2-4 K pieces so the last wave is
+    // as wide as the others and proportionally shorter.
+    if (tc && p.splits == 1 && tiles > num_sms) {
+        const int tail = tiles % num_sms;
+        const int s = std::min({4, tail > 0 ? num_sms / tail : 0, K / 512});
+        const int bm = sgemm_tc_tile_m(M);
+        const size_t wf = (size_t)tail * s * 128 * bm;
+        if (tail > 0 && 2 * tail <= num_sms && s >= 2 && wf <= max_work_floats) {
+            p.tail_tiles = tail;
+            p.tail_kps = (int)round_up((size_t)cdiv(K, s), 32);
+            p.tail_split = cdiv(K, p.tail_kps);
+            p.work_floats = (size_t)tail * p.tail_split * 128 * bm;
+        }
+    }
     return p;
 }
 

@@ -6,10 +6,15 @@ namespace cats {
 
 struct SgemmPlan {
     int tiles_m = 0, tiles_n = 0, splits = 1, k_per_split = 0;
-    size_t work_floats = 0;   // split-K partial-sum workspace (0 when splits == 1)
+    // tensor-core path with splits == 1: the last tail_tiles output tiles (the
+    // ones a last partial wave of CTAs would run alone) are computed in
+    // tail_split K pieces of tail_kps each, after the full tiles
+    int tail_tiles = 0, tail_split = 1, tail_kps = 0;
+    size_t work_floats = 0;   // partial-sum workspace (0 when nothing is split)
 };
 
-SgemmPlan sgemm_plan(int M, int N, int K, int num_sms);
+// max_work_floats caps the workspace: the tail split is only planned when it fits.
+SgemmPlan sgemm_plan(int M, int N, int K, int num_sms, size_t max_work_floats = (size_t)-1);
 
 // C[M][N] (leading dim ldc) = alpha * op(A) * op(B) + beta * C.  `work` must hold
 // plan.work_floats floats when plan.splits > 1.  Shapes the tensor cores can

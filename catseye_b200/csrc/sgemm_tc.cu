@@ -70,6 +70,10 @@ struct SgemmTcArgs {
     int ldc;
     float *work;        // K-split partials [splits][M][N] (splits > 1)
     int k_per_split;
+    int tiles_m;        // m tiles (tile t: m tile t % tiles_m, n tile t / tiles_m)
+    int main_tiles;     // tiles computed whole; the rest in tail_split K pieces of tail_kps
+    int tail_split, tail_kps;
+    float *tail_ws;     // tail pieces' partials [piece][TC_N x BM block, m-major]
     int *err;
 };
 
@@ -285,8 +289,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
     volatile int *abort_s = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * TC_N;
-    const int kb0 = blockIdx.z * a.k_per_split, kend = min(a.K, kb0 + a.k_per_split);
+    // work unit blockIdx.x: a whole tile, or K piece of a tail tile
+    const int unit = blockIdx.x, piece = unit - a.main_tiles;
+    const int tile = piece < 0 ? unit : a.main_tiles + piece / a.tail_split;
+    const int m0 = (tile % a.tiles_m) * BM, n0 = (tile / a.tiles_m) * TC_N;
+    const int kb0 = piece < 0 ? blockIdx.z * a.k_per_split : (piece % a.tail_split) * a.tail_kps;
+    const int kend = min(a.K, kb0 + (piece < 0 ? a.k_per_split : a.tail_kps));
     const int nk = kend > kb0 ? (kend - kb0 + TC_K - 1) / TC_K : 0;
     const int nc = (nk + TC_CH - 1) / TC_CH;
 
@@ -375,8 +383,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         const int q = warp & 3, half = warp >> 2;
         const int n = n0 + q * 32 + lane;
         const uint32_t lanes = tmem + ((uint32_t)(q * 32) << 16);
-        float *dst = a.work ? a.work + (size_t)blockIdx.z * a.M * a.N : a.C;
-        const int ld = a.work ? a.N : a.ldc;
+        // destination: C, a K split's slab [M][N], or a tail piece's block [m - m0][n - n0]
+        float *dst = piece >= 0 ? a.tail_ws + (size_t)piece * TC_N * BM
+                     : a.work   ? a.work + (size_t)blockIdx.z * a.M * a.N
+                                : a.C;
+        const int ld = piece >= 0 ? TC_N : a.work ? a.N : a.ldc;
+        const int mo = piece >= 0 ? m0 : 0, no = piece >= 0 ? n0 : 0;
+        const bool raw_sum = piece >= 0 || a.work;
 #pragma unroll 1
         for (int c0 = half * (BM / 2); c0 < (half + 1) * (BM / 2); c0 += 8) {
             float acc[8];
@@ -394,9 +407,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
                 for (int j = 0; j < 8; j++) {
                     const int m = m0 + c0 + j;
                     if (m >= a.M) break;
-                    float *p = dst + (size_t)m * ld + n;
+                    float *p = dst + (size_t)(m - mo) * ld + (n - no);
                     if (!good) *p = __int_as_float(0x7fc00000);   // a timed-out tile reads as NaN
-                    else if (a.work) *p = acc[j];
+                    else if (raw_sum) *p = acc[j];
                     else *p = a.beta == 0.f ? a.alpha * acc[j] : fmaf(a.alpha, acc[j], a.beta * *p);
                 }
             }
@@ -461,14 +474,50 @@ static cudaError_t launch_tc_t(dim3 grid, const SgemmTcArgs &a, cudaStream_t st)
     return cudaGetLastError();
 }
 
+// C = alpha * (sum of a tail tile's K pieces, in piece order) + beta * C
 template <int BM>
-static cudaError_t launch_tc_bm(bool ta, bool tb, const SgemmTcArgs &a, int splits, cudaStream_t st)
+__global__ void k_tail_reduce(const __grid_constant__ SgemmTcArgs a, int tail_tiles)
 {
-    const dim3 grid(cdiv(a.M, BM), cdiv(a.N, TC_N), splits);   // x: m tiles, y: n tiles, z: K splits
+    constexpr int TE = TC_N * BM;   // one tile's block in the workspace: [m - m0][n - n0]
+    const size_t total = (size_t)tail_tiles * TE;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / TE), e = (int)(i % TE);
+        const int tile = a.main_tiles + t;
+        const int m = (tile % a.tiles_m) * BM + e / TC_N, n = (tile / a.tiles_m) * TC_N + e % TC_N;
+        if (m >= a.M || n >= a.N) continue;
+        const float *w = a.tail_ws + (size_t)t * a.tail_split * TE + e;
+        float sum = 0.f;
+        for (int q = 0; q < a.tail_split; q++) sum += w[(size_t)q * TE];
+        float *p = a.C + (size_t)m * a.ldc + n;
+        *p = a.beta == 0.f ? a.alpha * sum : fmaf(a.alpha, sum, a.beta * *p);
+    }
+}
+
+template <int BM>
+static cudaError_t launch_tc_bm(bool ta, bool tb, const SgemmTcArgs &a, int units, int splits, cudaStream_t st)
+{
+    const dim3 grid(units, 1, splits);
     if (!ta && !tb) return launch_tc_t<false, false, BM>(grid, a, st);
     if (!ta && tb) return launch_tc_t<false, true, BM>(grid, a, st);
     if (ta && !tb) return launch_tc_t<true, false, BM>(grid, a, st);
     return launch_tc_t<true, true, BM>(grid, a, st);
+}
+
+template <int BM>
+static cudaError_t launch_tc(const SgemmPlan &p, bool ta, bool tb, SgemmTcArgs &a, cudaStream_t st)
+{
+    a.tiles_m = cdiv(a.M, BM);
+    const int tiles = a.tiles_m * cdiv(a.N, TC_N);
+    const bool tail = p.splits == 1 && p.tail_tiles > 0 && p.tail_tiles < tiles;
+    a.main_tiles = tail ? tiles - p.tail_tiles : tiles;
+    a.tail_split = tail ? p.tail_split : 1;
+    a.tail_kps = tail ? p.tail_kps : 0;
+    const int units = a.main_tiles + (tail ? p.tail_tiles * p.tail_split : 0);
+    cudaError_t e = launch_tc_bm<BM>(ta, tb, a, units, p.splits, st);
+    if (e || !tail) return e;
+    const size_t total = (size_t)p.tail_tiles * TC_N * BM;
+    k_tail_reduce<BM><<<(int)std::min<size_t>((total + 255) / 256, 148 * 8), 256, 0, st>>>(a, p.tail_tiles);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, int K, float alpha, const float *A,
@@ -476,6 +525,8 @@ cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, 
                             cudaStream_t st)
 {
     if (p.k_per_split % TC_K || (long long)p.k_per_split * p.splits < K) return cudaErrorInvalidValue;
+    if (p.tail_tiles > 0 && (p.tail_kps % TC_K || (long long)p.tail_kps * p.tail_split < K || !work))
+        return cudaErrorInvalidValue;
     SgemmTcArgs a;
     a.M = M; a.N = N; a.K = K;
     a.alpha = alpha; a.beta = beta;
@@ -483,9 +534,9 @@ cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, 
     a.C = C; a.ldc = ldc;
     a.work = p.splits > 1 ? work : nullptr;
     a.k_per_split = p.k_per_split;
+    a.tail_ws = work;
     a.err = err;
-    const cudaError_t e = sgemm_tc_tile_m(M) == 256 ? launch_tc_bm<256>(ta, tb, a, p.splits, st)
-                                                    : launch_tc_bm<128>(ta, tb, a, p.splits, st);
+    const cudaError_t e = sgemm_tc_tile_m(M) == 256 ? launch_tc<256>(p, ta, tb, a, st) : launch_tc<128>(p, ta, tb, a, st);
     if (e || p.splits == 1) return e;
     return launch_splitk_reduce(M, N, p.splits, alpha, work, beta, C, ldc, st);
 }

@@ -50,10 +50,11 @@ def test_sgemm_shapes(mm, orc, ta, tb, M, N, K):
 # Shapes the tensor-core (3xTF32) kernel takes: M*N*K >= 2^24 with the
 # contiguous extents a multiple of 4.  Ragged edges in every dimension, K
 # tails shorter than one 32-deep slice, K splits (few output tiles, long K),
-# a single output row block, and a long-K product whose error budget is the
-# tightest.
+# a single output row block, a long-K product whose error budget is the
+# tightest, and 160 output tiles on 148 SMs (the 12 past the last full wave
+# run as 3 K pieces each, summed afterwards).
 TC_SHAPES = [(300, 260, 1000), (196, 4100, 36), (4, 4096, 1024), (1024, 1024, 8192), (132, 516, 2052),
-             (128, 128, 4096), (2048, 64, 1536)]
+             (128, 128, 4096), (2048, 64, 1536), (2500, 2020, 2000)]
 
 
 @pytest.mark.parametrize("ta,tb", [("N", "N"), ("N", "T"), ("T", "N"), ("T", "T")])

@@ -39,6 +39,7 @@
 // Every wait is bounded; a CTA whose wait timed out writes its tile as NaN
 // (and sets the error word when one is given); TMEM is freed on every path.
 #include "sgemm.cuh"
+#include "conv.cuh"
 #include "tc.cuh"
 #include <algorithm>
 
@@ -57,7 +58,7 @@ struct TcCfg {
     static constexpr uint32_t BT = TC_N * 128;           // one 128-row x 32-float tile (B^T hi or lo)
     static constexpr uint32_t AT = BM * 128;             // one BM-row x 32-float tile (A hi or lo)
     static constexpr uint32_t STAGE = 2 * BT + 2 * AT;   // B^T hi, B^T lo, A hi, A lo
-    static constexpr int ST = BM == 256 ? 2 : 3;
+    static constexpr int ST = BM == 256 ? 2 : BM == 128 ? 3 : 4;
     static constexpr uint32_t TCOLS = 2 * BM;            // chunk accumulator + running sum
 };
 
@@ -75,17 +76,26 @@ struct SgemmTcArgs {
     int tail_split, tail_kps;
     float *tail_ws;     // tail pieces' partials [piece][TC_N x BM block, m-major]
     int *err;
+    // convolution mode: B = im2col(x), k = (ci * ks + ky) * ks + kx, n = (b, oy, ox);
+    // C = z[b][m][oy * ow + ox]
+    const float *x;
+    int ich, h, wd, ks, pad, stride, ow, ohw;
 };
+
+// Shared-memory table of the convolution's k index (conv mode, after TcBars):
+// the element offset ci * h * wd + ky * wd + kx and (ky << 16) | kx; k >= K
+// gets ky = 0x4000, which no bounds test passes.
+constexpr int TC_CONV_MAX_K = 2304;
 
 // Shared-memory barriers and flags after the stages.
 struct TcBars {
-    uint64_t full[3], empty[3];
+    uint64_t full[4], empty[4];
     uint64_t chunk_done;      // the chunk accumulator is complete (tcgen05.commit)
     uint64_t drained;         // the producers have folded it into the sum (8 warp arrivals)
     uint64_t done;            // every MMA of the CTA has completed
     uint32_t tmem;
     int abort;
-    int commits[3], chunk_commits;
+    int commits[4], chunk_commits;
 };
 
 // Round an fp32 bit pattern to tf32 (10 stored mantissa bits), to nearest
@@ -229,14 +239,76 @@ __device__ __forceinline__ bool flush_chunk(TcBars *bars, uint32_t tmem, int c, 
     return true;
 }
 
+// Convolution mode: a producer thread's four output pixels n0 + lane + 32 j
+// as an element offset (b * ich * h * wd + iy0 * wd + ix0) and the input
+// corner (iy0, ix0); pixels past N get a corner no bounds test passes.
+struct ConvPix {
+    int base[4], iy0[4], ix0[4];
+};
+
+__device__ __forceinline__ void conv_pixels(const SgemmTcArgs &a, int n0, ConvPix &cp)
+{
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int n = n0 + lane + 32 * j;
+        const int b = n / a.ohw, p = n - b * a.ohw, oy = p / a.ow, ox = p - oy * a.ow;
+        cp.iy0[j] = n < a.N ? oy * a.stride - a.pad : -0x40000;
+        cp.ix0[j] = ox * a.stride - a.pad;
+        cp.base[j] = n < a.N ? (b * a.ich * a.h + cp.iy0[j]) * a.wd + cp.ix0[j] : 0;
+    }
+}
+
+// The im2col tile of slice k0: thread (warp w, lane) gathers k = k0 + w + 8 i
+// for its four pixels into v[i] (component j = pixel lane + 32 j); lanes are
+// consecutive pixels, so each load instruction reads a contiguous row span.
+__device__ __forceinline__ void gather_tile(const SgemmTcArgs &a, const int2 *ktab, const ConvPix &cp, int k0,
+                                            float4 (&v)[4])
+{
+    const int w = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int2 e = ktab[k0 + w + 8 * i];
+        const int ky = e.y >> 16, kx = e.y & 0xffff;
+        float r[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int iy = cp.iy0[j] + ky, ix = cp.ix0[j] + kx;
+            r[j] = ((unsigned)iy < (unsigned)a.h && (unsigned)ix < (unsigned)a.wd) ? __ldg(a.x + cp.base[j] + e.x) : 0.f;
+        }
+        v[i] = make_float4(r[0], r[1], r[2], r[3]);
+    }
+}
+
+// Store a gathered tile as hi and lo in the MN-major layout of the B^T
+// tile: element (pixel lane + 32 j, k w + 8 i), 4-byte stores; the 32 lanes
+// of an instruction fill one 128-byte k-row, each bank once.
+__device__ __forceinline__ void store_gathered(uint8_t *hi_t, uint8_t *lo_t, const float4 (&v)[4])
+{
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int r = lane + 32 * j;
+            const uint32_t off = mn_sw128<TC_N>(r & ~3, w + 8 * i) + (r & 3) * 4;
+            const uint32_t hb = tf32_rna(__float_as_uint(e[j]));
+            *reinterpret_cast<uint32_t *>(hi_t + off) = hb;
+            *reinterpret_cast<uint32_t *>(lo_t + off) = tf32_rna(__float_as_uint(e[j] - __uint_as_float(hb)));
+        }
+    }
+}
+
 // One slice kb for the producers: fold the previous chunk into the sum when
 // kb is the second slice of a chunk, wait for the slice's stage to be free,
 // split the registers' fp32 values into hi and lo tiles, load slice kb + 2
 // into the same registers and hand the stage to the MMA warp.
-template <bool TA, bool TB, int BM>
+template <bool TA, bool TB, int BM, bool CONV>
 __device__ __forceinline__ bool produce(const SgemmTcArgs &a, uint8_t *smem, TcBars *bars, uint32_t tmem, int kb,
                                         int nk, int kb0, int kend, int m0, int n0, int &flushed,
-                                        float4 (&va)[BM / 32], float4 (&vb)[TC_N / 32])
+                                        float4 (&va)[BM / 32], float4 (&vb)[TC_N / 32], const int2 *ktab,
+                                        const ConvPix &cp)
 {
     using Cfg = TcCfg<BM>;
     if (kb % TC_CH == 1 && kb > TC_CH) {
@@ -249,11 +321,13 @@ __device__ __forceinline__ bool produce(const SgemmTcArgs &a, uint8_t *smem, TcB
                             CATS_DEVERR_MBAR_EMPTY);
     if (!__all_sync(0xffffffffu, ok)) return false;
     uint8_t *st = smem + s * Cfg::STAGE;
-    store_tile<TB, TC_N>(st, st + Cfg::BT, vb);
+    if (CONV) store_gathered(st, st + Cfg::BT, vb);
+    else store_tile<TB, TC_N>(st, st + Cfg::BT, vb);
     store_tile<!TA, BM>(st + 2 * Cfg::BT, st + 2 * Cfg::BT + Cfg::AT, va);
     if (kb + 2 < nk) {
         load_tile<!TA, BM>(a.A, a.lda, a.M, kend, m0, kb0 + (kb + 2) * TC_K, va);
-        load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + (kb + 2) * TC_K, vb);
+        if (CONV) gather_tile(a, ktab, cp, kb0 + (kb + 2) * TC_K, vb);
+        else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + (kb + 2) * TC_K, vb);
     }
     fence_proxy_async_smem();
     __syncwarp();
@@ -277,7 +351,7 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar)
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <bool TA, bool TB, int BM>
+template <bool TA, bool TB, int BM, bool CONV = false>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constant__ SgemmTcArgs a)
 {
     using Cfg = TcCfg<BM>;
@@ -287,6 +361,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
     uint8_t *smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
     TcBars *bars = reinterpret_cast<TcBars *>(smem + ST * Cfg::STAGE);
     volatile int *abort_s = &bars->abort;
+    int2 *ktab = reinterpret_cast<int2 *>(bars + 1);   // conv mode only
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // work unit blockIdx.x: a whole tile, or K piece of a tail tile
@@ -310,6 +385,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         bars->chunk_commits = 0;
         bars->abort = 0;
         fence_barrier_init();
+    }
+    if (CONV) {
+        const int kk2 = a.ks * a.ks, kpad = (a.K + TC_K - 1) / TC_K * TC_K;
+        for (int k = threadIdx.x; k < kpad; k += blockDim.x) {
+            const int ci = k / kk2, r = k - ci * kk2, ky = r / a.ks, kx = r - ky * a.ks;
+            ktab[k] = k < a.K ? make_int2((ci * a.h + ky) * a.wd + kx, (ky << 16) | kx) : make_int2(0, 0x4000 << 16);
+        }
     }
     if (warp == TC_MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -360,19 +442,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         // ---------------- producers: two slices in flight in registers
         float4 va0[BM / 32], vb0[TC_N / 32], va1[BM / 32], vb1[TC_N / 32];
         int flushed = 0;   // chunks folded into the sum so far
+        ConvPix cp;
+        if (CONV) conv_pixels(a, n0, cp);
         if (nk > 0) {
             load_tile<!TA, BM>(a.A, a.lda, a.M, kend, m0, kb0, va0);
-            load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0, vb0);
+            if (CONV) gather_tile(a, ktab, cp, kb0, vb0);
+            else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0, vb0);
         }
         if (nk > 1) {
             load_tile<!TA, BM>(a.A, a.lda, a.M, kend, m0, kb0 + TC_K, va1);
-            load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + TC_K, vb1);
+            if (CONV) gather_tile(a, ktab, cp, kb0 + TC_K, vb1);
+            else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + TC_K, vb1);
         }
         bool live = true;
         for (int kb = 0; kb < nk && live; kb += 2) {
-            live = produce<TA, TB, BM>(a, smem, bars, tmem, kb, nk, kb0, kend, m0, n0, flushed, va0, vb0);
+            live = produce<TA, TB, BM, CONV>(a, smem, bars, tmem, kb, nk, kb0, kend, m0, n0, flushed, va0, vb0, ktab,
+                                             cp);
             if (live && kb + 1 < nk)
-                live = produce<TA, TB, BM>(a, smem, bars, tmem, kb + 1, nk, kb0, kend, m0, n0, flushed, va1, vb1);
+                live = produce<TA, TB, BM, CONV>(a, smem, bars, tmem, kb + 1, nk, kb0, kend, m0, n0, flushed, va1,
+                                                 vb1, ktab, cp);
         }
         // a last chunk of a single slice: its predecessor is folded here
         if (live && flushed < nc - 1) live = flush_chunk<BM>(bars, tmem, flushed++, a.err);
@@ -383,12 +471,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         const int q = warp & 3, half = warp >> 2;
         const int n = n0 + q * 32 + lane;
         const uint32_t lanes = tmem + ((uint32_t)(q * 32) << 16);
-        // destination: C, a K split's slab [M][N], or a tail piece's block [m - m0][n - n0]
+        // destination: C, a K split's slab [M][N], or a tail piece's block [m - m0][n - n0];
+        // conv mode: z[b][m][p] for pixel n = b * ohw + p
         float *dst = piece >= 0 ? a.tail_ws + (size_t)piece * TC_N * BM
                      : a.work   ? a.work + (size_t)blockIdx.z * a.M * a.N
                                 : a.C;
-        const int ld = piece >= 0 ? TC_N : a.work ? a.N : a.ldc;
-        const int mo = piece >= 0 ? m0 : 0, no = piece >= 0 ? n0 : 0;
+        const int ld = CONV ? a.ohw : piece >= 0 ? TC_N : a.work ? a.N : a.ldc;
+        const int mo = piece >= 0 ? m0 : 0;
+        size_t noff = (size_t)(n - (piece >= 0 ? n0 : 0));
+        if (CONV) {
+            const int b = n / a.ohw;
+            noff = (size_t)b * a.M * a.ohw + (n - b * a.ohw);
+        }
         const bool raw_sum = piece >= 0 || a.work;
 #pragma unroll 1
         for (int c0 = half * (BM / 2); c0 < (half + 1) * (BM / 2); c0 += 8) {
@@ -407,7 +501,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
                 for (int j = 0; j < 8; j++) {
                     const int m = m0 + c0 + j;
                     if (m >= a.M) break;
-                    float *p = dst + (size_t)(m - mo) * ld + (n - no);
+                    float *p = dst + (size_t)(m - mo) * ld + noff;
                     if (!good) *p = __int_as_float(0x7fc00000);   // a timed-out tile reads as NaN
                     else if (raw_sum) *p = acc[j];
                     else *p = a.beta == 0.f ? a.alpha * acc[j] : fmaf(a.alpha, acc[j], a.beta * *p);
@@ -441,9 +535,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
 }
 
 template <int BM>
-static size_t smem_bytes()
+static size_t smem_bytes(int conv_kpad = 0)
 {
-    return 1024 + (size_t)TcCfg<BM>::ST * TcCfg<BM>::STAGE + sizeof(TcBars);
+    return 1024 + (size_t)TcCfg<BM>::ST * TcCfg<BM>::STAGE + sizeof(TcBars) + (size_t)conv_kpad * sizeof(int2);
 }
 
 size_t sgemm_tc_smem_bytes() { return std::max(smem_bytes<128>(), smem_bytes<256>()); }
@@ -539,6 +633,80 @@ cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, 
     const cudaError_t e = sgemm_tc_tile_m(M) == 256 ? launch_tc<256>(p, ta, tb, a, st) : launch_tc<128>(p, ta, tb, a, st);
     if (e || p.splits == 1) return e;
     return launch_splitk_reduce(M, N, p.splits, alpha, work, beta, C, ldc, st);
+}
+
+// ---------------------------------------------------------------- convolution
+
+bool conv_tc_usable(const float *w, int batch, int ich, int h, int wd, int ch, int ks, int pad, int stride)
+{
+    if (batch <= 0 || ich <= 0 || ch <= 0 || ch > 256 || ks <= 0 || stride <= 0) return false;
+    const int oh = conv_out(h, ks, pad, stride), ow = conv_out(wd, ks, pad, stride);
+    // the k table's invalid entry (ky = 0x4000) must fail every bounds test
+    if (oh <= 0 || ow <= 0 || ks >= 0x4000 || h + pad >= 0x4000 || wd >= 0x4000) return false;
+    const long long K = (long long)ich * ks * ks, N = (long long)batch * oh * ow;
+    // float4 weight loads along k; 32-bit offsets into the images; worth a tensor-core launch
+    if (K % 4 || K > TC_CONV_MAX_K || (uintptr_t)w % 16) return false;
+    if ((long long)batch * ich * h * wd >= (1LL << 31) || N >= (1LL << 31) || (long long)ch * N >= (1LL << 31))
+        return false;
+    return (double)ch * N * K >= 16.0 * 1024 * 1024;
+}
+
+template <int BM>
+static cudaError_t launch_conv_bm(const SgemmTcArgs &a, cudaStream_t st)
+{
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_sgemm_tc<false, false, BM, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem_bytes<BM>(TC_CONV_MAX_K));
+        if (e) return e;
+        attr = true;
+    }
+    const int kpad = (a.K + TC_K - 1) / TC_K * TC_K;
+    const int tiles = cdiv(a.M, BM) * cdiv(a.N, TC_N);
+    k_sgemm_tc<false, false, BM, true><<<tiles, TC_THREADS, smem_bytes<BM>(kpad), st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch, int ks,
+                           int pad, int stride, int *err, cudaStream_t st)
+{
+    if (!conv_tc_usable(w, batch, ich, h, wd, ch, ks, pad, stride)) return cudaErrorInvalidValue;
+    SgemmTcArgs a = {};
+    const int oh = conv_out(h, ks, pad, stride), ow = conv_out(wd, ks, pad, stride);
+    a.M = ch;
+    a.N = batch * oh * ow;
+    a.K = ich * ks * ks;
+    a.alpha = 1.f;
+    a.beta = 0.f;
+    a.A = w;
+    a.lda = a.K;
+    a.C = z;
+    a.k_per_split = (a.K + TC_K - 1) / TC_K * TC_K;
+    a.tail_split = 1;
+    a.err = err;
+    a.x = x;
+    a.ich = ich;
+    a.h = h;
+    a.wd = wd;
+    a.ks = ks;
+    a.pad = pad;
+    a.stride = stride;
+    a.ow = ow;
+    a.ohw = oh * ow;
+    if (ch <= 64) {
+        a.tiles_m = 1;
+        a.main_tiles = cdiv(a.N, TC_N);
+        return launch_conv_bm<64>(a, st);
+    }
+    if (ch <= 128) {
+        a.tiles_m = 1;
+        a.main_tiles = cdiv(a.N, TC_N);
+        return launch_conv_bm<128>(a, st);
+    }
+    a.tiles_m = cdiv(ch, 256);
+    a.main_tiles = a.tiles_m * cdiv(a.N, TC_N);
+    return launch_conv_bm<256>(a, st);
 }
 
 } // namespace cats

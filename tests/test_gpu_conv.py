@@ -46,7 +46,13 @@ def test_im2col_exact(mm, orc, c, h, w, kh, kw, ph, pw, sh, sw):
 CONVS = [(4, 3, 32, 32, 64, 3, 1, 1), (4, 64, 32, 32, 64, 3, 1, 1), (4, 64, 16, 16, 128, 3, 1, 1),
          (4, 128, 16, 16, 128, 3, 1, 1), (3, 8, 15, 17, 24, 3, 1, 2), (2, 6, 12, 10, 40, 3, 0, 1),
          (5, 16, 9, 9, 32, 1, 0, 1), (2, 5, 13, 11, 20, 5, 2, 1), (3, 7, 10, 10, 200, 3, 1, 1),
-         (1, 1, 1, 1, 1, 1, 0, 1), (7, 3, 5, 5, 96, 3, 1, 1)]
+         (1, 1, 1, 1, 1, 1, 0, 1), (7, 3, 5, 5, 96, 3, 1, 1),
+         # tensor-core (3xTF32) shapes: ch * N * K >= 2^24 with K a multiple of 4.  A
+         # 256-channel tile with 200 channels, stride 2 without padding and 96
+         # channels, 5x5 with 128-pixel tiles that straddle samples (oh * ow = 900),
+         # odd image sizes (255 pixels per sample), 1x1
+         (8, 32, 12, 12, 200, 3, 1, 1), (16, 16, 33, 33, 96, 3, 0, 2), (8, 4, 30, 30, 64, 5, 2, 1),
+         (8, 20, 15, 17, 48, 3, 1, 1), (16, 64, 16, 16, 128, 1, 0, 1)]
 
 
 @pytest.mark.parametrize("batch,ich,h,w,ch,ks,pad,stride", CONVS)

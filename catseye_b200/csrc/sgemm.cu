@@ -191,6 +191,11 @@ SgemmPlan sgemm_plan(int M, int N, int K, int num_sms, size_t max_work_floats)
     if (tiles < num_sms && K >= 512) {
         int s = std::min(cdiv(num_sms * 2, tiles), K / 256);
         p.splits = std::max(1, std::min(s, 32));
+    } else if (tiles < 16 && K >= 128) {
+        // a handful of tiles (a classifier layer): 64-deep splits, so one
+        // CTA does not walk K alone (when the workspace fits the cap)
+        const int s = std::max(1, std::min(cdiv(num_sms, tiles), K / 64));
+        if ((size_t)s * M * N <= max_work_floats) p.splits = s;
     }
     // whole 32-deep slices, the tensor-core kernel's unit (a multiple of BK)
     p.k_per_split = (int)round_up((size_t)cdiv(K, p.splits), 32);

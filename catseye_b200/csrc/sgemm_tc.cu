@@ -120,7 +120,7 @@ __device__ __forceinline__ void split4(float4 v, uint4 &hi, uint4 &lo)
 // per 128-byte row.  Else it is stored along rows (X[k][row], ld) and warp w
 // loads k = w + 8 (i % 4), rows 128 (i / 4) + 4 lane .. + 3: 512 contiguous
 // bytes of one k-row per warp instruction.
-template <bool K_CONTIG, int ROWS>
+template <bool K_CONTIG, int ROWS, bool SCALAR = false>
 __device__ __forceinline__ void load_tile(const float *__restrict__ X, int ld, int rows, int K, int r0, int k0,
                                           float4 (&v)[ROWS / 32])
 {
@@ -130,7 +130,17 @@ __device__ __forceinline__ void load_tile(const float *__restrict__ X, int ld, i
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (K_CONTIG) {
             const int f = t + TC_PROD * i, r = r0 + f / 8, k = k0 + 4 * (f % 8);
-            if (r < rows && k < K) v[i] = *reinterpret_cast<const float4 *>(X + (size_t)r * ld + k);
+            if (r < rows && k < K) {
+                if (!SCALAR) {
+                    v[i] = *reinterpret_cast<const float4 *>(X + (size_t)r * ld + k);
+                } else {   // rows not 16-byte aligned (a convolution's K = ich * ks^2 not a multiple of 4)
+                    const float *p = X + (size_t)r * ld + k;
+                    v[i].x = p[0];
+                    if (k + 1 < K) v[i].y = p[1];
+                    if (k + 2 < K) v[i].z = p[2];
+                    if (k + 3 < K) v[i].w = p[3];
+                }
+            }
         } else {
             const int k = k0 + (t >> 5) + 8 * (i & 3), r = r0 + 128 * (i >> 2) + 4 * (t & 31);
             if (k < K && r < rows) v[i] = *reinterpret_cast<const float4 *>(X + (size_t)k * ld + r);
@@ -304,7 +314,7 @@ __device__ __forceinline__ void store_gathered(uint8_t *hi_t, uint8_t *lo_t, con
 // kb is the second slice of a chunk, wait for the slice's stage to be free,
 // split the registers' fp32 values into hi and lo tiles, load slice kb + 2
 // into the same registers and hand the stage to the MMA warp.
-template <bool TA, bool TB, int BM, bool CONV>
+template <bool TA, bool TB, int BM, int CONV>
 __device__ __forceinline__ bool produce(const SgemmTcArgs &a, uint8_t *smem, TcBars *bars, uint32_t tmem, int kb,
                                         int nk, int kb0, int kend, int m0, int n0, int &flushed,
                                         float4 (&va)[BM / 32], float4 (&vb)[TC_N / 32], const int2 *ktab,
@@ -325,7 +335,7 @@ __device__ __forceinline__ bool produce(const SgemmTcArgs &a, uint8_t *smem, TcB
     else store_tile<TB, TC_N>(st, st + Cfg::BT, vb);
     store_tile<!TA, BM>(st + 2 * Cfg::BT, st + 2 * Cfg::BT + Cfg::AT, va);
     if (kb + 2 < nk) {
-        load_tile<!TA, BM>(a.A, a.lda, a.M, kend, m0, kb0 + (kb + 2) * TC_K, va);
+        load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0 + (kb + 2) * TC_K, va);
         if (CONV) gather_tile(a, ktab, cp, kb0 + (kb + 2) * TC_K, vb);
         else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + (kb + 2) * TC_K, vb);
     }
@@ -351,7 +361,9 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar)
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <bool TA, bool TB, int BM, bool CONV = false>
+// CONV: 0 GEMM, 1 convolution, 2 convolution whose weight rows are not
+// 16-byte aligned (scalar weight loads)
+template <bool TA, bool TB, int BM, int CONV = 0>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constant__ SgemmTcArgs a)
 {
     using Cfg = TcCfg<BM>;
@@ -445,12 +457,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         ConvPix cp;
         if (CONV) conv_pixels(a, n0, cp);
         if (nk > 0) {
-            load_tile<!TA, BM>(a.A, a.lda, a.M, kend, m0, kb0, va0);
+            load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0, va0);
             if (CONV) gather_tile(a, ktab, cp, kb0, vb0);
             else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0, vb0);
         }
         if (nk > 1) {
-            load_tile<!TA, BM>(a.A, a.lda, a.M, kend, m0, kb0 + TC_K, va1);
+            load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0 + TC_K, va1);
             if (CONV) gather_tile(a, ktab, cp, kb0 + TC_K, vb1);
             else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + TC_K, vb1);
         }
@@ -644,19 +656,21 @@ bool conv_tc_usable(const float *w, int batch, int ich, int h, int wd, int ch, i
     // the k table's invalid entry (ky = 0x4000) must fail every bounds test
     if (oh <= 0 || ow <= 0 || ks >= 0x4000 || h + pad >= 0x4000 || wd >= 0x4000) return false;
     const long long K = (long long)ich * ks * ks, N = (long long)batch * oh * ow;
-    // float4 weight loads along k; 32-bit offsets into the images; worth a tensor-core launch
-    if (K % 4 || K > TC_CONV_MAX_K || (uintptr_t)w % 16) return false;
+    // 32-bit offsets into the images; at least three 32-deep slices per tile (a
+    // shallower convolution is bound by writing its output, which the CUDA-core
+    // kernel does with less fixed cost per tile)
+    if (K > TC_CONV_MAX_K || K < 96) return false;
     if ((long long)batch * ich * h * wd >= (1LL << 31) || N >= (1LL << 31) || (long long)ch * N >= (1LL << 31))
         return false;
     return (double)ch * N * K >= 16.0 * 1024 * 1024;
 }
 
-template <int BM>
+template <int BM, int CONV>
 static cudaError_t launch_conv_bm(const SgemmTcArgs &a, cudaStream_t st)
 {
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_sgemm_tc<false, false, BM, true>,
+        cudaError_t e = cudaFuncSetAttribute(k_sgemm_tc<false, false, BM, CONV>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem_bytes<BM>(TC_CONV_MAX_K));
         if (e) return e;
@@ -664,8 +678,14 @@ static cudaError_t launch_conv_bm(const SgemmTcArgs &a, cudaStream_t st)
     }
     const int kpad = (a.K + TC_K - 1) / TC_K * TC_K;
     const int tiles = cdiv(a.M, BM) * cdiv(a.N, TC_N);
-    k_sgemm_tc<false, false, BM, true><<<tiles, TC_THREADS, smem_bytes<BM>(kpad), st>>>(a);
+    k_sgemm_tc<false, false, BM, CONV><<<tiles, TC_THREADS, smem_bytes<BM>(kpad), st>>>(a);
     return cudaGetLastError();
+}
+
+template <int BM>
+static cudaError_t launch_conv_bm(const SgemmTcArgs &a, bool scalar_w, cudaStream_t st)
+{
+    return scalar_w ? launch_conv_bm<BM, 2>(a, st) : launch_conv_bm<BM, 1>(a, st);
 }
 
 cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch, int ks,
@@ -681,6 +701,7 @@ cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, 
     a.beta = 0.f;
     a.A = w;
     a.lda = a.K;
+    const bool scalar_w = a.K % 4 != 0 || (uintptr_t)w % 16 != 0;
     a.C = z;
     a.k_per_split = (a.K + TC_K - 1) / TC_K * TC_K;
     a.tail_split = 1;
@@ -697,16 +718,16 @@ cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, 
     if (ch <= 64) {
         a.tiles_m = 1;
         a.main_tiles = cdiv(a.N, TC_N);
-        return launch_conv_bm<64>(a, st);
+        return launch_conv_bm<64>(a, scalar_w, st);
     }
     if (ch <= 128) {
         a.tiles_m = 1;
         a.main_tiles = cdiv(a.N, TC_N);
-        return launch_conv_bm<128>(a, st);
+        return launch_conv_bm<128>(a, scalar_w, st);
     }
     a.tiles_m = cdiv(ch, 256);
     a.main_tiles = a.tiles_m * cdiv(a.N, TC_N);
-    return launch_conv_bm<256>(a, st);
+    return launch_conv_bm<256>(a, scalar_w, st);
 }
 
 } // namespace cats

@@ -50,9 +50,11 @@ CONVS = [(4, 3, 32, 32, 64, 3, 1, 1), (4, 64, 32, 32, 64, 3, 1, 1), (4, 64, 16, 
          # tensor-core (3xTF32) shapes: ch * N * K >= 2^24 with K a multiple of 4.  A
          # 256-channel tile with 200 channels, stride 2 without padding and 96
          # channels, 5x5 with 128-pixel tiles that straddle samples (oh * ow = 900),
-         # odd image sizes (255 pixels per sample), 1x1
+         # odd image sizes (255 pixels per sample), 1x1, and K = 99 and 117 (weight
+         # rows not 16-byte aligned: scalar weight loads)
          (8, 32, 12, 12, 200, 3, 1, 1), (16, 16, 33, 33, 96, 3, 0, 2), (8, 4, 30, 30, 64, 5, 2, 1),
-         (8, 20, 15, 17, 48, 3, 1, 1), (16, 64, 16, 16, 128, 1, 0, 1)]
+         (8, 20, 15, 17, 48, 3, 1, 1), (16, 64, 16, 16, 128, 1, 0, 1), (16, 11, 20, 20, 40, 3, 1, 1),
+         (8, 13, 24, 24, 72, 3, 1, 1)]
 
 
 @pytest.mark.parametrize("batch,ich,h,w,ch,ks,pad,stride", CONVS)

@@ -42,8 +42,9 @@ token at a time, so its tok/s is its decode rate).
 4096^3 fp32 NN sgemm (cats_sgemm_dev), or the 32x32x3 CNN's four
 convolutions and two linear layers at batch 128 (cats_conv2d_forward_dev /
 cats_linear_forward_dev, 25.15 GFLOP).  value = GFLOP/s on device buffers;
-e2e = the host-pointer API with its copies; roofline against the nominal
-fp32 SIMT peak; cpu_baseline = the reference's gemm_rnn / layer forwards
+e2e = the host-pointer API with its copies; roofline against the 3xTF32
+tensor peak (the measured bf16 peak / 2 for tf32 / 3 products per fp32
+product), since both run on k_sgemm_tc; cpu_baseline = the reference's gemm_rnn / layer forwards
 (oracle/_ref, OpenMP on all cores) on a bounded sample.
 With torchrun (N > 1) every rank decodes its own replica (no collective on
 the data path yet): value = sum over ranks, time = max over ranks.
@@ -458,15 +459,6 @@ def layer_flops(L):
     return 2 * b * co * _conv_out(h, k, pad, s) * _conv_out(w, k, pad, s) * ci * k * k
 
 
-def fp32_peak():
-    """Nominal fp32 SIMT peak: 148 SMs x 128 FMA/clock x 2 x the max SM clock."""
-    mhz = 1965.0
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
-        mhz = float(json.load(open(p)).get("sm_max_mhz", mhz))
-    return 148 * 128 * 2 * mhz * 1e6 / 1e12
-
-
 def gemm_cpu_reference(workload):
     """The reference's own CPU code (oracle/_ref, OpenMP on all cores) on a bounded sample."""
     from oracle.cpu import Reference
@@ -633,16 +625,12 @@ def gemm_main(args):
         gfs = ws * flops * args.steps / (ms * 1e-3) / 1e9
         achieved = flops * args.steps / (ms * 1e-3) / 1e12
         cfg["parallelism"] = f"replicas{ws}" if ws > 1 else "single"
-        if args.workload == "sgemm_4096":
-            # 3xTF32 on tcgen05: three tf32 products per fp32 product, tf32 at half the bf16 rate
-            bf16, bf16_kind = tensor_peak()
-            peak = bf16 / 2 / 3
-            roof = {"bound": "tensor", "kernel": "k_sgemm_tc (3xTF32, tcgen05 kind::tf32)",
-                    "peak_kind": f"{bf16_kind} / 2 (tf32 rate) / 3 (products per fp32 product)"}
-        else:
-            peak = fp32_peak()
-            roof = {"bound": "fp32-simt", "kernel": "k_conv_fwd + k_sgemm_tc",
-                    "peak_kind": "nominal (148 SMs x 128 FMA/clock x 2 x max SM clock)"}
+        # 3xTF32 on tcgen05: three tf32 products per fp32 product, tf32 at half the bf16 rate
+        bf16, bf16_kind = tensor_peak()
+        peak = bf16 / 2 / 3
+        roof = {"bound": "tensor", "peak_kind": f"{bf16_kind} / 2 (tf32 rate) / 3 (products per fp32 product)",
+                "kernel": "k_sgemm_tc (3xTF32, tcgen05 kind::tf32)" if args.workload == "sgemm_4096"
+                else "k_sgemm_tc conv mode (3 of 4 convolutions) + k_conv_fwd (3->64) + k_sgemm(_tc) (linear)"}
         line = {"metric": metric, "value": round(gfs, 1), "unit": "GFLOP/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,

@@ -29,9 +29,12 @@ def _case(orc, t, n, d, T, seed):
 # (n, d, T): full 128 x 256 tiles; ragged rows and tokens; a partial last
 # 64-block segment (11008 = 5 x 2048 + 768); the smallest shapes; grids small
 # enough that K is split across CTAs (long K, few rows: 16 splits; the 7B w2
-# shape at batch 16)
+# shape at batch 16).  T <= 32 with n a multiple of 256 runs the narrow-tile
+# kernel (four K slices per stage): 16 and 32 tokens, 17 (ragged tokens in a
+# 32-wide tile), one token, and d = 1000 (a last tile whose rows + 32 i run out)
 SHAPES = [(4096, 4096, 512), (4096, 1000, 16), (11008, 4096, 100), (64, 128, 1), (8192, 256, 300),
-          (2048, 11008, 33), (128, 17, 7), (28672, 256, 16), (11008, 4096, 16)]
+          (2048, 11008, 33), (128, 17, 7), (28672, 256, 16), (11008, 4096, 16), (4096, 2048, 32),
+          (8192, 640, 17), (4096, 256, 1)]
 
 
 @pytest.mark.parametrize("t", [Q4_0, Q8_0])

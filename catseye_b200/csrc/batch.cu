@@ -37,6 +37,7 @@ namespace cats {
 
 constexpr int AT_THREADS = 256;
 constexpr int AT_KC = 32;          // cache positions per chunk
+constexpr int DEC_MAX_HS_ATT = 128; // head size k_attn_tok holds as one float4 per lane
 constexpr int AT_NQ = 64;          // query rows per CTA: tokens x the query heads of one kv head
 constexpr int AT_MAXHS = 128;
 
@@ -745,6 +746,76 @@ static int make_blocks(const LlmModel *m, const BatchTok *tok, int T, int2 *bloc
     return nb;
 }
 
+// Attention of single-token blocks (batched decode): one CTA per (block,
+// query head) and eight warps over the cache positions, four in flight per
+// warp, each lane holding four dimensions of q, k and v; every warp keeps its
+// own online softmax and the warps merge in shared memory (:1693-1722, the
+// same score, max-subtracted expf and weighted sum as k_attn_batch).
+constexpr int AK_WARPS = 8;
+
+__global__ void __launch_bounds__(AK_WARPS * 32) k_attn_tok(const __grid_constant__ AttnBatchArgs a)
+{
+    __shared__ float scr[AK_WARPS][DEC_MAX_HS_ATT + 4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int h = blockIdx.y, hs = a.hs;
+    const int tok = a.blocks[blockIdx.x].x;
+    const BatchTok bt = a.tok[tok];
+    const int T = bt.pos + 1;
+    const bool mine = lane * 4 < hs;
+    const float rs = sqrtf((float)hs);
+    const size_t base = (size_t)bt.seq * a.seq_stride + a.layer_off + (size_t)(h / a.kv_mul) * hs + lane * 4;
+    const float *kc = a.kc + base, *vc = a.vc + base;
+    constexpr int U = 4;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 qv = mine ? *(reinterpret_cast<const float4 *>(a.q + (size_t)tok * a.q_dim + h * hs) + lane) : z4;
+    float4 acc = z4;
+    float m = -INFINITY, lsum = 0.f;
+    for (int tb = warp * U; tb < T; tb += AK_WARPS * U) {
+        float4 kr[U], vr[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int t = min(tb + u, T - 1);   // clamped rows are loaded but not used
+            kr[u] = mine ? *reinterpret_cast<const float4 *>(kc + (size_t)t * a.kv_dim) : z4;
+            vr[u] = mine ? *reinterpret_cast<const float4 *>(vc + (size_t)t * a.kv_dim) : z4;
+        }
+        float dot[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) dot[u] = qv.x * kr[u].x + qv.y * kr[u].y + qv.z * kr[u].z + qv.w * kr[u].w;
+#pragma unroll
+        for (int u = 0; u < U; u++) dot[u] = warp_sum(dot[u]);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (tb + u >= T) break;
+            const float sc = __fdiv_rn(dot[u], rs);
+            const float mn = fmaxf(m, sc);
+            const float corr = expf(m - mn);
+            const float p = expf(sc - mn);
+            lsum = lsum * corr + p;
+            acc.x = acc.x * corr + p * vr[u].x;
+            acc.y = acc.y * corr + p * vr[u].y;
+            acc.z = acc.z * corr + p * vr[u].z;
+            acc.w = acc.w * corr + p * vr[u].w;
+            m = mn;
+        }
+    }
+    if (lane == 0) { scr[warp][0] = m; scr[warp][1] = lsum; }
+    if (mine) reinterpret_cast<float4 *>(&scr[warp][4])[lane] = acc;
+    __syncthreads();
+    if (tid < hs) {
+        float M = -INFINITY;
+        for (int w = 0; w < AK_WARPS; w++) M = fmaxf(M, scr[w][0]);
+        float L = 0.f, v = 0.f;
+        for (int w = 0; w < AK_WARPS; w++) {
+            const float mw = scr[w][0];
+            if (mw == -INFINITY) continue;
+            const float e = expf(mw - M);
+            L += e * scr[w][1];
+            v += e * scr[w][4 + tid];
+        }
+        a.xb[(size_t)tok * a.q_dim + h * hs + tid] = v / L;
+    }
+}
+
 static cudaError_t launch_attn_batch(LlmModel *m, int l, int nblocks, int max_rows, cudaStream_t st)
 {
     AttnBatchArgs a;
@@ -763,6 +834,11 @@ static cudaError_t launch_attn_batch(LlmModel *m, int l, int nblocks, int max_ro
     a.kv_mul = c.n_heads / c.n_kv_heads;
     a.seq_len = c.seq_len;
     a.n_seqs = m->n_seqs;
+    // single-token blocks (batched decode): a CTA per (block, query head)
+    if (max_rows == a.kv_mul && a.hs <= DEC_MAX_HS_ATT && a.hs % 4 == 0) {
+        k_attn_tok<<<dim3(nblocks, m->heads_loc), AK_WARPS * 32, 0, st>>>(a);
+        return cudaGetLastError();
+    }
     // blocks of 16 query rows or more (prefill) go to the tensor cores
     if (a.hs == MA_HS && max_rows >= 16) {
         const size_t smem = ma_smem_bytes();

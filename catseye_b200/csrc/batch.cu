@@ -42,6 +42,53 @@ constexpr int AT_NQ = 64;          // query rows per CTA: tokens x the query hea
 constexpr int AT_MAXHS = 128;
 
 // ------------------------------------------------------------- small kernels
+// A product's element i: y[i], or, for a K split the product left to its
+// reader (SplitOut), the sum of the partials in split order, the arithmetic
+// of the split-sum kernel.
+struct PartSrc {
+    const float *y;
+    const float *ws;
+    int splits;
+    long long count;   // elements of one partial slab ([T][d])
+
+    __device__ __forceinline__ float ld1(size_t i) const
+    {
+        if (splits <= 1) return y[i];
+        float p = 0.f;
+        for (int z = 0; z < splits; z++) p += ws[(size_t)z * count + i];
+        return p;
+    }
+    __device__ __forceinline__ float2 ld2(size_t i) const
+    {
+        if (splits <= 1) return *reinterpret_cast<const float2 *>(y + i);
+        float2 p = make_float2(0.f, 0.f);
+        for (int z = 0; z < splits; z++) {
+            const float2 v = *reinterpret_cast<const float2 *>(ws + (size_t)z * count + i);
+            p.x += v.x;
+            p.y += v.y;
+        }
+        return p;
+    }
+    __device__ __forceinline__ float4 ld4(size_t i) const
+    {
+        if (splits <= 1) return *reinterpret_cast<const float4 *>(y + i);
+        float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z = 0; z < splits; z++) {
+            const float4 v = *reinterpret_cast<const float4 *>(ws + (size_t)z * count + i);
+            p.x += v.x;
+            p.y += v.y;
+            p.z += v.z;
+            p.w += v.w;
+        }
+        return p;
+    }
+};
+
+static PartSrc part_src(const float *y, const SplitOut &so, long long count)
+{
+    return PartSrc{y, so.ws, so.splits, count};
+}
+
 // x[t] = emb[token_t] (dequantize(x, emb, token, dim) of an fp32 table, :1652)
 __global__ void k_embed(const BatchTok *__restrict__ bt, const float *__restrict__ emb, float *__restrict__ x, int dim,
                         int vocab, int *err)
@@ -57,15 +104,22 @@ __global__ void k_embed(const BatchTok *__restrict__ bt, const float *__restrict
 
 // rmsnorm (llm/catseye_llm.h:684-698: ss = mean(x^2) + 1e-5, o = w * (x / sqrt(ss)))
 // of token t's row, written as fp16 into the x16 operand.  One CTA per token.
-__global__ void __launch_bounds__(256) k_rmsnorm_x16(const float *__restrict__ x, const float *__restrict__ w,
-                                                     __half *__restrict__ x16, int n, int Tpad)
+// `add` (a residual product whose K split was left to this kernel): x += the
+// product first, and the sum is written back (the residual stream).
+__global__ void __launch_bounds__(256) k_rmsnorm_x16(float *__restrict__ x, const float *__restrict__ w,
+                                                     __half *__restrict__ x16, int n, int Tpad, PartSrc add)
 {
     __shared__ float red[8];
     const int t = blockIdx.x, tid = threadIdx.x;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)t * n);
+    float4 *xr = reinterpret_cast<float4 *>(x + (size_t)t * n);
     float ss = 0.f;
     for (int i = tid; i < n / 4; i += blockDim.x) {
-        const float4 v = xr[i];
+        float4 v = xr[i];
+        if (add.splits > 1) {
+            const float4 p = add.ld4((size_t)t * n + 4 * i);
+            v = make_float4(v.x + p.x, v.y + p.y, v.z + p.z, v.w + p.w);
+            xr[i] = v;
+        }
         ss = fmaf(v.x, v.x, ss);
         ss = fmaf(v.y, v.y, ss);
         ss = fmaf(v.z, v.z, ss);
@@ -92,7 +146,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm_x16(const float *__restrict__ x
 
 // RoPE (rope_llama, :1597-1620) on the q and k rows of the qkv product, q to
 // q[t], k and v into the cache at (sequence, layer, pos).  One thread per pair.
-__global__ void k_rope_kv(const float *__restrict__ y, int T, const BatchTok *__restrict__ bt, float *__restrict__ q,
+__global__ void k_rope_kv(PartSrc y, int T, const BatchTok *__restrict__ bt, float *__restrict__ q,
                           float *__restrict__ kc, float *__restrict__ vc, size_t seq_stride, size_t layer_off,
                           int q_dim, int kv_dim, int hs, int seq_len, int n_seqs, int *err)
 {
@@ -101,7 +155,7 @@ __global__ void k_rope_kv(const float *__restrict__ y, int T, const BatchTok *__
          i += (long long)gridDim.x * blockDim.x) {
         const int t = (int)(i / np), r0 = 2 * (int)(i % np);
         const BatchTok b = bt[t];
-        float2 v = *reinterpret_cast<const float2 *>(y + (size_t)t * qkv + r0);
+        float2 v = y.ld2((size_t)t * qkv + r0);
         if (r0 < q_dim) {
             rope_pair(v.x, v.y, r0, hs, b.pos);
             *reinterpret_cast<float2 *>(q + (size_t)t * q_dim + r0) = v;
@@ -121,21 +175,21 @@ __global__ void k_rope_kv(const float *__restrict__ y, int T, const BatchTok *__
 
 // SwiGLU of the interleaved [w1;w3] product (row 2i = w1_i x, 2i+1 = w3_i x):
 // h_i = silu(w1_i x) * (w3_i x) (:1744-1752), written as fp16 into x16.
-__global__ void k_swiglu_x16(const float *__restrict__ y, int T, int hidden, __half *__restrict__ x16, int Tpad)
+__global__ void k_swiglu_x16(PartSrc y, int T, int hidden, __half *__restrict__ x16, int Tpad)
 {
     const int cpr = hidden / 8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * cpr;
          i += (long long)gridDim.x * blockDim.x) {
         const int t = (int)(i / cpr), ci = (int)(i % cpr), kb = ci >> 3, c = ci & 7;
         const int e0 = kb * 64 + x16_src_off(c);
-        const float4 *row = reinterpret_cast<const float4 *>(y + (size_t)t * 2 * hidden);
+        const size_t row = (size_t)t * 2 * hidden;
         float h[8];
 #pragma unroll
         for (int run = 0; run < 2; run++) {
-            const float4 *src = row + (2 * (e0 + 16 * run)) / 4;
+            const size_t src = row + 2 * (e0 + 16 * run);
 #pragma unroll
             for (int j = 0; j < 2; j++) {
-                const float4 v = src[j];
+                const float4 v = y.ld4(src + 4 * j);
                 h[4 * run + 2 * j] = v.x * (1.f / (1.f + expf(-v.x))) * v.y;
                 h[4 * run + 2 * j + 1] = v.z * (1.f / (1.f + expf(-v.z))) * v.w;
             }
@@ -153,7 +207,7 @@ __global__ void k_add(float *__restrict__ x, const float *__restrict__ d, long l
 
 // Logits of token t from the classifier slices lg[tp][T][vocab_loc] into
 // logits[t][vocab], and the greedy argmax (first maximum) into next[t].
-__global__ void __launch_bounds__(256) k_logits_argmax(const float *__restrict__ lg, int T, int vocab_loc, int tp,
+__global__ void __launch_bounds__(256) k_logits_argmax(PartSrc lg, int T, int vocab_loc, int tp,
                                                        float *__restrict__ logits, int *__restrict__ next, int *err)
 {
     __shared__ unsigned long long red[8];
@@ -162,7 +216,7 @@ __global__ void __launch_bounds__(256) k_logits_argmax(const float *__restrict__
     unsigned long long best = 0ull;
     for (int j = tid; j < vocab; j += blockDim.x) {
         const int r = j / vocab_loc, jj = j - r * vocab_loc;
-        const float v = lg[((size_t)r * T + t) * vocab_loc + jj];
+        const float v = lg.ld1(((size_t)r * T + t) * vocab_loc + jj);
         logits[(size_t)t * vocab + j] = v;
         const unsigned long long k = argmax_key(v, j);
         best = k > best ? k : best;
@@ -856,10 +910,13 @@ static cudaError_t launch_attn_batch(LlmModel *m, int l, int nblocks, int max_ro
 
 // Accumulate a row-split product (wo, w2) into the residual stream: directly,
 // or, when sharded, through the delta buffer, a sum-allreduce and an add.
-static cudaError_t residual_product(LlmModel *m, const DevWeight &W, int T, cudaStream_t st)
+// Unsharded, a K split is left to the next rmsnorm (*pend), which adds it.
+static cudaError_t residual_product(LlmModel *m, const DevWeight &W, int T, cudaStream_t st, SplitOut *pend)
 {
     const LlmConfig &c = m->c;
-    if (c.tp_size <= 1) return launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_x, T, true, m->bt_ws, m->bt_ws_bytes, m->err, st);
+    *pend = SplitOut{};
+    if (c.tp_size <= 1)
+        return launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_x, T, true, m->bt_ws, m->bt_ws_bytes, m->err, st, pend);
     cudaError_t e = launch_qgemm_x16(W.L, W.ptr, m->bt_x16, m->bt_delta, T, false, m->bt_ws, m->bt_ws_bytes, m->err, st);
     if (e) return e;
     m->allreduce(m->comm_ctx, m->bt_delta, (size_t)T * c.dim, st);
@@ -877,34 +934,47 @@ cudaError_t llm_batch_enqueue(LlmModel *m, int T, int nblocks, bool advance, int
     k_embed<<<T, 128, 0, st>>>(m->bt_tok, m->emb, m->bt_x, c.dim, c.vocab, m->err);
     if ((e = cudaGetLastError())) return e;
     const size_t seq_stride = (size_t)c.n_layers * c.seq_len * m->kv_dim;
+    // A product split over K leaves its partials to the kernel that reads it
+    // next (the split sum folded into RoPE, SwiGLU, rmsnorm or the argmax).
+    const long long nd = (long long)T * c.dim, nqkv = (long long)T * (m->q_dim + 2 * m->kv_dim);
+    SplitOut so, pend;   // pend: the last residual product's split, added by the next rmsnorm
     for (int l = 0; l < c.n_layers; l++) {
-        k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_att + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad);
+        k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_att + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad,
+                                         part_src(m->bt_x, pend, nd));
         if ((e = cudaGetLastError())) return e;
         if ((e = launch_qgemm_x16(m->qkv[l].L, m->qkv[l].ptr, m->bt_x16, m->bt_y, T, false, m->bt_ws,
-                                    m->bt_ws_bytes, m->err, st))) return e;
-        const long long np = (long long)T * (m->q_dim + 2 * m->kv_dim) / 2;
-        k_rope_kv<<<grid_for(np, 256), 256, 0, st>>>(m->bt_y, T, m->bt_tok, m->bt_q, m->kcache, m->vcache, seq_stride,
-                                                     (size_t)l * c.seq_len * m->kv_dim, m->q_dim, m->kv_dim,
-                                                     m->head_size, c.seq_len, m->n_seqs, m->err);
+                                    m->bt_ws_bytes, m->err, st, &so))) return e;
+        const long long np = nqkv / 2;
+        k_rope_kv<<<grid_for(np, 256), 256, 0, st>>>(part_src(m->bt_y, so, nqkv), T, m->bt_tok, m->bt_q, m->kcache,
+                                                     m->vcache, seq_stride, (size_t)l * c.seq_len * m->kv_dim,
+                                                     m->q_dim, m->kv_dim, m->head_size, c.seq_len, m->n_seqs, m->err);
         if ((e = cudaGetLastError())) return e;
         if ((e = launch_attn_batch(m, l, nblocks, m->bt_max_rows, st))) return e;
         if ((e = launch_x16(m->bt_xb, m->bt_x16, T, m->q_dim, st))) return e;
-        if ((e = residual_product(m, m->wo[l], T, st))) return e;
-        k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_ffn + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad);
+        if ((e = residual_product(m, m->wo[l], T, st, &pend))) return e;
+        k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_ffn + (size_t)l * c.dim, m->bt_x16, c.dim, Tpad,
+                                         part_src(m->bt_x, pend, nd));
         if ((e = cudaGetLastError())) return e;
         if ((e = launch_qgemm_x16(m->w13[l].L, m->w13[l].ptr, m->bt_x16, m->bt_y, T, false, m->bt_ws,
-                                    m->bt_ws_bytes, m->err, st))) return e;
+                                    m->bt_ws_bytes, m->err, st, &so))) return e;
         const long long nh = (long long)T * (m->hidden_loc / 8);
-        k_swiglu_x16<<<grid_for(nh, 256), 256, 0, st>>>(m->bt_y, T, m->hidden_loc, m->bt_x16, Tpad);
+        k_swiglu_x16<<<grid_for(nh, 256), 256, 0, st>>>(part_src(m->bt_y, so, (long long)T * 2 * m->hidden_loc), T,
+                                                        m->hidden_loc, m->bt_x16, Tpad);
         if ((e = cudaGetLastError())) return e;
-        if ((e = residual_product(m, m->w2[l], T, st))) return e;
+        if ((e = residual_product(m, m->w2[l], T, st, &pend))) return e;
     }
-    k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_final, m->bt_x16, c.dim, Tpad);
+    k_rmsnorm_x16<<<T, 256, 0, st>>>(m->bt_x, m->rms_final, m->bt_x16, c.dim, Tpad, part_src(m->bt_x, pend, nd));
     if ((e = cudaGetLastError())) return e;
     float *lg = m->bt_lg + (size_t)c.tp_rank * T * m->vocab_loc;
-    if ((e = launch_qgemm_x16(m->cls.L, m->cls.ptr, m->bt_x16, lg, T, false, m->bt_ws, m->bt_ws_bytes, m->err, st))) return e;
-    if (c.tp_size > 1) m->allgather(m->comm_ctx, m->bt_lg, (size_t)T * m->vocab_loc, c.tp_rank, st);
-    k_logits_argmax<<<T, 256, 0, st>>>(m->bt_lg, T, m->vocab_loc, c.tp_size, m->bt_logits, m->bt_next, m->err);
+    // sharded, the slices are gathered first: the classifier's split is summed in place
+    if ((e = launch_qgemm_x16(m->cls.L, m->cls.ptr, m->bt_x16, lg, T, false, m->bt_ws, m->bt_ws_bytes, m->err, st,
+                              c.tp_size > 1 ? nullptr : &so))) return e;
+    if (c.tp_size > 1) {
+        m->allgather(m->comm_ctx, m->bt_lg, (size_t)T * m->vocab_loc, c.tp_rank, st);
+        so = SplitOut{};
+    }
+    k_logits_argmax<<<T, 256, 0, st>>>(part_src(m->bt_lg, so, (long long)T * m->vocab_loc), T, m->vocab_loc,
+                                       c.tp_size, m->bt_logits, m->bt_next, m->err);
     if ((e = cudaGetLastError())) return e;
     if (advance) {
         k_batch_advance<<<1, 256, 0, st>>>(m->bt_tok, m->bt_next, T, log, log_cap, m->bt_step);

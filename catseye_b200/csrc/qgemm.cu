@@ -512,8 +512,9 @@ cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t s
 }
 
 cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
-                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st)
+                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st, SplitOut *defer)
 {
+    if (defer) *defer = SplitOut{};
     if (T <= 0) return cudaSuccess;
     if (!qgemm_supported(L)) return cudaErrorInvalidValue;
     QgemmArgs a;
@@ -541,6 +542,10 @@ cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __ha
     const int bn = pick_bn(T);
     cudaError_t e = L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
     if (e || splits == 1) return e;
+    if (defer) {   // the caller's next kernel adds the partials
+        *defer = SplitOut{ws, splits};
+        return cudaSuccess;
+    }
     const long long count = (long long)T * L.d;
     k_splitk_sum<<<(int)std::min<long long>((count + 255) / 256, 148LL * 8), 256, 0, st>>>(ws, splits, count, y,
                                                                                           a.accumulate);

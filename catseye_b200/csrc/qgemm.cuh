@@ -53,8 +53,18 @@ size_t qgemm_workspace_bytes(const WeightLayout &L, int T);
 // and fp32 accumulation, X given as x16.  ws (ws_bytes) holds the K-split
 // partials; with less room than qgemm_workspace_bytes the product runs as
 // one pass over K.
+// With `defer` set, a product split over K leaves its partials in ws
+// ([splits][T][d]) for the caller's next kernel to add (in split order, as
+// the sum kernel would, then onto y when accumulating) instead of launching
+// the sum: *defer = {ws, splits}; splits == 1 means y holds the result.
+struct SplitOut {
+    const float *ws = nullptr;
+    int splits = 1;
+};
+
 cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
-                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st);
+                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st,
+                             SplitOut *defer = nullptr);
 
 // The same from fp32 x (converted into the x16 scratch, qgemm_x16_bytes, first).
 cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,

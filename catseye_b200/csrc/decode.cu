@@ -49,7 +49,7 @@ constexpr int DEC_MAX_HS = 128;                               // head size held 
 constexpr int DEC_STAGE_V = 4;                                // staging loads in flight per thread (512 threads)
 constexpr int DEC_STAGE_V_WIDE = 6;                           // the same without rmsnorm: the hidden vector in one pass
 constexpr uint32_t DEC_HEADER = 1024;                         // mbarriers + scratch at the start of smem
-constexpr uint32_t GRID_SPIN_LIMIT = 1u << 22;                // polls of ~0.5-1 us each: a few seconds at most
+constexpr uint32_t GRID_SPIN_LIMIT = 1u << 22;                // polls of ~0.5-1 us each (with a 50 ns pause): seconds at most
 
 // One weight in the tile-chunk layout (16-row tiles, 64-unit segments).
 struct WDesc {
@@ -172,7 +172,11 @@ __device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, u
             // barrier; the acquire polls make the other CTAs' writes visible
             red_release_add(a.bar, 1u);
             uint32_t i = 0;
+            // 148 pollers on one line: a short pause between polls keeps their
+            // traffic from slowing the weight stream and the other CTAs'
+            // arrivals (measured on B200: no pause 728 tok/s, 50 ns 802, 400 ns 783)
             while (ld_acquire_u32(a.bar) < target) {
+                __nanosleep(50);
                 if ((++i & 63) == 0 && (i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag))) {
                     ok = false;
                     break;

@@ -886,7 +886,10 @@ int cats_conv2d_forward_dev(const float *x, const float *w, float *z, int batch,
     if (!ensure_init()) return g.last_err;
     if (!x || !w || !z || batch <= 0 || ch <= 0 || !conv_geom_ok(ich, h, wd, ksize, ksize, pad, pad, stride, stride))
         return fail(CATS_ERR_ARG, what);
-    return check(launch_conv2d_forward(x, w, z, batch, ich, h, wd, ch, ksize, pad, stride, g.d_err,
+    // scratch for the weights in the tensor-core path's channel-blocked order
+    const size_t wpb = (size_t)ch * ich * ksize * ksize * 4;
+    if (grow((void **)&g.d_work, &g.cap_work, wpb)) return g.last_err;
+    return check(launch_conv2d_forward(x, w, z, batch, ich, h, wd, ch, ksize, pad, stride, g.d_err, g.d_work,
                                        stream ? (cudaStream_t)stream : g.stream),
                  what);
 }

@@ -157,10 +157,10 @@ __global__ void __launch_bounds__(CV_NT, 2) k_conv_fwd(const __grid_constant__ C
 }
 
 cudaError_t launch_conv2d_forward(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch,
-                                  int ks, int pad, int stride, int *err, cudaStream_t st)
+                                  int ks, int pad, int stride, int *err, float *wperm, cudaStream_t st)
 {
     if (conv_tc_usable(w, batch, ich, h, wd, ch, ks, pad, stride))
-        return launch_conv_tc(x, w, z, batch, ich, h, wd, ch, ks, pad, stride, err, st);
+        return launch_conv_tc(x, w, z, batch, ich, h, wd, ch, ks, pad, stride, err, wperm, st);
     ConvArgs a;
     a.x = x;
     a.w = w;

@@ -18,12 +18,15 @@ cudaError_t launch_im2col(const float *im, int channels, int height, int width, 
 // Shapes the tensor cores take (conv_tc_usable) run as 3xTF32 on tcgen05
 // (launch_conv_tc, sgemm_tc.cu); the rest on the CUDA cores.  `err` (may be
 // null) receives CATS_DEVERR_* bits when a tensor-core wait times out.
+// `wperm` (may be null): room for ch * ich * ks^2 floats, where the weights
+// are permuted into the channel-blocked order the tensor-core path gathers
+// fastest in (input channels a multiple of 32).
 cudaError_t launch_conv2d_forward(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch,
-                                  int ks, int pad, int stride, int *err, cudaStream_t st);
+                                  int ks, int pad, int stride, int *err, float *wperm, cudaStream_t st);
 
 bool conv_tc_usable(const float *w, int batch, int ich, int h, int wd, int ch, int ks, int pad, int stride);
 cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch, int ks,
-                           int pad, int stride, int *err, cudaStream_t st);
+                           int pad, int stride, int *err, float *wperm, cudaStream_t st);
 
 // z[b][o] = w[in*out + o] (the bias the linear forward adds, catseye.h:416-444).
 cudaError_t launch_bias_rows(const float *bias, float *z, int batch, int out, cudaStream_t st);

@@ -290,6 +290,36 @@ __device__ __forceinline__ void gather_tile(const SgemmTcArgs &a, const int2 *kt
     }
 }
 
+// Convolution mode 3 (the input channels a multiple of 32): K in the order
+// k' = (ky ks + kx) ich + ci, so slice s is one kernel offset kyx = 32 s / ich
+// over channels ci0 = 32 s % ich .. + 31.  A thread's four pixels then need
+// one bounds test and one base address per slice, and its four channel rows
+// of the slice add ci h wd each.  The weights are permuted into the same
+// order first (k_perm_weights); the sums are the same products in another
+// order.
+__device__ __forceinline__ void gather_tile_cb(const SgemmTcArgs &a, const ConvPix &cp, int slice, float4 (&v)[4])
+{
+    const int w = threadIdx.x >> 5;
+    const int k0 = slice * TC_K, kyx = k0 / a.ich, ci0 = k0 - kyx * a.ich;
+    const int ky = kyx / a.ks, kx = kyx - ky * a.ks;
+    const int hw = a.h * a.wd;
+    int off[4];
+    bool ok[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        ok[j] = (unsigned)(cp.iy0[j] + ky) < (unsigned)a.h && (unsigned)(cp.ix0[j] + kx) < (unsigned)a.wd;
+        off[j] = cp.base[j] + ky * a.wd + kx;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int co = (ci0 + w + 8 * i) * hw;
+        float r[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) r[j] = ok[j] ? __ldg(a.x + off[j] + co) : 0.f;
+        v[i] = make_float4(r[0], r[1], r[2], r[3]);
+    }
+}
+
 // Store a gathered tile as hi and lo in the MN-major layout of the B^T
 // tile: element (pixel lane + 32 j, k w + 8 i), 4-byte stores; the 32 lanes
 // of an instruction fill one 128-byte k-row, each bank once.
@@ -335,9 +365,14 @@ __device__ __forceinline__ bool produce(const SgemmTcArgs &a, uint8_t *smem, TcB
     else store_tile<TB, TC_N>(st, st + Cfg::BT, vb);
     store_tile<!TA, BM>(st + 2 * Cfg::BT, st + 2 * Cfg::BT + Cfg::AT, va);
     if (kb + 2 < nk) {
-        load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0 + (kb + 2) * TC_K, va);
-        if (CONV) gather_tile(a, ktab, cp, kb0 + (kb + 2) * TC_K, vb);
-        else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + (kb + 2) * TC_K, vb);
+        if (CONV == 3) {
+            load_tile<true, BM>(a.A, a.lda, a.M, kend, m0, kb0 + (kb + 2) * TC_K, va);
+            gather_tile_cb(a, cp, kb + 2, vb);
+        } else {
+            load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0 + (kb + 2) * TC_K, va);
+            if (CONV) gather_tile(a, ktab, cp, kb0 + (kb + 2) * TC_K, vb);
+            else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + (kb + 2) * TC_K, vb);
+        }
     }
     fence_proxy_async_smem();
     __syncwarp();
@@ -362,7 +397,8 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar)
 }
 
 // CONV: 0 GEMM, 1 convolution, 2 convolution whose weight rows are not
-// 16-byte aligned (scalar weight loads)
+// 16-byte aligned (scalar weight loads), 3 convolution in the channel-blocked
+// K order (input channels a multiple of 32)
 template <bool TA, bool TB, int BM, int CONV = 0>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constant__ SgemmTcArgs a)
 {
@@ -398,7 +434,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         bars->abort = 0;
         fence_barrier_init();
     }
-    if (CONV) {
+    if (CONV == 1 || CONV == 2) {
         const int kk2 = a.ks * a.ks, kpad = (a.K + TC_K - 1) / TC_K * TC_K;
         for (int k = threadIdx.x; k < kpad; k += blockDim.x) {
             const int ci = k / kk2, r = k - ci * kk2, ky = r / a.ks, kx = r - ky * a.ks;
@@ -456,15 +492,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_sgemm_tc(const __grid_constan
         int flushed = 0;   // chunks folded into the sum so far
         ConvPix cp;
         if (CONV) conv_pixels(a, n0, cp);
-        if (nk > 0) {
-            load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0, va0);
-            if (CONV) gather_tile(a, ktab, cp, kb0, vb0);
-            else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0, vb0);
-        }
-        if (nk > 1) {
-            load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0 + TC_K, va1);
-            if (CONV) gather_tile(a, ktab, cp, kb0 + TC_K, vb1);
-            else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + TC_K, vb1);
+        if (CONV == 3) {
+            if (nk > 0) {
+                load_tile<true, BM>(a.A, a.lda, a.M, kend, m0, kb0, va0);
+                gather_tile_cb(a, cp, 0, vb0);
+            }
+            if (nk > 1) {
+                load_tile<true, BM>(a.A, a.lda, a.M, kend, m0, kb0 + TC_K, va1);
+                gather_tile_cb(a, cp, 1, vb1);
+            }
+        } else {
+            if (nk > 0) {
+                load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0, va0);
+                if (CONV) gather_tile(a, ktab, cp, kb0, vb0);
+                else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0, vb0);
+            }
+            if (nk > 1) {
+                load_tile<!TA, BM, CONV == 2>(a.A, a.lda, a.M, kend, m0, kb0 + TC_K, va1);
+                if (CONV) gather_tile(a, ktab, cp, kb0 + TC_K, vb1);
+                else load_tile<TB, TC_N>(a.B, a.ldb, a.N, kend, n0, kb0 + TC_K, vb1);
+            }
         }
         bool live = true;
         for (int kb = 0; kb < nk && live; kb += 2) {
@@ -649,6 +696,17 @@ cudaError_t launch_sgemm_tc(const SgemmPlan &p, bool ta, bool tb, int M, int N, 
 
 // ---------------------------------------------------------------- convolution
 
+// w[m][ci ks^2 + kyx] -> wp[m][kyx ich + ci], the channel-blocked K order
+__global__ void k_perm_weights(const float *__restrict__ w, float *__restrict__ wp, int M, int ich, int kk2)
+{
+    const long long K = (long long)ich * kk2, total = (long long)M * K;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long m = i / K;
+        const int kp = (int)(i - m * K), kyx = kp / ich, ci = kp - kyx * ich;
+        wp[i] = w[m * K + (long long)ci * kk2 + kyx];
+    }
+}
+
 bool conv_tc_usable(const float *w, int batch, int ich, int h, int wd, int ch, int ks, int pad, int stride)
 {
     if (batch <= 0 || ich <= 0 || ch <= 0 || ch > 256 || ks <= 0 || stride <= 0) return false;
@@ -676,20 +734,31 @@ static cudaError_t launch_conv_bm(const SgemmTcArgs &a, cudaStream_t st)
         if (e) return e;
         attr = true;
     }
-    const int kpad = (a.K + TC_K - 1) / TC_K * TC_K;
+    const int kpad = CONV == 3 ? 0 : (a.K + TC_K - 1) / TC_K * TC_K;   // mode 3 needs no k table
     const int tiles = cdiv(a.M, BM) * cdiv(a.N, TC_N);
     k_sgemm_tc<false, false, BM, CONV><<<tiles, TC_THREADS, smem_bytes<BM>(kpad), st>>>(a);
     return cudaGetLastError();
 }
 
+// mode 3 (channel-blocked K order) when the input channels are a multiple of
+// 32 and there is room for the permuted weights; else the k-table gather
 template <int BM>
-static cudaError_t launch_conv_bm(const SgemmTcArgs &a, bool scalar_w, cudaStream_t st)
+static cudaError_t launch_conv_bm(SgemmTcArgs a, bool scalar_w, float *wperm, cudaStream_t st)
 {
+    if (a.ich % TC_K == 0 && wperm) {
+        const long long total = (long long)a.M * a.K;
+        k_perm_weights<<<(int)std::min<long long>((total + 255) / 256, 148LL * 8), 256, 0, st>>>(a.A, wperm, a.M, a.ich,
+                                                                                               a.ks * a.ks);
+        cudaError_t e = cudaGetLastError();
+        if (e) return e;
+        a.A = wperm;
+        return launch_conv_bm<BM, 3>(a, st);
+    }
     return scalar_w ? launch_conv_bm<BM, 2>(a, st) : launch_conv_bm<BM, 1>(a, st);
 }
 
 cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, int ich, int h, int wd, int ch, int ks,
-                           int pad, int stride, int *err, cudaStream_t st)
+                           int pad, int stride, int *err, float *wperm, cudaStream_t st)
 {
     if (!conv_tc_usable(w, batch, ich, h, wd, ch, ks, pad, stride)) return cudaErrorInvalidValue;
     SgemmTcArgs a = {};
@@ -718,16 +787,16 @@ cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, 
     if (ch <= 64) {
         a.tiles_m = 1;
         a.main_tiles = cdiv(a.N, TC_N);
-        return launch_conv_bm<64>(a, scalar_w, st);
+        return launch_conv_bm<64>(a, scalar_w, wperm, st);
     }
     if (ch <= 128) {
         a.tiles_m = 1;
         a.main_tiles = cdiv(a.N, TC_N);
-        return launch_conv_bm<128>(a, scalar_w, st);
+        return launch_conv_bm<128>(a, scalar_w, wperm, st);
     }
     a.tiles_m = cdiv(ch, 256);
     a.main_tiles = a.tiles_m * cdiv(a.N, TC_N);
-    return launch_conv_bm<256>(a, scalar_w, st);
+    return launch_conv_bm<256>(a, scalar_w, wperm, st);
 }
 
 } // namespace cats

@@ -47,7 +47,14 @@ tensor peak (the measured bf16 peak / 2 for tf32 / 3 products per fp32
 product), since both run on k_sgemm_tc; cpu_baseline = the reference's gemm_rnn / layer forwards
 (oracle/_ref, OpenMP on all cores) on a bounded sample.
 With torchrun (N > 1) every rank decodes its own replica (no collective on
-the data path yet): value = sum over ranks, time = max over ranks.
+the data path): value = sum over ranks, time = max over ranks.  With --tp
+the N ranks instead hold one model sharded by tensor parallelism (wq/wk/wv
+and w1/w3 by rows, wo and w2 by input columns, the classifier by vocabulary
+rows) and decode one sequence: the per-phase kernels in a CUDA graph with an
+NCCL allreduce after wo and after w2, on the library's own communicator
+(value = that sequence's tokens/s, "strong" scaling; roofline per GPU over
+the rank's weight slice).  torch.distributed then runs on gloo and only
+shares the NCCL id, aligns the ranks and takes the max of their times.
 """
 import argparse
 import json
@@ -156,7 +163,7 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def dist_init():
+def dist_init(backend="nccl"):
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if ws == 1:
@@ -166,7 +173,10 @@ def dist_init():
     import torch.distributed as dist
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    if backend == "nccl":
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     return dist, rank, ws, local
 
 
@@ -210,8 +220,15 @@ def run_ours(args, dist, rank, ws, local):
     _lib.init(local)
     torch.cuda.set_device(local)
     cfg = cfg_for(args.workload, args.layers)
-    m = llm.GpuLLM(cfg)
+    tp = args.tp and ws > 1
+    if tp:
+        m = llm.GpuLLM(cfg, rank, ws)
+        m.tp_connect(llm.tp_share_id())
+        m.set_engine(llm.ENGINE_GRAPH)   # the persistent kernel runs one GPU
+    else:
+        m = llm.GpuLLM(cfg)
     m.init_random(SEED)
+    red_dev = "cpu" if tp else "cuda"     # gloo reduces host tensors
     stream = torch.cuda.ExternalStream(m.stream)
     rng = np.random.default_rng(SEED + 1)
     prompt = rng.integers(0, cfg.vocab, PROMPT)
@@ -239,7 +256,7 @@ def run_ours(args, dist, rank, ws, local):
     barrier()
     ms = e0.elapsed_time(e1)
     if dist:
-        t = torch.tensor([ms], device="cuda")
+        t = torch.tensor([ms], device=red_dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     clocks = clk.summary()
@@ -254,20 +271,20 @@ def run_ours(args, dist, rank, ws, local):
         tok = int(np.argmax(lg))
     e2e_s = time.perf_counter() - t0
     if dist:
-        t = torch.tensor([e2e_s], device="cuda")
+        t = torch.tensor([e2e_s], device=red_dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
 
     # per-phase kernels of the graph engine, timed alone (diagnostic)
     kinds = {}
-    for k, name in enumerate(("qkv", "wo", "w13", "w2", "cls")):
+    for k, name in enumerate(() if tp else ("qkv", "wo", "w13", "w2", "cls")):
         a, b = m.time_matvec(k, reps=2)
         kinds[name] = {"us_per_launch": round(a * 1e3, 2), "gbs": round(b / (a * 1e-3) / 1e9, 1)}
     wbytes = m.weight_bytes()
     m.close()
     # algorithmic bytes of the timed launch: every weight once per step, plus the
     # K and V rows 0..pos of every layer that attention reads
-    kv_row = cfg.kv_dim * 4
+    kv_row = cfg.kv_dim * 4 // (ws if tp else 1)   # this rank's K/V heads
     kv_bytes = sum(2 * cfg.n_layers * kv_row * (p + 1) for p in range(pos0 + args.warmup, pos0 + args.warmup + args.steps))
     kbytes = wbytes * args.steps + kv_bytes
     kms = ms
@@ -657,6 +674,8 @@ def main():
                     choices=sorted(WORKLOADS) + sorted(BATCHED) + ["sgemm_4096", "cnn_forward_b128"])
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="decode workloads under torchrun: shard one model over the ranks (tensor parallelism)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload in ("sgemm_4096", "cnn_forward_b128"):
@@ -684,14 +703,16 @@ def main():
         print(json.dumps(line))
         return
 
-    dist, rank, ws, local = dist_init()
+    dist, rank, ws, local = dist_init("gloo" if args.tp else "nccl")
     ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg = run_ours(args, dist, rank, ws, local)
     if rank != 0:
         if dist:
             dist.destroy_process_group()
         return
     peak, peak_kind = peaks()
-    tok_s = ws * args.steps / (ms * 1e-3)
+    tp = args.tp and ws > 1
+    seqs = 1 if tp else ws   # sequences decoded by the whole job
+    tok_s = seqs * args.steps / (ms * 1e-3)
     achieved = kbytes / (kms * 1e-3) / 1e9
     traffic = None
     tf = os.path.join(ROOT, "profiles", "decode_traffic.json")
@@ -701,23 +722,29 @@ def main():
     line = {
         "metric": "decode tok/s (batch 1)", "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)", 8: "q8_0 x q8"}[cfg.wtype],
         "data": "synthetic",
         "config": {"workload": workload_name(args), "batch": 1, "prompt": PROMPT, "dim": cfg.dim,
                    "layers": cfg.n_layers, "context": cfg.seq_len,
-                   "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                   "parallelism": f"tp{ws}" if tp else (f"replicas{ws}" if ws > 1 else "single"),
                    "l2": (f"weights {wbytes / 1e9:.2f} GB per step > 126 MB L2; no flush" if wbytes > 126e6 else
                           f"weights {wbytes / 1e6:.0f} MB per step; L2-resident, no flush")},
-        "roofline": {"bound": "hbm", "kernel": "k_decode (persistent cooperative decode, %d steps per launch)"
-                     % args.steps, "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+        "roofline": {"bound": "hbm",
+                     "kernel": ("graph engine per GPU: k_matvec / k_attention / residual adds, NCCL allreduce after "
+                                "wo and w2, one CUDA graph per token" if tp else
+                                "k_decode (persistent cooperative decode, %d steps per launch)" % args.steps),
+                     "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                      "bytes_per_launch": int(kbytes), "weight_bytes_per_step": int(wbytes),
                      "ms_per_launch": round(kms, 3)},
         "graph_engine_kernels": kinds,
-        "e2e": {"value": round(ws * args.e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 16,
+        "e2e": {"value": round(seqs * args.e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": cfg.vocab * 4},
-        "gpu_launches": 1,
+        # persistent kernel: one launch; graph engine with tensor parallelism: per layer the qkv,
+        # attention, wo, w1/w3 and w2 kernels and two residual adds, then the classifier and
+        # the advance kernel, per step (the NCCL collectives are NCCL's kernels)
+        "gpu_launches": args.steps * (7 * cfg.n_layers + 2) if tp else 1,
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:

@@ -199,10 +199,11 @@ __device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, u
 // the CTA is unwinding.
 __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, const Smem &sm, int *err, int code)
 {
+    // no software pause: try_wait parks the thread until the phase completes
+    // or a hardware time limit passes (same-box A/B 821.2 -> 823.3 tok/s)
     for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*sm.abort_s) return false;
-        if (i > 64) __nanosleep(32);
     }
     if (err) atomicOr(err, code);
     *sm.abort_s = 1;

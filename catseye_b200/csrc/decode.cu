@@ -45,6 +45,7 @@ constexpr int DEC_WARPS = DEC_GROUPS * DEC_GW;                // 16 consumer war
 constexpr int DEC_NC = 32 * DEC_WARPS;                        // 512 consumer threads
 constexpr int DEC_THREADS = DEC_NC + 32 * DEC_GROUPS;         // + one producer warp per ring
 constexpr int DEC_MAX_STAGES = 16;                            // per ring (two rings)
+constexpr int DEC_DEFAULT_STAGES = 4;                         // slots per ring unless tuned
 constexpr int DEC_RPW = 2;                                    // rows per warp in a 16-row tile
 constexpr int DEC_MAX_HS = 128;                               // head size held as one float4 per lane
 constexpr int DEC_STAGE_V = 4;                                // staging loads in flight per thread (512 threads)
@@ -766,11 +767,15 @@ int decode_prepare(LlmModel *m)
     const size_t cap = 227 * 1024;
     const size_t fixed = decode_smem_bytes((int)v.size(), 0, slot, xs);
     if (fixed + (size_t)DEC_GROUPS * 2 * slot > cap) return E_UNSUPPORTED;   // at least two slots per ring
-    m->dec_stages = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / ((size_t)DEC_GROUPS * slot));
-    // tuning: CATS_DECODE_RING_STAGES caps the slots per ring (weight bytes in flight per SM)
+    const int fit = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / ((size_t)DEC_GROUPS * slot));
+    // Four slots per ring by default: with more, the copies queued at a phase
+    // boundary lengthen the chain's L2 round trips more than they feed the
+    // dots (7B Q4_0 same-box A/B: 5 slots 823 tok/s, 4 slots 836, 3 slots 834;
+    // 70B: 5 and 4 slots equal).  CATS_DECODE_RING_STAGES sets 2..fit instead.
+    m->dec_stages = std::min(fit, DEC_DEFAULT_STAGES);
     if (const char *e = getenv("CATS_DECODE_RING_STAGES")) {
         const int s = atoi(e);
-        if (s >= 2 && s < m->dec_stages) m->dec_stages = s;
+        if (s >= 2 && s <= fit) m->dec_stages = s;
     }
     m->dec_slot = slot;
     m->dec_xs = xs;

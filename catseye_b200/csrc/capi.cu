@@ -188,6 +188,7 @@ void matmul_host(int type, float *xout, void *x, void *w, int n, int d, const ch
 namespace cats {
 // the sticky status, for entry points defined in other files
 int capi_fail(int code, const char *what) { return fail(code, what); }
+int noalloc_device_error(bool clear);   // noalloc.cu: the no-allocation sgemm's status word
 }
 
 // ===================================================================== C ABI
@@ -235,15 +236,18 @@ void cats_gpu_term(void)
 }
 
 int cats_gpu_last_error(void) { return g.last_err; }
-void cats_gpu_clear_error(void) { g.last_err = 0; }
+void cats_gpu_clear_error(void)
+{
+    g.last_err = 0;
+    cats::noalloc_device_error(true);
+}
 const char *cats_gpu_error_string(int code) { return err_name(code); }
 
 int cats_gpu_device_error(void)
 {
-    if (!g.init) return 0;
     int h = 0;
-    cudaMemcpy(&h, g.d_err, 4, cudaMemcpyDeviceToHost);
-    return h;
+    if (g.init) cudaMemcpy(&h, g.d_err, 4, cudaMemcpyDeviceToHost);
+    return h | cats::noalloc_device_error(false);
 }
 
 int cats_gpu_register_weight(const void *w, int type, int n, int d)

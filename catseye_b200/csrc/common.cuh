@@ -39,6 +39,24 @@ enum Err : int {
 __host__ __device__ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 __host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// A kernel's dynamic shared-memory limit is an attribute of the kernel on one
+// device: raising it on device 0 leaves it at the default on device 1.  Each
+// call site keeps one bit per device ordinal (ordinals >= 64 set the
+// attribute on every call); concurrent first calls both set it, which is
+// harmless because the value is the same.
+template <class F>
+inline cudaError_t once_per_device(unsigned long long &mask, F &&set_attr)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (__atomic_load_n(&mask, __ATOMIC_ACQUIRE) & bit)) return cudaSuccess;
+    e = set_attr();
+    if (e == cudaSuccess && bit) __atomic_fetch_or(&mask, bit, __ATOMIC_RELEASE);
+    return e;
+}
+
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
 {

@@ -363,13 +363,11 @@ template <int WT, int RPW, bool XF>
 static cudaError_t launch_t(const MatvecArgs &a, cudaStream_t st, bool pdl, int grid_override)
 {
     const size_t smem = matvec_smem_bytes(a, WT);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e =
-            cudaFuncSetAttribute(k_matvec<WT, RPW, XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static unsigned long long attr_set = 0;   // one bit per device
+    cudaError_t ea = once_per_device(attr_set, [] {
+        return cudaFuncSetAttribute(k_matvec<WT, RPW, XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    });
+    if (ea != cudaSuccess) return ea;
     int grid = grid_override > 0 ? grid_override : std::min(a.n_tiles, matvec_num_sms());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

@@ -432,12 +432,13 @@ static cudaError_t prepare_bn(int bn, int *per_sm)
 // raised on the way.
 static int resident_per_sm(int type, int bn)
 {
-    static int cache[2][5][8] = {};   // [type][bn][device], 0 = not queried
+    static int cache[2][5][64] = {};   // [type][bn][device], 0 = not queried
     int dev = 0;
     cudaGetDevice(&dev);
     const int ti = type == W_Q4_0 ? 0 : 1;
     const int bi = bn == 256 ? 0 : bn == 128 ? 1 : bn == 64 ? 2 : bn == 32 ? 3 : 4;
-    int &c = cache[ti][bi][dev & 7];
+    int spare = 0;   // ordinals past the table are queried (and the limit raised) on every call
+    int &c = dev >= 0 && dev < 64 ? cache[ti][bi][dev] : spare;
     if (c == 0) {
         int n = 0;
         const cudaError_t e = type == W_Q4_0 ? prepare_bn<W_Q4_0>(bn, &n) : prepare_bn<W_Q8_0>(bn, &n);

@@ -190,7 +190,11 @@ SgemmPlan sgemm_plan(int M, int N, int K, int num_sms, size_t max_work_floats)
     // to give every split a few k-slabs of its own
     if (tiles < num_sms && K >= 512) {
         int s = std::min(cdiv(num_sms * 2, tiles), K / 256);
-        p.splits = std::max(1, std::min(s, 32));
+        s = std::max(1, std::min(s, 32));
+        // the workspace cap limits the split (down to none), it never refuses the product
+        const size_t fit = max_work_floats / std::max<size_t>(1, (size_t)M * N);
+        if ((size_t)s > fit) s = fit >= 2 ? (int)fit : 1;
+        p.splits = s;
     } else if (tiles < 16 && K >= 128) {
         // a handful of tiles (a classifier layer): 64-deep splits, so one
         // CTA does not walk K alone (when the workspace fits the cap)

@@ -615,14 +615,12 @@ int sgemm_tc_tile_m(int M) { return M > 128 ? 256 : 128; }
 template <bool TA, bool TB, int BM>
 static cudaError_t launch_tc_t(dim3 grid, const SgemmTcArgs &a, cudaStream_t st)
 {
-    static bool attr = false;
+    static unsigned long long attr = 0;   // one bit per device
     const size_t smem = smem_bytes<BM>();
-    if (!attr) {
-        cudaError_t e =
-            cudaFuncSetAttribute(k_sgemm_tc<TA, TB, BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e) return e;
-        attr = true;
-    }
+    cudaError_t e = once_per_device(attr, [smem] {
+        return cudaFuncSetAttribute(k_sgemm_tc<TA, TB, BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
+    if (e) return e;
     k_sgemm_tc<TA, TB, BM><<<grid, TC_THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }
@@ -726,14 +724,12 @@ bool conv_tc_usable(const float *w, int batch, int ich, int h, int wd, int ch, i
 template <int BM, int CONV>
 static cudaError_t launch_conv_bm(const SgemmTcArgs &a, cudaStream_t st)
 {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_sgemm_tc<false, false, BM, CONV>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem_bytes<BM>(TC_CONV_MAX_K));
-        if (e) return e;
-        attr = true;
-    }
+    static unsigned long long attr = 0;   // one bit per device
+    cudaError_t e = once_per_device(attr, [] {
+        return cudaFuncSetAttribute(k_sgemm_tc<false, false, BM, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem_bytes<BM>(TC_CONV_MAX_K));
+    });
+    if (e) return e;
     const int kpad = CONV == 3 ? 0 : (a.K + TC_K - 1) / TC_K * TC_K;   // mode 3 needs no k table
     const int tiles = cdiv(a.M, BM) * cdiv(a.N, TC_N);
     k_sgemm_tc<false, false, BM, CONV><<<tiles, TC_THREADS, smem_bytes<BM>(kpad), st>>>(a);

@@ -271,12 +271,16 @@ int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const flo
  * stream, NULL = the default stream).  Skinny problems split K into a
  * workspace that is a fixed array compiled into the library:
  * CATS_SGEMM_NOALLOC_SCRATCH_FLOATS floats (8 MiB), held by every GPU that
- * loads the library until the process exits.  A problem whose split-K
- * workspace would exceed it is rejected with CATS_ERR_ARG before any launch.
+ * loads the library until the process exits.  The K split is fitted to that
+ * array (fewer splits, down to none), so no size is refused for it.
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) and the SM count; make that first call before any
  * stream capture.  Every call shares the one array, so calls that overlap on
- * the GPU (other streams, other host threads) race on it; serialize them. */
+ * the GPU (other streams, other host threads) race on it; serialize them.
+ * The call returns before the GPU work ends: a bounded wait of the
+ * tensor-core kernel that gave up writes its output tile as NaN and sets a
+ * bit in a status word of the current device (also a fixed array), which
+ * cats_gpu_device_error() returns OR-ed in and cats_gpu_clear_error() resets. */
 #define CATS_SGEMM_NOALLOC_SCRATCH_FLOATS (2 * 1024 * 1024)
 int cats_sgemm_dev_noalloc(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda,
                            const float *b, int ldb, float beta, float *c, int ldc, void *stream);

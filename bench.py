@@ -181,62 +181,174 @@ def dist_init(backend="nccl"):
 
 
 # ------------------------------------------------------------- CPU reference
-def cpu_reference(cfg, kind="reference", samples=3):
-    """Time the reference's own decode step on the host cores on a bounded sample.
+def _omp_all_cores():
+    """The reference's OpenMP loops on every host core: torchrun exports
+    OMP_NUM_THREADS=1, which would otherwise leave the reference one thread."""
+    import ctypes
+    n = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        ctypes.CDLL("libgomp.so.1").omp_set_num_threads(n)
+    except (OSError, AttributeError):
+        pass
+    return n
 
-    Two models with the workload's shapes but 1 and 2 layers (classifier
-    included) are timed; per-token time = t1 + (L - 1) * (t2 - t1)."""
+
+def _host_timing_model(cfg, orc, layers):
+    """A host model with the workload's shapes for timing the reference step:
+    one seeded layer of N(0, 0.02) weights quantized like the GPU model's,
+    copied into `layers` separate layers (every layer's weights are distinct
+    memory, so each step streams all of them; the dot products' cost does not
+    depend on the values)."""
     from dataclasses import replace
-    from oracle.cpu import Oracle, Reference, ref_available
     from oracle.models import ModelWeights
+    one = ModelWeights(replace(cfg, n_layers=1), SEED, orc)
+
+    class MW:
+        pass
+    mw = MW()
+    mw.cfg = replace(cfg, n_layers=layers)
+    mw.emb, mw.rms_final, mw.wcls = one.emb, one.rms_final, one.wcls
+    mw.rms_att = np.ones((layers, cfg.dim), np.float32)
+    mw.rms_ffn = np.ones((layers, cfg.dim), np.float32)
+    from oracle.cpu import aligned
+    for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+        blob = getattr(one, k)
+        out = aligned(np.empty(blob.size * layers, blob.dtype))   # the reference's 256-byte alignment, no copy later
+        out.reshape(layers, blob.size)[:] = blob
+        setattr(mw, k, out)
+    return mw
+
+
+def _host_mem_available():
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def cpu_reference(cfg, kind="reference", tokens=12):
+    """Time the reference's own decode step (cats_llama2_transformer, oracle/_ref
+    built for all cores) on the host cores, for `tokens` real steps of the
+    workload's model at its own context length, after 8 prompt steps.
+
+    A model too large for the host's free memory is timed at two layer counts
+    far apart (a quarter and a half of its layers): per token = t_a + (L - L_a)
+    * (t_b - t_a) / (L_b - L_a), stated in `sample`."""
+    from dataclasses import replace
+    from catseye_b200 import llm
+    from oracle.cpu import Oracle, Reference, ref_available
+    cores = _omp_all_cores()
     orc = Oracle()
     use_ref = kind == "reference" and ref_available("llm_allcores") and cfg.wtype in (0, 2)
-    times = {}
-    for L in (1, 2):
-        c = replace(cfg, n_layers=L, seq_len=64)
-        mw = ModelWeights(c, SEED, orc)
+    full = llm.weight_bytes(cfg) + 2 * cfg.n_layers * cfg.seq_len * cfg.kv_dim * 4
+    fits = full * 1.3 < _host_mem_available() or full < 8e9
+
+    def time_model(L):
+        mw = _host_timing_model(cfg, orc, L)
         m = Reference("llm_allcores").llm(mw) if use_ref else orc.llm(mw)
-        m.step(1, 0)
-        ts = []
-        for pos in range(1, 1 + samples):
-            t0 = time.perf_counter()
-            m.step(pos, pos)
-            ts.append(time.perf_counter() - t0)
-        times[L] = min(ts)
+        rng = np.random.default_rng(SEED + 1)
+        tok = 0
+        for pos, t in enumerate(rng.integers(0, cfg.vocab, PROMPT)):   # prompt, untimed
+            tok = int(np.argmax(m.step(int(t), pos)))
+        t0 = time.perf_counter()
+        for i in range(tokens):
+            tok = int(np.argmax(m.step(tok, PROMPT + i)))
+        dt = (time.perf_counter() - t0) / tokens
         del m, mw
-    t_layer = max(times[2] - times[1], 1e-9)
-    t_tok = times[1] + (cfg.n_layers - 1) * t_layer
-    cores = os.cpu_count()
+        return dt
+
+    if fits:
+        t_tok = time_model(cfg.n_layers)
+        sample = (f"full {cfg.n_layers}-layer model (context {cfg.seq_len}), {tokens} greedy steps at positions "
+                  f"{PROMPT}-{PROMPT + tokens - 1} after an {PROMPT}-token prompt: {t_tok * 1e3:.1f} ms per token")
+    else:
+        la, lb = max(1, cfg.n_layers // 4), max(2, cfg.n_layers // 2)
+        ta, tb = time_model(la), time_model(lb)
+        t_tok = ta + (cfg.n_layers - la) * (tb - ta) / (lb - la)
+        sample = (f"{la}- and {lb}-layer models (context {cfg.seq_len}; the full model exceeds the host's free "
+                  f"memory), {tokens} greedy steps each; per token = t{la} + {cfg.n_layers - la} x (t{lb} - t{la}) "
+                  f"/ {lb - la} = {t_tok * 1e3:.1f} ms")
     return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": cores,
-            "kind": "reference" if use_ref else "port",
-            "sample": f"1- and 2-layer models of the same shapes (+classifier), best of {samples} steps each at "
-                      f"pos 1-{samples}; per token = t1 + {cfg.n_layers - 1} x (t2 - t1) = {t_tok * 1e3:.1f} ms"}
+            "kind": "reference" if use_ref else "port", "sample": sample}
+
+
+def decode_config(args, cfg, ws, tp):
+    """The `config` object of a decode line, the same in both arms."""
+    from catseye_b200 import llm
+    wbytes = llm.weight_bytes(cfg)
+    return {"workload": workload_name(args), "batch": 1, "prompt": PROMPT, "dim": cfg.dim,
+            "layers": cfg.n_layers, "context": cfg.seq_len,
+            "parallelism": f"tp{ws}" if tp else (f"replicas{ws}" if ws > 1 else "single"),
+            "l2": (f"weights {wbytes / 1e9:.2f} GB per step > 126 MB L2; no flush" if wbytes > 126e6 else
+                   f"weights {wbytes / 1e6:.0f} MB per step; L2-resident, no flush")}
 
 
 # ------------------------------------------------------------------ our arm
+PARITY_STEPS = 8
+
+
+def tp_parity(args, cfg, dist, rank, prompt_logits):
+    """Sharded model vs one GPU: rank 0 builds the unsharded model of the same
+    seed on its own GPU, feeds it the same prompt and compares every step's
+    logits (normwise) and greedy token with what the sharded ranks computed.
+    The other ranks wait at the barrier."""
+    from catseye_b200 import llm
+    out = None
+    if rank == 0:
+        m = llm.GpuLLM(cfg)
+        m.init_random(SEED)
+        rng = np.random.default_rng(SEED + 1)
+        errs, same = [], 0
+        for pos, tok in enumerate(rng.integers(0, cfg.vocab, PROMPT)[:PARITY_STEPS]):
+            lg = m.step(int(tok), pos)
+            t = prompt_logits[pos]
+            errs.append(float(np.linalg.norm(t - lg) / np.linalg.norm(lg)))
+            same += int(np.argmax(t)) == int(np.argmax(lg))
+        m.close()
+        # quantized activations: a Q8 code rounding the other way after a float-order
+        # difference moves the logits by up to a few 1e-2 (the reference's own AVX
+        # and plain-C builds differ by 3-4e-2 on the 7B model); fp32 models: 1e-4
+        bar = 1e-4 if cfg.wtype == 0 else 6e-2
+        out = {"vs": "the same model unsharded on one GPU (seed %d), prompt steps 0-%d" % (SEED, PARITY_STEPS - 1),
+               "max_rel": round(max(errs), 6), "bar": bar, "greedy_equal": f"{same}/{len(errs)}",
+               "ok": bool(max(errs) < bar and (cfg.wtype != 0 or same == len(errs)))}
+    if dist:
+        dist.barrier()
+    return out
+
+
 def run_ours(args, dist, rank, ws, local):
     import torch
     from catseye_b200 import _lib, llm
     _lib.init(local)
     torch.cuda.set_device(local)
     cfg = cfg_for(args.workload, args.layers)
-    tp = args.tp and ws > 1
+    tp = ws > 1 and not args.replicas
     if tp:
         m = llm.GpuLLM(cfg, rank, ws)
         m.tp_connect(llm.tp_share_id())
-        m.set_engine(llm.ENGINE_GRAPH)   # the persistent kernel runs one GPU
     else:
         m = llm.GpuLLM(cfg)
+    engine = "persistent"
+    if tp and not m.tp_persistent():
+        m.set_engine(llm.ENGINE_GRAPH)
+        engine = "graph"
     m.init_random(SEED)
     red_dev = "cpu" if tp else "cuda"     # gloo reduces host tensors
     stream = torch.cuda.ExternalStream(m.stream)
     rng = np.random.default_rng(SEED + 1)
     prompt = rng.integers(0, cfg.vocab, PROMPT)
+    prompt_logits = []
     for pos, tok in enumerate(prompt):            # prompt forcing (untimed)
-        m.step(int(tok), pos)
+        prompt_logits.append(m.step(int(tok), pos).copy())
+    parity = tp_parity(args, cfg, dist, rank, prompt_logits) if tp else None
     pos0 = PROMPT
     assert pos0 + args.warmup + args.steps + args.e2e_steps <= cfg.seq_len
-    m.set_position(int(np.argmax(m.logits())), pos0)
+    m.set_position(int(np.argmax(prompt_logits[-1])), pos0)
     m.enqueue(args.warmup)
     m.synchronize()
 
@@ -287,8 +399,8 @@ def run_ours(args, dist, rank, ws, local):
     kv_row = cfg.kv_dim * 4 // (ws if tp else 1)   # this rank's K/V heads
     kv_bytes = sum(2 * cfg.n_layers * kv_row * (p + 1) for p in range(pos0 + args.warmup, pos0 + args.warmup + args.steps))
     kbytes = wbytes * args.steps + kv_bytes
-    kms = ms
-    return ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg
+    return dict(ms=ms, e2e_s=e2e_s, kbytes=kbytes, kinds=kinds, wbytes=wbytes, clocks=clocks, cfg=cfg, tp=tp,
+                engine=engine, parity=parity)
 
 
 # -------------------------------------------- batched step (prefill, batch 16)
@@ -404,7 +516,7 @@ def batched_main(args):
             return
         from catseye_b200 import llm
         cfg = getattr(llm, name).with_type(t)
-        cb = cpu_reference(cfg, "reference", samples=3)
+        cb = cpu_reference(cfg, "reference")
         cb["sample"] += "; the reference runs a prompt or a batch one token at a time, so this is its rate"
         print(json.dumps({"impl": "reference", "metric": metric, "value": round(cb["value"], 3), "unit": "tok/s",
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
@@ -479,6 +591,7 @@ def layer_flops(L):
 def gemm_cpu_reference(workload):
     """The reference's own CPU code (oracle/_ref, OpenMP on all cores) on a bounded sample."""
     from oracle.cpu import Reference
+    cores = _omp_all_cores()
     rc = Reference("cnn")
     rng = np.random.default_rng(SEED)
     if workload == "sgemm_4096":
@@ -491,7 +604,7 @@ def gemm_cpu_reference(workload):
             t0 = time.perf_counter()
             rc.sgemm("N", "N", n, n, n, 1.0, A, B, 0.0, C)
             ts.append(time.perf_counter() - t0)
-        return {"value": 2 * n ** 3 / min(ts) / 1e9, "unit": "GFLOP/s", "cores": os.cpu_count(), "kind": "reference",
+        return {"value": 2 * n ** 3 / min(ts) / 1e9, "unit": "GFLOP/s", "cores": cores, "kind": "reference",
                 "sample": f"gemm_rnn {n}^3 (17.2 GFLOP), best of 2"}
     # CNN: every layer at batch 4 (the linear layers at 128), scaled to batch 128
     t_total = 0.0
@@ -511,7 +624,7 @@ def gemm_cpu_reference(workload):
             rc.linear_forward(x, wt, b, ci, co)
             t_total += time.perf_counter() - t0
     gf = sum(layer_flops(L) for L in CNN_LAYERS)
-    return {"value": gf / t_total / 1e9, "unit": "GFLOP/s", "cores": os.cpu_count(), "kind": "reference",
+    return {"value": gf / t_total / 1e9, "unit": "GFLOP/s", "cores": cores, "kind": "reference",
             "sample": f"convolutions at batch 4 scaled x32, linear layers at batch 128; {t_total:.2f} s per forward"}
 
 
@@ -674,8 +787,9 @@ def main():
                     choices=sorted(WORKLOADS) + sorted(BATCHED) + ["sgemm_4096", "cnn_forward_b128"])
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tp", action="store_true",
-                    help="decode workloads under torchrun: shard one model over the ranks (tensor parallelism)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="decode workloads under torchrun: every rank decodes its own replica instead of one "
+                         "model sharded over the ranks by tensor parallelism (the default)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload in ("sgemm_4096", "cnn_forward_b128"):
@@ -689,65 +803,68 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
         cfg = cfg_for(args.workload, args.layers)
-        cb = cpu_reference(cfg, "reference", samples=max(3, min(args.steps, 5)))
+        cb = cpu_reference(cfg, "reference")
         line = {"impl": "reference", "metric": "decode tok/s (batch 1)", "value": round(cb["value"], 3),
                 "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(1e3 / cb["value"], 3), "higher_is_better": True, "scaling": "weak",
+                "ms_per_step": round(1e3 / cb["value"], 3), "higher_is_better": True,
+                "scaling": "strong" if ws > 1 and not args.replicas else "weak",
                 "vs_baseline": None, "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)",
                                                8: "q8_0 x q8"}[cfg.wtype],
-                "data": "synthetic", "config": {"workload": workload_name(args), "batch": 1, "prompt": PROMPT},
+                "data": "synthetic", "config": decode_config(args, cfg, ws, ws > 1 and not args.replicas),
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
 
-    dist, rank, ws, local = dist_init("gloo" if args.tp else "nccl")
-    ms, e2e_s, kms, kbytes, kinds, wbytes, clocks, cfg = run_ours(args, dist, rank, ws, local)
+    tp_default = int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.replicas
+    dist, rank, ws, local = dist_init("gloo" if tp_default else "nccl")
+    r = run_ours(args, dist, rank, ws, local)
     if rank != 0:
         if dist:
             dist.destroy_process_group()
         return
+    cfg, ms, tp = r["cfg"], r["ms"], r["tp"]
     peak, peak_kind = peaks()
-    tp = args.tp and ws > 1
     seqs = 1 if tp else ws   # sequences decoded by the whole job
     tok_s = seqs * args.steps / (ms * 1e-3)
-    achieved = kbytes / (kms * 1e-3) / 1e9
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tf):
-        traffic = json.load(open(tf)).get(workload_name(args), {}).get("dram_bytes_per_step")
-        traffic = traffic * args.steps if traffic else None
+    achieved = r["kbytes"] / (ms * 1e-3) / 1e9
+    if tp and r["engine"] == "persistent":
+        kern = "k_decode per GPU with the partial rows of wo and w2 pushed to every peer (%d steps per launch)" % args.steps
+    elif tp:
+        kern = ("graph engine per GPU: k_matvec / k_attention / residual adds, NCCL allreduce after wo and w2, one "
+                "CUDA graph per token")
+    else:
+        kern = "k_decode (persistent cooperative decode, %d steps per launch)" % args.steps
     line = {
         "metric": "decode tok/s (batch 1)", "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)", 8: "q8_0 x q8"}[cfg.wtype],
         "data": "synthetic",
-        "config": {"workload": workload_name(args), "batch": 1, "prompt": PROMPT, "dim": cfg.dim,
-                   "layers": cfg.n_layers, "context": cfg.seq_len,
-                   "parallelism": f"tp{ws}" if tp else (f"replicas{ws}" if ws > 1 else "single"),
-                   "l2": (f"weights {wbytes / 1e9:.2f} GB per step > 126 MB L2; no flush" if wbytes > 126e6 else
-                          f"weights {wbytes / 1e6:.0f} MB per step; L2-resident, no flush")},
-        "roofline": {"bound": "hbm",
-                     "kernel": ("graph engine per GPU: k_matvec / k_attention / residual adds, NCCL allreduce after "
-                                "wo and w2, one CUDA graph per token" if tp else
-                                "k_decode (persistent cooperative decode, %d steps per launch)" % args.steps),
+        "config": decode_config(args, cfg, ws, tp),
+        "roofline": {"bound": "hbm", "kernel": kern,
                      "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "bytes_per_launch": int(kbytes), "weight_bytes_per_step": int(wbytes),
-                     "ms_per_launch": round(kms, 3)},
-        "graph_engine_kernels": kinds,
-        "e2e": {"value": round(seqs * args.e2e_steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 16,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     # DRAM bytes come from ncu captures, which a timed run does not take
+                     "traffic": None,
+                     "bytes_per_launch": int(r["kbytes"]), "weight_bytes_per_step": int(r["wbytes"]),
+                     "ms_per_launch": round(ms, 3)},
+        "e2e": {"value": round(seqs * args.e2e_steps / r["e2e_s"], 2), "unit": "tok/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": cfg.vocab * 4},
-        # persistent kernel: one launch; graph engine with tensor parallelism: per layer the qkv,
-        # attention, wo, w1/w3 and w2 kernels and two residual adds, then the classifier and
-        # the advance kernel, per step (the NCCL collectives are NCCL's kernels)
-        "gpu_launches": args.steps * (7 * cfg.n_layers + 2) if tp else 1,
-        "clocks": clocks,
+        # persistent kernel: one launch (per GPU); graph engine with tensor parallelism: per layer the
+        # qkv, attention, wo, w1/w3 and w2 kernels and two residual adds, then the classifier and the
+        # advance kernel, per step (the NCCL collectives are NCCL's kernels)
+        "gpu_launches": args.steps * (7 * cfg.n_layers + 2) if (tp and r["engine"] == "graph") else 1,
+        "clocks": r["clocks"],
     }
-    if not args.no_cpu_baseline:
+    if r["kinds"]:
+        line["graph_engine_kernels"] = r["kinds"]
+    if r["parity"]:
+        line["parity"] = r["parity"]
+    if not args.no_cpu_baseline and ws == 1:
         line["cpu_baseline"] = cpu_reference(cfg, "reference")
     print(json.dumps(line))
     if dist:

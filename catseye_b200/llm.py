@@ -159,6 +159,14 @@ class GpuLLM:
                    "time_product")
         return ms.value, fl.value, wb.value
 
+    def tp_persistent(self):
+        """Select the persistent kernel for this model; False (engine unchanged)
+        when this build runs the model only in the per-phase graph engine."""
+        if self.lib.cats_gpu_llm_set_engine(self.h, ENGINE_PERSISTENT) != 0:
+            self.lib.cats_gpu_clear_error()
+            return False
+        return True
+
     def set_engine(self, engine):
         """ENGINE_PERSISTENT (default): one cooperative kernel runs whole tokens;
         ENGINE_GRAPH: a CUDA graph of per-phase kernels."""

@@ -31,10 +31,12 @@ def _ptr(a):
 
 
 def aligned(a, align=256):
-    """Copy `a` into a buffer whose address is a multiple of `align` bytes: the
-    reference allocates everything 256-byte aligned (llm/catseye_llm.h:36-46)
-    and its AVX code uses aligned loads."""
+    """`a` itself when its address is a multiple of `align` bytes, else a copy
+    in such a buffer: the reference allocates everything 256-byte aligned
+    (llm/catseye_llm.h:36-46) and its AVX code uses aligned loads."""
     a = np.ascontiguousarray(a)
+    if a.ctypes.data % align == 0:
+        return a
     raw = np.empty(a.nbytes + align, dtype=np.uint8)
     off = (-raw.ctypes.data) % align
     out = raw[off:off + a.nbytes].view(a.dtype).reshape(a.shape)
@@ -232,6 +234,8 @@ class Reference:
             L.ref_llm_destroy.argtypes = [_vp]
             if hasattr(L, "ref_llm_use_f32_activations"):   # AVX builds only (matmul_q4_0)
                 L.ref_llm_use_f32_activations.argtypes = [_vp]
+            if hasattr(L, "ref_llm_use_q8_activations"):
+                L.ref_llm_use_q8_activations.argtypes = [_vp]
         else:
             L.ref_sgemm.argtypes = [C.c_char, C.c_char, C.c_int, C.c_int, C.c_int, C.c_float,
                                     _vp, _vp, C.c_float, _vp]
@@ -325,6 +329,11 @@ class RefLLM:
             if not hasattr(ref.lib, "ref_llm_use_f32_activations"):
                 raise ValueError("this reference build has no matmul_q4_0 (AVX builds only)")
             ref.lib.ref_llm_use_f32_activations(self.h)
+
+    def use_q8_activations(self):
+        """Rebind the Q4_0 tensors to the default quantize_q8 + matmul_q4_0_q8
+        (after a prompt went through the fp32-activation binding)."""
+        self.ref.lib.ref_llm_use_q8_activations(self.h)
 
     def step(self, token, pos):
         p = self.ref.lib.ref_llm_step(self.h, token, pos)

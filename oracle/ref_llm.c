@@ -145,6 +145,24 @@ int ref_llm_use_f32_activations(void *h)
 }
 #endif
 
+/* Back to the runtime's default Q4_0 binding (gguf_matmul / gguf_quantize,
+ * llm/catseye_llm.h:2583-2607): used after a prompt went through the
+ * fp32-activation binding, so the decode steps that follow run the default
+ * quantize_q8 + matmul_q4_0_q8 path over the cache the prompt left. */
+int ref_llm_use_q8_activations(void *h)
+{
+    ref_model *r = h;
+    int k = 0;
+    for (int i = 0; i < (int)(sizeof(r->m.tensor) / sizeof(r->m.tensor[0])); i++) {
+        cats_tensor *t = &r->m.tensor[i];
+        if (t->data && t->type == GGML_TYPE_Q4_0) {
+            bind(t, GGML_TYPE_Q4_0, t->data);
+            k++;
+        }
+    }
+    return k;
+}
+
 void ref_llm_destroy(void *h)
 {
     ref_model *r = h;

@@ -130,3 +130,32 @@ def test_gemm_forms_drop_in(gpu, orc):
         getattr(gpu, name)(M, N, K, 1.0, C.c_void_p(A.ctypes.data), C.c_void_p(B.ctypes.data), 0.0,
                            C.c_void_p(c.ctypes.data))
         assert rel(c, orc.sgemm(ta, tb, M, N, K, 1.0, A, B, 0.0, np.zeros(M * N, np.float32))) < TOL
+
+
+# The standalone SGEMM configuration (square M = N = K of 1024, 2048, 4096 in
+# the three forms catseye.h calls, beta 0 and 1) through the host drop-in
+# cats_sgemm, checked on 64 sampled rows of C: against the reference's own
+# gemm_rnn / gemm_rnt / gemm_rtn run on those rows only (A's sampled rows,
+# or A's sampled columns for TN, which give exactly those rows of C), and
+# against a float64 product.  The reference accumulates in fp32 in K order,
+# so its own error grows with K: the bar against it is 1e-5 plus that error.
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+@pytest.mark.parametrize("ta,tb", [("N", "N"), ("N", "T"), ("T", "N")])
+@pytest.mark.parametrize("n", [1024, 2048, 4096])
+def test_sgemm_config_sizes_sampled_rows(mm, ref_cnn, ta, tb, n, beta):
+    rng = np.random.default_rng(n * 7 + (ta == "T") * 3 + (tb == "T") + int(beta) * 11)
+    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    B = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    C0 = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    c = C0.copy()
+    mm.sgemm(ta, tb, n, n, n, 1.0, A, B, beta, c)
+    rows = np.sort(rng.choice(n, 64, replace=False))
+    a_rows = np.ascontiguousarray(A[:, rows] if ta == "T" else A[rows])   # [K][64] for TN, else [64][K]
+    c_ref = ref_cnn.sgemm(ta, tb, 64, n, n, 1.0, a_rows.reshape(-1), B.reshape(-1), beta,
+                          np.ascontiguousarray(C0[rows]).reshape(-1)).reshape(64, n)
+    opA = (A.T if ta == "T" else A)[rows].astype(np.float64)
+    opB = (B.T if tb == "T" else B).astype(np.float64)
+    exact = opA @ opB + beta * C0[rows].astype(np.float64)
+    got = c[rows]
+    assert rel(got, exact) < TOL, (ta, tb, n, beta)
+    assert rel(got, c_ref) < TOL + rel(c_ref, exact), (ta, tb, n, beta, rel(c_ref, exact))

@@ -338,6 +338,8 @@ def run_ours(args, dist, rank, ws, local):
         m.set_engine(llm.ENGINE_GRAPH)
         engine = "graph"
     m.init_random(SEED)
+    if dist:   # sharded: the ranks start their first step together (the exchange waits are bounded)
+        dist.barrier()
     red_dev = "cpu" if tp else "cuda"     # gloo reduces host tensors
     stream = torch.cuda.ExternalStream(m.stream)
     rng = np.random.default_rng(SEED + 1)

@@ -67,6 +67,7 @@ SIGNATURES = {
     "cats_gpu_tp_unique_id_bytes": (_sz, []),
     "cats_gpu_tp_unique_id": (_i, [_vp, _sz]),
     "cats_gpu_llm_tp_connect": (_i, [_vp, _vp]),
+    "cats_gpu_llm_tp_loopback": (_i, [_vp]),
     "cats_gpu_llm_trace_step": (_i, [_vp, _i, _i, _vp, _i, C.POINTER(C.c_int)]),
     "cats_gpu_llm_set_position": (_i, [_vp, _i, _i]),
     "cats_gpu_llm_synchronize": (_i, [_vp]),

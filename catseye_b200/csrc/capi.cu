@@ -476,7 +476,8 @@ cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg)
                 cfg->wtype, cfg->tp_size > 1 ? cfg->tp_rank : 0, cfg->tp_size > 0 ? cfg->tp_size : 1};
     if (c.tp_rank < 0 || c.tp_rank >= c.tp_size) { fail(CATS_ERR_ARG, "cats_gpu_llm_create: tp_rank"); return nullptr; }
     cats_gpu_llm *h = new cats_gpu_llm();
-    // the persistent kernel has no exchange step yet: sharded models use the per-phase graph
+    // sharded models run the per-phase graph until cats_gpu_llm_tp_connect has
+    // mapped the peers' exchange buffers (then the persistent kernel)
     if (c.tp_size > 1) h->engine = CATS_ENGINE_GRAPH;
     int rc = llm_alloc(&h->m, c);
     if (rc == CATS_OK && cudaMalloc(&h->tok_log, (size_t)(c.seq_len + 1) * 4) != cudaSuccess) rc = CATS_ERR_NOMEM;
@@ -519,6 +520,7 @@ static int ensure_graph(cats_gpu_llm *h)
 {
     if (!h->m.weights_ready) return fail(CATS_ERR_ARG, "llm: weights not set");
     if (h->engine == CATS_ENGINE_PERSISTENT) {
+        if (h->m.c.tp_size > 1 && !h->m.tp_p2p) return fail(CATS_ERR_ARG, "llm: tensor parallel model not connected");
         int rc = decode_prepare(&h->m);
         return rc ? fail(rc, "llm: persistent decode setup") : CATS_OK;
     }
@@ -546,8 +548,10 @@ int cats_gpu_llm_set_engine(cats_gpu_llm *h, int engine)
 {
     if (!h || (engine != CATS_ENGINE_PERSISTENT && engine != CATS_ENGINE_GRAPH))
         return fail(CATS_ERR_ARG, "cats_gpu_llm_set_engine");
-    if (engine == CATS_ENGINE_PERSISTENT && h->m.c.tp_size > 1)
-        return fail(CATS_ERR_UNSUPPORTED, "cats_gpu_llm_set_engine: the persistent engine runs one GPU");
+    if (engine == CATS_ENGINE_PERSISTENT && h->m.c.tp_size > 1 && !h->m.tp_p2p)
+        return fail(CATS_ERR_UNSUPPORTED,
+                    "cats_gpu_llm_set_engine: this sharded model has no mapped peers (not connected, ranks sharing "
+                    "a GPU, or CATS_TP_NO_P2P=1): the persistent engine needs them");
     h->engine = engine;
     return CATS_OK;
 }
@@ -566,7 +570,18 @@ int cats_gpu_llm_tp_connect(cats_gpu_llm *h, const void *id)
     if (!h || !id || h->m.c.tp_size < 2) return fail(CATS_ERR_ARG, "cats_gpu_llm_tp_connect");
     if (check(cudaSetDevice(g.device), "cats_gpu_llm_tp_connect")) return g.last_err;
     int rc = tp_connect(&h->m, id);
-    return rc ? fail(rc, "cats_gpu_llm_tp_connect") : CATS_OK;
+    if (rc) return fail(rc, "cats_gpu_llm_tp_connect");
+    if (h->m.tp_p2p) h->engine = CATS_ENGINE_PERSISTENT;   // the exchange inside the persistent kernel
+    return CATS_OK;
+}
+
+int cats_gpu_llm_tp_loopback(cats_gpu_llm *h)
+{
+    if (!h || h->m.c.tp_size < 2) return fail(CATS_ERR_ARG, "cats_gpu_llm_tp_loopback");
+    int rc = tp_loopback(&h->m);
+    if (rc) return fail(rc, "cats_gpu_llm_tp_loopback");
+    h->engine = CATS_ENGINE_PERSISTENT;
+    return CATS_OK;
 }
 
 int cats_gpu_llm_set_position(cats_gpu_llm *h, int token, int pos)

@@ -28,10 +28,24 @@
 //    (:1944-1956) into the next token and position, so `steps` tokens decode
 //    with no host round trip.
 //
+//  * Tensor parallelism (one process and one GPU per rank): each rank runs
+//    this kernel over its weight slices (llm.cu shards them).  wo and w2 give
+//    partial sums of every row; a CTA keeps its rows in shared memory and, at
+//    the phase's end, stores them with plain 64-byte stores straight into
+//    every rank's exchange buffer over NVLink (peer memory mapped with CUDA
+//    IPC), then counts itself in on every rank with a system-scope atomic and
+//    waits (bounded) until all CTAs of all ranks have done so.  The next
+//    staging adds the residual and the ranks' partial rows in rank order, so
+//    every rank holds the same residual stream bit for bit.  The classifier
+//    rows go to every rank's logits the same way, and the greedy key is a
+//    system-scope max on every rank's word.  No collective library call, no
+//    bulk copy from peer memory, no multicast.
+//
 // Shared memory: a fixed 1 KB header (the mbarriers at offset 0, reduction
 // scratch, flags), the weight descriptors, then the two rings (group g's
-// slot k at index g * stages + k), then the staged activation.  The
-// mbarriers are invalidated before the kernel exits.
+// slot k at index g * stages + k), then the staged activation, then (with
+// tensor parallelism) the CTA's rows to push.  The mbarriers are invalidated
+// before the kernel exits.
 #include "llm.cuh"
 #include "mv_device.cuh"
 #include <algorithm>
@@ -82,6 +96,13 @@ struct DecodeArgs {
     int *err;
     unsigned long long *trace;   // optional per-CTA phase timeline (globaltimer ns), trace_stride records each
     int trace_stride;
+    // tensor parallelism (tp_size > 1; see TpXchg for the exchange buffers)
+    int tp_size, tp_rank, vocab_off;
+    unsigned int tp_epoch;                // arrivals per source rank counted before this launch
+    uint8_t *tp_peer[TP_MAX_RANKS];       // rank r's exchange buffer, mapped here (this rank's at tp_rank)
+    unsigned long long tp_logits_off;     // byte offset of the logits in an exchange buffer
+    float *x_alt;                         // the residual stream alternates between x and x_alt
+    uint32_t push_bytes;                  // shared memory for the CTA's rows to push
 };
 
 __device__ __forceinline__ unsigned long long global_ns()
@@ -131,6 +152,7 @@ struct Smem {
     volatile int *abort_s;   // hint for bounded waits: stop waiting, the kernel is unwinding
     volatile int *sync_ok;   // grid_sync's decision, written by thread 0 between its two CTA barriers
     WDesc *wd;               // the weight descriptors, copied in at the start (global reads cost microseconds)
+    float *push;             // tensor parallelism: this CTA's rows of the phase, 16 per tile it owns
 };
 
 __host__ __device__ inline size_t desc_bytes(int n_wd)
@@ -149,14 +171,15 @@ __device__ __forceinline__ Smem smem_layout(uint8_t *base, const DecodeArgs &a)
     s.wd = reinterpret_cast<WDesc *>(base + DEC_HEADER);
     s.ring = base + DEC_HEADER + desc_bytes(a.n_wd);
     s.xs = s.ring + (size_t)DEC_GROUPS * a.stages * a.slot_bytes;
+    s.push = reinterpret_cast<float *>(s.xs + a.xs_bytes);
     return s;
 }
 static_assert(2 * DEC_GROUPS * DEC_MAX_STAGES * 8 + 64 * 4 + 8 <= DEC_HEADER, "smem header overflow");
 static_assert(sizeof(WDesc) % 16 == 0, "descriptors are copied as 16-byte words");
 
-size_t decode_smem_bytes(int n_wd, int stages, uint32_t slot, uint32_t xs)
+size_t decode_smem_bytes(int n_wd, int stages, uint32_t slot, uint32_t xs, uint32_t push = 0)
 {
-    return DEC_HEADER + desc_bytes(n_wd) + (size_t)DEC_GROUPS * stages * slot + xs;
+    return DEC_HEADER + desc_bytes(n_wd) + (size_t)DEC_GROUPS * stages * slot + xs + push;
 }
 
 // Grid barrier among the consumer threads of every CTA.  Returns false when
@@ -182,6 +205,137 @@ __device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, u
                 if ((++i & 63) == 0 && (i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag))) {
                     ok = false;
                     break;
+                }
+            }
+        }
+        if (!ok) {
+            if (a.err) atomicOr(a.err, CATS_DEVERR_PEER_WAIT);
+            atomicExch(a.abort_flag, 1);
+            *sm.abort_s = 1;
+        }
+        *sm.sync_ok = ok ? 1 : 0;
+    }
+    named_bar_sync(1, DEC_NC);
+    return *sm.sync_ok != 0;
+}
+
+// Tiles of a weight this CTA owns: blockIdx.x, blockIdx.x + grid, ...  They
+// are processed in pairs; group g takes tile 2p+g of pair p, through its own
+// ring.  The producer issues a pair's chunks alternately into the two rings
+// (tile A seg 0, tile B seg 0, tile A seg 1, ...).
+__device__ __forceinline__ int my_tiles(const WDesc &W)
+{
+    return (int)blockIdx.x < W.n_tiles ? (W.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The partial rows of every rank for one exchange: the residual stream plus
+// rank 0's rows, plus rank 1's, ... in rank order (identical on every rank),
+// with all loads of a round issued before any is used.
+struct ReduceSrc {
+    const float4 *x;      // residual stream before the block
+    const float4 *recv;   // [ranks][n4] partial rows
+    int ranks;
+    __device__ __forceinline__ static float4 add4(float4 a, float4 b)
+    {
+        return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+    }
+    template <int V>
+    __device__ __forceinline__ void fill(float4 (&v)[V], int i0, int stride, int n4) const
+    {
+        constexpr int RB = V >= 4 ? 2 : (V == 2 ? 4 : 8);   // partial vectors per round of loads
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            const int i = i0 + k * stride;
+            v[k] = i < n4 ? __ldcg(x + i) : z;
+        }
+        for (int r0 = 0; r0 < ranks; r0 += RB) {
+            float4 p[RB][V];
+#pragma unroll
+            for (int rr = 0; rr < RB; rr++)
+#pragma unroll
+                for (int k = 0; k < V; k++) {
+                    const int i = i0 + k * stride;
+                    p[rr][k] = (r0 + rr < ranks && i < n4) ? __ldcg(recv + (size_t)(r0 + rr) * n4 + i) : z;
+                }
+#pragma unroll
+            for (int rr = 0; rr < RB; rr++)
+                if (r0 + rr < ranks)
+#pragma unroll
+                    for (int k = 0; k < V; k++) v[k] = add4(v[k], p[rr][k]);
+        }
+    }
+};
+
+__device__ __forceinline__ float *tp_recv(const DecodeArgs &a, int rank, int slot)
+{
+    return reinterpret_cast<float *>(a.tp_peer[rank] + TpXchg::recv) + (size_t)slot * a.tp_size * a.dim;
+}
+
+// Store this CTA's rows of weight W (sm.push, 16 per owned tile) into every
+// rank's buffer: the partial rows of this rank in slot `slot` (logits = false)
+// or the logits rows at the rank's vocabulary offset.  Four consecutive
+// threads write one tile's 64 bytes to one rank.
+__device__ __forceinline__ void tp_push(const DecodeArgs &a, const Smem &sm, const WDesc &W, bool logits, int slot)
+{
+    constexpr int R = DEC_GW * DEC_RPW;
+    const int items = my_tiles(W) * a.tp_size * (R / 4);
+    for (int it = threadIdx.x; it < items; it += DEC_NC) {
+        const int q = it & (R / 4 - 1), rest = it / (R / 4);
+        const int r = rest % a.tp_size, j = rest / a.tp_size;
+        const int row = (blockIdx.x + j * gridDim.x) * R + q * 4;
+        if (row >= W.d) continue;
+        float *dst = logits ? reinterpret_cast<float *>(a.tp_peer[r] + a.tp_logits_off) + a.vocab_off + row
+                            : tp_recv(a, r, slot) + (size_t)a.tp_rank * a.dim + row;
+        const float *src = sm.push + j * R + q * 4;
+        if (row + 4 <= W.d && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            *reinterpret_cast<float4 *>(dst) = *reinterpret_cast<const float4 *>(src);
+        } else {
+            for (int e = 0; e < 4 && row + e < W.d; e++) dst[e] = src[e];
+        }
+    }
+}
+
+// Exchange among the ranks (and grid barrier of this rank's CTAs): push the
+// CTA's rows of W (when given), publish them and the CTA's greedy key (the
+// classifier, key != 0) with a system-scope fence, count in on every rank,
+// then wait until every CTA of every rank has counted in.  Bounded like
+// grid_sync, with the same CTA-wide decision.
+__device__ __forceinline__ bool tp_sync(const DecodeArgs &a, const Smem &sm, unsigned &target, const WDesc *W,
+                                        bool logits, int slot, unsigned long long key)
+{
+    named_bar_sync(1, DEC_NC);   // the CTA's rows are in shared memory
+    if (W && *sm.abort_s == 0) tp_push(a, sm, *W, logits, slot);
+    named_bar_sync(1, DEC_NC);   // every store of the CTA issued
+    if (threadIdx.x == 0) {
+        bool ok = *sm.abort_s == 0;
+        if (ok) {
+            target += gridDim.x;
+            for (int r = 0; key && r < a.tp_size; r++)
+                asm volatile("red.relaxed.sys.global.max.u64 [%0], %1;"
+                             ::"l"(a.tp_peer[r] + TpXchg::argmax), "l"(key) : "memory");
+            // cumulative: orders the CTA's stores (seen by this thread through
+            // the CTA barrier) before the arrivals below, for every GPU
+            __threadfence_system();
+            for (int r = 0; r < a.tp_size; r++)
+                asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;"
+                             ::"l"(reinterpret_cast<unsigned *>(a.tp_peer[r] + TpXchg::bar) + a.tp_rank) : "memory");
+            const unsigned *bar = reinterpret_cast<const unsigned *>(a.tp_peer[a.tp_rank] + TpXchg::bar);
+            uint32_t i = 0;
+            for (int r = 0; r < a.tp_size && ok; r++) {
+                while ((int)(ld_acquire_sys_u32(bar + r) - target) < 0) {
+                    __nanosleep(50);
+                    if ((++i & 63) == 0 && (i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag))) {
+                        ok = false;
+                        break;
+                    }
                 }
             }
         }
@@ -241,16 +395,10 @@ __device__ __forceinline__ void ring_adv(Ring &r, int stages)
     if (++r.slot == stages) { r.slot = 0; r.phase ^= 1; }
 }
 
-// Tiles of a weight this CTA owns: blockIdx.x, blockIdx.x + grid, ...  They
-// are processed in pairs; group g takes tile 2p+g of pair p, through its own
-// ring.  The producer issues a pair's chunks alternately into the two rings
-// (tile A seg 0, tile B seg 0, tile A seg 1, ...).
-__device__ __forceinline__ int my_tiles(const WDesc &W)
-{
-    return (int)blockIdx.x < W.n_tiles ? (W.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-}
 
-enum DecEpi { DE_QKV, DE_ADD, DE_SWIGLU, DE_CLS };
+// DE_PUSH: tensor parallelism's partial rows of wo / w2, kept in shared
+// memory for tp_sync to push (the residual is added when they are summed).
+enum DecEpi { DE_QKV, DE_ADD, DE_SWIGLU, DE_CLS, DE_PUSH };
 
 // Residual rows (row0, row0 + 1) of tile t for this warp, read by lane 0.  A
 // load queued behind the SM's weight copies takes microseconds, so these are
@@ -332,12 +480,23 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
                     } else if (epi == DE_ADD) {   // residual (:1731-1733, :1759-1761)
                         a.x[row0] = xr[0] + v0;
                         if (row0 + 1 < W.d) a.x[row0 + 1] = xr[1] + v1;
+                    } else if (epi == DE_PUSH) {
+                        float *pr = sm.push + (2 * p + grp) * R + gw * DEC_RPW;
+                        pr[0] = v0;
+                        pr[1] = v1;
                     } else {
-                        a.logits[row0] = v0;
-                        unsigned long long k = argmax_key(v0, row0);
+                        // tensor parallelism: this rank's vocabulary rows, pushed to every rank at tp_sync
+                        if (a.tp_size > 1) {
+                            float *pr = sm.push + (2 * p + grp) * R + gw * DEC_RPW;
+                            pr[0] = v0;
+                            pr[1] = v1;
+                        } else {
+                            a.logits[row0] = v0;
+                            if (row0 + 1 < W.d) a.logits[row0 + 1] = v1;
+                        }
+                        unsigned long long k = argmax_key(v0, a.vocab_off + row0);
                         if (row0 + 1 < W.d) {
-                            a.logits[row0 + 1] = v1;
-                            const unsigned long long k1 = argmax_key(v1, row0 + 1);
+                            const unsigned long long k1 = argmax_key(v1, a.vocab_off + row0 + 1);
                             k = k1 > k ? k1 : k;
                         }
                         best = k > best ? k : best;
@@ -577,19 +736,39 @@ __device__ __forceinline__ void produce(const DecodeArgs &a, const Smem &sm, int
 }
 
 // Consumers (16 warps).  Every consumer warp takes the same path through
-// stage_act / grid_sync (both hold CTA barriers); only grid_sync's broadcast
-// decision ends it.
-template <int WT>
+// stage_act / grid_sync / tp_sync (all hold CTA barriers); only their
+// broadcast decision ends it.
+//
+// With tensor parallelism the residual stream alternates between two buffers:
+// the staging after an exchange reads one (plus every rank's partial rows)
+// and CTA 0 writes the sum into the other, which no CTA reads until the next
+// exchange has completed.  The partial rows alternate between two slots: a
+// slot is written again only two exchanges later, after every rank has
+// passed the exchange that follows its reading.
+template <int WT, bool TP>
 __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr bool tp = TP;   // a separate instance: the one-GPU form keeps its registers
     Ring rg{0, 0};
-    unsigned target = 0;
+    unsigned target = 0, xtarget = a.tp_epoch;
     unsigned long long best = 0ull;
     const int tid = threadIdx.x;
     const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
     const float no_rows[2] = {0.f, 0.f};
+    float *xcur = a.x, *xnext = a.x_alt;   // tensor parallelism: the residual stream's two buffers
+    int slot = 0;                          // tensor parallelism: the slot the next partial rows go to
     int tk = 0;
+    // staging after an exchange: residual + every rank's partial rows of `slot`
+    auto stage_sum = [&](const float *norm_w) {
+        stage_act<WT, DEC_STAGE_V>(ReduceSrc{reinterpret_cast<const float4 *>(xcur),
+                                             reinterpret_cast<const float4 *>(tp_recv(a, a.tp_rank, slot)), a.tp_size},
+                                   a.dim, norm_w, blockIdx.x == 0 ? xnext : nullptr, sm.xs, sm.red, tid, DEC_NC);
+        float *t = xcur;
+        xcur = xnext;
+        xnext = t;
+        slot ^= 1;
+    };
     trace_mark(a, tk);
     for (int step = 0; step < a.steps; step++) {
         const int pos = ld_volatile_i32(&a.params->pos);
@@ -606,7 +785,9 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             // qkv: rmsnorm + quantize, [wq;wk;wv], RoPE, k/v into the cache
             if (l == 0)
                 stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.emb + (size_t)token * a.dim), false},
-                                           a.dim, a.rms_att, blockIdx.x == 0 ? a.x : nullptr, sm.xs, sm.red, tid, DEC_NC);
+                                           a.dim, a.rms_att, blockIdx.x == 0 ? xcur : nullptr, sm.xs, sm.red, tid, DEC_NC);
+            else if (tp)
+                stage_sum(a.rms_att + (size_t)l * a.dim);
             else
                 stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_att + (size_t)l * a.dim, nullptr, sm.xs,
                                            sm.red, tid, DEC_NC);
@@ -615,8 +796,8 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
-            float xr[2];
-            residual_first(a, wl[1], xr);   // x is final until the wo epilogue
+            float xr[2] = {0.f, 0.f};
+            if (!tp) residual_first(a, wl[1], xr);   // x is final until the wo epilogue
             // short contexts: one CTA per head, merged in shared memory
             if (pos < DEC_LOCAL_ATTN_MAX_T && a.heads <= (int)gridDim.x &&
                 a.xs_bytes >= local_attn_scratch_bytes(a.head_size))
@@ -626,18 +807,22 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             if (!(alive = grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
-            // wo: quantize the attention output, matvec, residual add
+            // wo: quantize the attention output, matvec, residual add (tensor
+            // parallelism: partial rows exchanged, summed by the next staging)
             stage_act<WT, DEC_STAGE_V, false>(Float4Src{reinterpret_cast<const float4 *>(a.xb), true}, a.q_dim,
                                               nullptr, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT>(a, sm, wl[1], rg, DE_ADD, l, pos, best, tk, xr);
+            run_matvec<WT>(a, sm, wl[1], rg, tp ? DE_PUSH : DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
-            if (!(alive = grid_sync(a, sm, target))) break;
+            if (!(alive = tp ? tp_sync(a, sm, xtarget, &wl[1], false, slot, 0ull) : grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
-            residual_first(a, wl[3], xr);   // x is final until the w2 epilogue
+            if (!tp) residual_first(a, wl[3], xr);   // x is final until the w2 epilogue
             // w1/w3 + SwiGLU
-            stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs,
-                                       sm.red, tid, DEC_NC);
+            if (tp)
+                stage_sum(a.rms_ffn + (size_t)l * a.dim);
+            else
+                stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs,
+                                           sm.red, tid, DEC_NC);
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
@@ -647,27 +832,33 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             stage_act<WT, DEC_STAGE_V_WIDE, false>(Float4Src{reinterpret_cast<const float4 *>(a.hb), true}, a.hidden,
                                                    nullptr, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
-            run_matvec<WT>(a, sm, wl[3], rg, DE_ADD, l, pos, best, tk, xr);
+            run_matvec<WT>(a, sm, wl[3], rg, tp ? DE_PUSH : DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
-            alive = grid_sync(a, sm, target);
+            alive = tp ? tp_sync(a, sm, xtarget, &wl[3], false, slot, 0ull) : grid_sync(a, sm, target);
             trace_mark(a, tk);
         }
         if (!alive) break;
         // classifier + greedy argmax
-        stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
+        if (tp)
+            stage_sum(a.rms_final);
+        else
+            stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
         best = 0ull;
         trace_mark(a, tk);
-        run_matvec<WT>(a, sm, sm.wd[4 * a.n_layers], rg, DE_CLS, 0, pos, best, tk, no_rows);
+        const WDesc &wc = sm.wd[4 * a.n_layers];
+        run_matvec<WT>(a, sm, wc, rg, DE_CLS, 0, pos, best, tk, no_rows);
         trace_mark(a, tk);
         unsigned long long *keys = reinterpret_cast<unsigned long long *>(sm.red + 32);
         if (lane == 0) keys[warp] = best;
         named_bar_sync(1, DEC_NC);
+        unsigned long long mk = 0;
         if (tid == 0) {
-            unsigned long long mk = 0;
             for (int w = 0; w < DEC_WARPS; w++) mk = keys[w] > mk ? keys[w] : mk;
-            if (mk) atomicMax(a.argmax, mk);
+            if (mk && !tp) atomicMax(a.argmax, mk);
         }
-        if (!grid_sync(a, sm, target)) break;
+        // tensor parallelism: the logits rows go to every rank and the key is
+        // maxed into every rank's word (thread 0 holds the CTA's key)
+        if (!(tp ? tp_sync(a, sm, xtarget, &wc, true, 0, mk) : grid_sync(a, sm, target))) break;
         if (blockIdx.x == 0 && tid == 0) {
             const unsigned long long k = atomicAdd(a.argmax, 0ull);
             int idx = 0x7fffffff - (int)(uint32_t)(k & 0xffffffffu);
@@ -690,7 +881,7 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
     }
 }
 
-template <int WT>
+template <int WT, bool TP>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant__ DecodeArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -715,7 +906,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(const __grid_constant
     if (warp >= DEC_WARPS) {
         if (lane == 0) produce(a, sm, warp - DEC_WARPS);
     } else {
-        consume<WT>(a, sm);
+        consume<WT, TP>(a, sm);
     }
     // Every thread gets here (none returns early) once all copies have landed
     // and every arrive is done: retire the mbarriers so the next kernel on
@@ -764,8 +955,16 @@ int decode_prepare(LlmModel *m)
     if (!add(m->cls)) return E_UNSUPPORTED;
     slot = (uint32_t)round_up(slot, 128);
     const uint32_t xs = (uint32_t)round_up(c.wtype == W_F32 ? (size_t)maxn * 4 : (size_t)(maxn / 32) * 40, 128);
+    // tensor parallelism: the rows of the CTA's tiles of wo / w2 (dim rows) and
+    // of the classifier slice, held until they are pushed
+    uint32_t push = 0;
+    if (c.tp_size > 1) {
+        const int R = DEC_GW * DEC_RPW, grid = matvec_num_sms();
+        const int rows = std::max(c.dim, m->vocab_loc);
+        push = (uint32_t)round_up((size_t)cdiv(cdiv(rows, R), grid) * R * 4, 128);
+    }
     const size_t cap = 227 * 1024;
-    const size_t fixed = decode_smem_bytes((int)v.size(), 0, slot, xs);
+    const size_t fixed = decode_smem_bytes((int)v.size(), 0, slot, xs, push);
     if (fixed + (size_t)DEC_GROUPS * 2 * slot > cap) return E_UNSUPPORTED;   // at least two slots per ring
     const int fit = (int)std::min<size_t>(DEC_MAX_STAGES, (cap - fixed) / ((size_t)DEC_GROUPS * slot));
     // Four slots per ring by default: with more, the copies queued at a phase
@@ -779,6 +978,7 @@ int decode_prepare(LlmModel *m)
     }
     m->dec_slot = slot;
     m->dec_xs = xs;
+    m->dec_push = push;
     m->dec_max_splits = 64;
     // all or nothing: wdesc is set last, so a failed setup is retried in full
     void *wd = nullptr;
@@ -799,10 +999,10 @@ int decode_prepare(LlmModel *m)
     return E_OK;
 }
 
-template <int WT>
+template <int WT, bool TP>
 static cudaError_t launch_decode_t(const DecodeArgs &a, size_t smem, int grid, cudaStream_t st)
 {
-    cudaError_t e = cudaFuncSetAttribute(k_decode<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(k_decode<WT, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -814,7 +1014,7 @@ static cudaError_t launch_decode_t(const DecodeArgs &a, size_t smem, int grid, c
     attrs[0].val.cooperative = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_decode<WT>, a);
+    return cudaLaunchKernelEx(&cfg, k_decode<WT, TP>, a);
 }
 
 cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, unsigned long long *trace,
@@ -864,16 +1064,44 @@ cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, uns
     a.err = m->err;
     a.trace = trace;
     a.trace_stride = trace_stride;
-    const size_t smem = decode_smem_bytes(a.n_wd, a.stages, a.slot_bytes, a.xs_bytes);
+    const int grid = matvec_num_sms();
+    a.tp_size = 1;
+    a.tp_rank = 0;
+    a.vocab_off = 0;
+    a.tp_epoch = 0;
+    a.tp_logits_off = 0;
+    a.x_alt = m->x2;
+    a.push_bytes = m->dec_push;
+    for (int r = 0; r < TP_MAX_RANKS; r++) a.tp_peer[r] = nullptr;
+    if (c.tp_size > 1) {
+        if (!m->tp_p2p) return cudaErrorInvalidValue;   // sharded models need the mapped exchange buffers
+        a.tp_size = c.tp_size;
+        a.tp_rank = c.tp_rank;
+        a.vocab_off = m->vocab_off;
+        a.tp_epoch = m->tp_epoch;
+        a.tp_logits_off = TpXchg::logits(c.tp_size, c.dim);
+        for (int r = 0; r < c.tp_size; r++) a.tp_peer[r] = m->tp_peer[r];
+        a.argmax = reinterpret_cast<unsigned long long *>(m->tp_xchg + TpXchg::argmax);
+        a.logits = m->logits;   // inside the exchange buffer; written by the pushes
+    }
+    const size_t smem = decode_smem_bytes(a.n_wd, a.stages, a.slot_bytes, a.xs_bytes, a.push_bytes);
     cudaError_t e = cudaMemsetAsync(m->dec_bar, 0, 16, m->stream);
     if (e) return e;
-    const int grid = matvec_num_sms();
+    const bool tp = c.tp_size > 1;
     switch (c.wtype) {
-    case W_F32: return launch_decode_t<W_F32>(a, smem, grid, m->stream);
-    case W_Q4_0: return launch_decode_t<W_Q4_0>(a, smem, grid, m->stream);
-    case W_Q8_0: return launch_decode_t<W_Q8_0>(a, smem, grid, m->stream);
+    case W_F32: e = tp ? launch_decode_t<W_F32, true>(a, smem, grid, m->stream)
+                       : launch_decode_t<W_F32, false>(a, smem, grid, m->stream); break;
+    case W_Q4_0: e = tp ? launch_decode_t<W_Q4_0, true>(a, smem, grid, m->stream)
+                        : launch_decode_t<W_Q4_0, false>(a, smem, grid, m->stream); break;
+    case W_Q8_0: e = tp ? launch_decode_t<W_Q8_0, true>(a, smem, grid, m->stream)
+                        : launch_decode_t<W_Q8_0, false>(a, smem, grid, m->stream); break;
+    default: return cudaErrorInvalidValue;
     }
-    return cudaErrorInvalidValue;
+    // every step of a launch runs 2 exchanges per layer and the classifier's,
+    // each counting one arrival per CTA of every rank on every rank
+    if (e == cudaSuccess && c.tp_size > 1)
+        m->tp_epoch += (unsigned)steps * (unsigned)(2 * c.n_layers + 1) * (unsigned)grid;
+    return e;
 }
 
 } // namespace cats

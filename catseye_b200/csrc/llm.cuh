@@ -6,6 +6,8 @@
 
 namespace cats {
 
+constexpr int TP_MAX_RANKS = 8;   // tensor-parallel ranks of the persistent kernel's exchange (one box)
+
 struct DevWeight {
     WeightLayout L;
     uint8_t *ptr = nullptr;
@@ -63,7 +65,7 @@ struct LlmModel {
     float *dec_part = nullptr;            // attention chunk partials [heads][max_splits][hs + 4]
     unsigned int *dec_bar = nullptr;      // [0] grid barrier counter, [1] abort flag
     int dec_stages = 0, dec_max_splits = 32;
-    uint32_t dec_slot = 0, dec_xs = 0;
+    uint32_t dec_slot = 0, dec_xs = 0, dec_push = 0;
     // batched step (batch.cu): prefill and batched decode on the tensor cores
     int n_seqs = 1;                       // KV sequences: kcache is [seq][layer][seq_len][kv_dim]
     int bt_cap = 0;                       // tokens per batched step (0: not reserved)
@@ -90,6 +92,26 @@ struct LlmModel {
     ArgmaxReduceFn argmax_reduce = nullptr;
     AllgatherFn allgather = nullptr;
     void *comm_ctx = nullptr;
+    // Tensor parallelism inside the persistent kernel (tp.cu, decode.cu): every
+    // rank's exchange buffer mapped into this process (CUDA IPC over NVLink),
+    // which the ranks' kernels write with plain stores and signal with
+    // system-scope atomics.  Layout of one buffer (TpXchg offsets):
+    // arrival counters per source rank, the greedy-argmax key, the partial
+    // rows of wo / w2 [2 slots][tp_size][dim], the full logits [vocab].
+    uint8_t *tp_xchg = nullptr;           // this rank's buffer (cudaMalloc, exported)
+    uint8_t *tp_peer[TP_MAX_RANKS] = {};  // rank r's buffer in this process (tp_peer[tp_rank] = tp_xchg)
+    bool tp_p2p = false;                  // ranks on distinct GPUs, buffers mapped: the persistent engine may run
+    unsigned int tp_epoch = 0;            // arrivals per source rank counted by the launches so far (wraps)
+    float *logits_own = nullptr;          // the model's own logits buffer while m->logits points into tp_xchg
+};
+
+// offsets into a tensor-parallel exchange buffer (LlmModel::tp_xchg)
+struct TpXchg {
+    static constexpr size_t bar = 0;         // unsigned int [TP_MAX_RANKS]: arrivals from each source rank
+    static constexpr size_t argmax = 128;    // unsigned long long: greedy key, max over every rank's rows
+    static constexpr size_t recv = 256;      // float [2][tp_size][dim]: partial rows of wo / w2
+    static size_t logits(int tp_size, int dim) { return recv + round_up((size_t)2 * tp_size * dim * 4, 256); }
+    static size_t bytes(int tp_size, int dim, int vocab) { return logits(tp_size, dim) + round_up((size_t)vocab * 4, 256); }
 };
 
 // tensor parallel (tp.cu): an NCCL unique id (made on one rank, passed to all),
@@ -97,6 +119,7 @@ struct LlmModel {
 int tp_unique_id(void *out, size_t bytes);
 size_t tp_unique_id_bytes();
 int tp_connect(LlmModel *m, const void *id_bytes);
+int tp_loopback(LlmModel *m);   // every rank's exchange buffer = this rank's (failure-detection check)
 void tp_release(LlmModel *m);
 
 int llm_alloc(LlmModel *m, const LlmConfig &c);

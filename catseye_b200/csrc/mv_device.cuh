@@ -54,6 +54,16 @@ struct Float4Src {
     const float4 *p;
     bool coherent;
     __device__ __forceinline__ float4 operator()(int i) const { return coherent ? __ldcg(p + i) : p[i]; }
+    // elements i0, i0 + stride, ... (V of them; zero past n4), every load issued before any is used
+    template <int V>
+    __device__ __forceinline__ void fill(float4 (&v)[V], int i0, int stride, int n4) const
+    {
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            const int i = i0 + k * stride;
+            v[k] = i < n4 ? (*this)(i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
 };
 
 // Stage the activation x[n] into xs: optional rmsnorm with norm_w
@@ -86,9 +96,9 @@ __device__ __forceinline__ void stage_act(const Src &src, int n, const float *no
 #pragma unroll
         for (int k = 0; k < V; k++) {
             const int i = base + tid + k * nthr;
-            v[k] = i < n4 ? src(i) : make_float4(0.f, 0.f, 0.f, 0.f);
             g[k] = (norm_w && i < n4) ? nw4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
         }
+        src.template fill<V>(v, base + tid, nthr, n4);
         float scale = 1.f;
         if (norm_w) {
             float ss = 0.f;

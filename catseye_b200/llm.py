@@ -159,6 +159,12 @@ class GpuLLM:
                    "time_product")
         return ms.value, fl.value, wb.value
 
+    def tp_loopback(self):
+        """Failure-detection check on one GPU: every rank's exchange buffer is
+        this rank's own, so the first exchange of a step waits for ranks that
+        never arrive and the step raises CatsGpuError (CATS_ERR_TIMEOUT)."""
+        _lib.check(self.lib.cats_gpu_llm_tp_loopback(self.h), "tp_loopback")
+
     def tp_persistent(self):
         """Select the persistent kernel for this model; False (engine unchanged)
         when this build runs the model only in the per-phase graph engine."""

@@ -175,13 +175,32 @@ int cats_gpu_llm_set_engine(cats_gpu_llm *m, int engine);
  * unique id (cats_gpu_tp_unique_id_bytes() bytes) and the caller hands it to
  * every rank; each rank calls cats_gpu_llm_tp_connect with it (the calls of
  * all ranks must overlap: NCCL waits for every rank) before its first step.
- * Sharded models run the per-phase graph engine: after wo and after w2 an
- * NCCL sum allreduce of dim floats, after the classifier a max allreduce of
- * the greedy key and an allgather of the logits.  Every rank feeds the same
- * tokens and gets the full logits. */
+ * With every rank on its own GPU of one box (up to 8 ranks), the connect
+ * also maps every rank's exchange buffer into every other rank (CUDA IPC) and
+ * the model runs the persistent kernel: after wo and after w2 each CTA stores
+ * its partial rows into every rank's buffer over NVLink and counts itself in
+ * with a system-scope atomic (bounded waits), and every rank adds the partial
+ * rows in rank order, so all ranks keep the same residual stream; the
+ * classifier rows and the greedy key reach every rank the same way.  Else
+ * (ranks sharing a GPU, more than 8 ranks, or CATS_TP_NO_P2P=1 on every rank)
+ * it runs the per-phase graph engine: after wo and after w2 an NCCL sum
+ * allreduce of dim floats, after the classifier a max allreduce of the
+ * greedy key and an allgather of the logits.  cats_gpu_llm_set_engine selects
+ * either where both are possible.  Every rank feeds the same tokens and gets
+ * the full logits.  The ranks must start each call within the exchange's
+ * bounded wait (a few seconds) of one another.  After a bounded wait expires
+ * (CATS_ERR_TIMEOUT) a sharded model's ranks are out of step: destroy and
+ * recreate them. */
 size_t cats_gpu_tp_unique_id_bytes(void);
 int cats_gpu_tp_unique_id(void *id, size_t bytes);
 int cats_gpu_llm_tp_connect(cats_gpu_llm *m, const void *id);
+/* Failure-detection check of the tensor-parallel exchange on one GPU (no
+ * counterpart in the reference, which has no multi-GPU path): instead of
+ * connecting to other ranks, map every rank's exchange buffer to this rank's
+ * own.  No other rank ever arrives, so the first step's first exchange gives
+ * up after its bounded wait (seconds) and the step returns CATS_ERR_TIMEOUT
+ * with the GPU context intact.  The model is unusable for decoding after it. */
+int cats_gpu_llm_tp_loopback(cats_gpu_llm *m);
 /* One step of the persistent engine with a phase timeline, the counterpart
  * of the reference's per-layer CATS_CHECK timings (catseye.h:2110-2117):
  * host receives [2][ctas][per_cta] stamps taken by thread 0 of each CTA:

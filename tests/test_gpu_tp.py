@@ -1,10 +1,19 @@
-"""Tensor-parallel decode over NCCL: a model sharded over 2 GPUs (one
-process per GPU) against the same seeded model on one GPU.
+"""Tensor-parallel decode: a model sharded over 2, 4 or 8 GPUs (one process
+per GPU) against the same seeded model on one GPU and against the
+reference's own step (oracle/_ref) on the same weights.
 
-Each rank quantizes the same 32-blocks the unsharded model does; only the
-allreduce's summation order differs.  Bars: fp32 logits <= 1e-4 per step and
-equal greedy tokens; Q4_0 within the Q8 flip amplitude (3e-2).  Needs two
-visible GPUs (skipped on one)."""
+Two sharded engines: the persistent kernel with the exchange over peer
+memory (partial rows of wo / w2 pushed to every rank, system-scope arrival
+counters), and the per-phase graph with NCCL allreduces.  Each rank quantizes
+the same 32-blocks the unsharded model does; only the order of the partial
+sums differs.  Bars: fp32 logits <= 1e-4 per step and equal greedy tokens;
+Q4_0 within the Q8 flip amplitude (3e-2).  Needs as many visible GPUs as
+ranks (skipped otherwise).
+
+The failure-detection check runs on one GPU: a sharded model whose peers
+never arrive (every rank's exchange buffer mapped to its own) must give up at
+its first exchange after the bounded wait and report CATS_ERR_TIMEOUT, with
+the GPU context still usable."""
 import os
 import socket
 
@@ -15,9 +24,11 @@ from models import rel
 
 pytestmark = pytest.mark.gpu
 
-CFG = dict(dim=512, hidden=1408, n_layers=2, n_heads=8, n_kv_heads=2, vocab=4096, seq_len=64)
+# GQA (16 query heads over 8 kv heads) that shards over 2, 4 and 8 ranks
+CFG = dict(dim=512, hidden=1536, n_layers=2, n_heads=16, n_kv_heads=8, vocab=4096, seq_len=64)
 FEED = [3, 17, 400, 4095, 5, 123, 77, 9]
 SEED = 31
+PERSISTENT, GRAPH = 0, 1
 
 
 def _free_port():
@@ -45,73 +56,99 @@ def _batch_run(m):
     return [row.copy() for row in lg], [int(t) for t in np.asarray(gen).reshape(-1)]
 
 
-def _rank(rank, world, port, wtype, batched, out):
+def _rank(rank, world, port, wtype, batched, engine, out):
     import torch.distributed as dist
-    from catseye_b200 import _lib, llm
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from catseye_b200 import _lib, llm
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         _lib.init(rank)
         m = llm.GpuLLM(llm.LlmConfig(**CFG, wtype=wtype), rank, world)
         m.tp_connect(llm.tp_share_id())
+        p2p = m.tp_persistent()          # the peers were mapped (every rank on its own GPU)
+        m.set_engine(engine)
         m.init_random(SEED)
+        dist.barrier()   # the ranks start their first step together (the exchange waits are bounded)
         logits, toks = (_batch_run if batched else _decode_run)(m)
         m.close()
-        out.put((rank, logits, toks))
+        out.put((rank, logits, toks, p2p))
     except Exception as e:   # reported to the parent, which fails the test
-        out.put((rank, repr(e), None))
+        out.put((rank, repr(e), None, None))
     finally:
         dist.destroy_process_group()
 
 
-def _sharded(wtype, world=2, batched=False):
+def _sharded(wtype, world=2, batched=False, engine=PERSISTENT):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, wtype, batched, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, wtype, batched, engine, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     for _ in procs:
-        r, logits, toks = q.get(timeout=600)
-        res[r] = (logits, toks)
+        r, logits, toks, p2p = q.get(timeout=600)
+        res[r] = (logits, toks, p2p)
     for p in procs:
         p.join(timeout=120)
-    for r, (logits, toks) in res.items():
+    for r, (logits, toks, _) in res.items():
         assert toks is not None, (r, logits)
     return res
 
 
-@pytest.fixture(scope="module")
-def two_gpus(gpu):
+def _need(world):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("tensor parallel needs two visible GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"tensor parallel over {world} ranks needs {world} visible GPUs")
 
 
-@pytest.mark.parametrize("wtype,tol", [(0, 1e-4), (2, 3e-2)])
-def test_two_rank_decode_matches_one_gpu(two_gpus, wtype, tol):
+@pytest.fixture(scope="module")
+def one_gpu_runs(gpu):
+    """The unsharded model's runs, and the reference's logits on the same weights."""
     from catseye_b200 import llm
-    one = llm.GpuLLM(llm.LlmConfig(**CFG, wtype=wtype))
-    one.set_engine(llm.ENGINE_GRAPH)
-    one.init_random(SEED)
-    ref, ref_toks = _decode_run(one)
-    one.close()
-    res = _sharded(wtype)
-    for r, (logits, toks) in res.items():
+    from oracle.cpu import Oracle, Reference, ref_available
+    from test_gpu_llm import _synth_weights
+    out = {}
+    for wtype in (0, 2):
+        cfg = llm.LlmConfig(**CFG, wtype=wtype)
+        one = llm.GpuLLM(cfg)
+        one.init_random(SEED)
+        out[wtype] = _decode_run(one)
+        one.close()
+        w = _synth_weights(llm, cfg, SEED)
+        r = Reference("llm").llm(w) if ref_available("llm") else Oracle().llm(w)
+        out[("ref", wtype)] = [r.step(t, p) for p, t in enumerate(FEED)]
+    return out
+
+
+@pytest.mark.parametrize("engine", [PERSISTENT, GRAPH])
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("wtype,tol", [(0, 1e-4), (2, 3e-2)])
+def test_sharded_decode_matches_one_gpu_and_reference(one_gpu_runs, world, engine, wtype, tol):
+    _need(world)
+    ref, ref_toks = one_gpu_runs[wtype]
+    want = one_gpu_runs[("ref", wtype)]
+    res = _sharded(wtype, world, engine=engine)
+    for r, (logits, toks, p2p) in res.items():
+        assert p2p, "peers not mapped although every rank has its own GPU"
         errs = [rel(a, b) for a, b in zip(logits, ref)]
+        errs_ref = [rel(a, b) for a, b in zip(logits, want)]
         assert max(errs) < tol, (r, errs)
+        assert max(errs_ref) < tol, (r, errs_ref)
         if wtype == 0:
             assert [int(np.argmax(a)) for a in logits] == [int(np.argmax(b)) for b in ref]
+            assert [int(np.argmax(a)) for a in logits] == [int(np.argmax(b)) for b in want]
             assert toks == ref_toks, r
     # every rank holds the full logits and decodes the same tokens
-    assert res[0][1] == res[1][1]
-    assert all(np.array_equal(a, b) for a, b in zip(res[0][0], res[1][0]))
+    for r in range(1, world):
+        assert res[0][1] == res[r][1]
+        assert all(np.array_equal(a, b) for a, b in zip(res[0][0], res[r][0])), r
 
 
-def test_two_rank_batched_step_matches_one_gpu(two_gpus):
+def test_two_rank_batched_step_matches_one_gpu(gpu):
     """The batched step sharded over 2 GPUs (wo/w2 partial products
     sum-allreduced, classifier slices allgathered) against the same model on
     one GPU.  Only fp32 summation orders differ, but a residual that differs
@@ -119,15 +156,38 @@ def test_two_rank_batched_step_matches_one_gpu(two_gpus):
     the next product's operand, so the logits carry that flip (measured
     <= 2.1e-4; bar 1e-3, half the batched step's bar against the oracle) and
     the greedy tokens of both sequences are equal."""
+    _need(2)
     from catseye_b200 import llm
     one = llm.GpuLLM(llm.LlmConfig(**CFG, wtype=2))
     one.init_random(SEED)
     ref, ref_toks = _batch_run(one)
     one.close()
     res = _sharded(2, batched=True)
-    for r, (logits, toks) in res.items():
+    for r, (logits, toks, _) in res.items():
         errs = [rel(a, b) for a, b in zip(logits, ref)]
         print("rank", r, "logit errors", ["%.1e" % e for e in errs], "tokens", toks, "one GPU", ref_toks)
         assert max(errs) < 1e-3, (r, errs)
         assert toks == ref_toks, r
     assert res[0][1] == res[1][1]
+
+
+def test_exchange_wait_gives_up_when_peers_never_arrive(gpu):
+    """One GPU, a 2-rank model whose second rank does not exist: the step's
+    first exchange waits (bounded) for arrivals that never come, then the
+    kernel sets its error word and returns; the host raises CATS_ERR_TIMEOUT.
+    The context stays usable: an unsharded model decodes afterwards."""
+    from catseye_b200 import _lib, llm
+    cfg = llm.LlmConfig(**CFG, wtype=2)
+    m = llm.GpuLLM(cfg, 0, 2)
+    m.init_random(SEED)
+    m.tp_loopback()
+    with pytest.raises(_lib.CatsGpuError):
+        m.step(3, 0)
+    assert m.lib.cats_gpu_last_error() == 4   # CATS_ERR_TIMEOUT
+    m.lib.cats_gpu_clear_error()
+    m.close()
+    one = llm.GpuLLM(cfg)
+    one.init_random(SEED)
+    lg = one.step(3, 0)
+    assert np.isfinite(lg).all()
+    one.close()

@@ -89,6 +89,16 @@ SIGNATURES = {
     "cats_conv2d_forward_dev": (_i, [_vp, _vp, _vp] + [_i] * 8 + [_vp]),
     "cats_linear_forward": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "cats_linear_forward_dev": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "cats_col2im": (None, [_vp] + [_i] * 9 + [_vp]),
+    "cats_col2im_dev": (_i, [_vp] + [_i] * 9 + [_vp, _vp]),
+    "cats_conv2d_backward": (None, [_vp, _vp, _vp] + [_i] * 8),
+    "cats_conv2d_backward_dev": (_i, [_vp, _vp, _vp] + [_i] * 8 + [_vp]),
+    "cats_conv2d_update": (None, [_vp, _vp, _vp] + [_i] * 8),
+    "cats_conv2d_update_dev": (_i, [_vp, _vp, _vp] + [_i] * 8 + [_vp]),
+    "cats_linear_backward": (None, [_vp, _vp, _vp, _i, _i, _i]),
+    "cats_linear_backward_dev": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "cats_linear_update": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _f]),
+    "cats_linear_update_dev": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp]),
 }
 
 _LIB = None

@@ -45,6 +45,10 @@ struct Ctx {
     size_t cap_x16 = 0;
     float *d_ws = nullptr;     // its K-split partials
     size_t cap_ws = 0;
+    // CNN training: the batched column matrix, the channel-major gradients,
+    // and a fourth host-copy staging buffer
+    float *d_col = nullptr, *d_tr = nullptr, *d_d = nullptr;
+    size_t cap_col = 0, cap_tr = 0, cap_d = 0;
 };
 
 Ctx g;
@@ -224,12 +228,14 @@ void cats_gpu_term(void)
     cudaStreamSynchronize(g.stream);
     for (auto &kv : g.weights) if (kv.second.W.ptr) cudaFree(kv.second.W.ptr);
     g.weights.clear();
-    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err, g.d_x16, g.d_ws};
+    void *bufs[] = {g.d_x, g.d_out, g.d_a, g.d_b, g.d_c, g.d_work, g.d_err, g.d_x16, g.d_ws, g.d_col, g.d_tr, g.d_d};
     for (void *b : bufs) if (b) cudaFree(b);
     g.d_x = nullptr; g.d_out = nullptr; g.d_a = g.d_b = g.d_c = g.d_work = nullptr; g.d_err = nullptr;
     g.d_x16 = nullptr;
     g.d_ws = nullptr;
+    g.d_col = g.d_tr = g.d_d = nullptr;
     g.d_x_cap = g.d_out_cap = g.cap_a = g.cap_b = g.cap_c = g.cap_work = g.cap_x16 = g.cap_ws = 0;
+    g.cap_col = g.cap_tr = g.cap_d = 0;
     cudaStreamDestroy(g.stream);
     g.stream = nullptr;
     g.init = false;
@@ -957,6 +963,184 @@ void cats_linear_forward(const float *x, const float *w, float *z, int batch, in
     if (check(cudaMemcpyAsync(g.d_b, w, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
     if (cats_linear_forward_dev(g.d_a, g.d_b, g.d_c, batch, in, out, g.stream)) return;
     if (check(cudaMemcpyAsync(z, g.d_c, zb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+// ------------------------------------------------------------- CNN training
+int cats_col2im_dev(const float *col, int channels, int height, int width, int kh, int kw, int ph, int pw, int sh,
+                    int sw, float *im, void *stream)
+{
+    const char *what = "cats_col2im_dev";
+    if (!ensure_init()) return g.last_err;
+    if (!im || !col || !conv_geom_ok(channels, height, width, kh, kw, ph, pw, sh, sw)) return fail(CATS_ERR_ARG, what);
+    const long long P = (long long)conv_out(height, kh, ph, sh) * conv_out(width, kw, pw, sw);
+    return check(launch_col2im(col, P, 1, channels, height, width, kh, kw, ph, pw, sh, sw, im,
+                               stream ? (cudaStream_t)stream : g.stream),
+                 what);
+}
+
+void cats_col2im(const float *col, int channels, int height, int width, int kh, int kw, int ph, int pw, int sh,
+                 int sw, float *im)
+{
+    const char *what = "cats_col2im";
+    if (!ensure_init()) return;
+    if (!im || !col || !conv_geom_ok(channels, height, width, kh, kw, ph, pw, sh, sw)) { fail(CATS_ERR_ARG, what); return; }
+    const size_t ib = (size_t)channels * height * width * 4;
+    const size_t cb = (size_t)channels * kh * kw * conv_out(height, kh, ph, sh) * conv_out(width, kw, pw, sw) * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, cb) || grow((void **)&g.d_c, &g.cap_c, ib)) return;
+    if (check(cudaMemcpyAsync(g.d_a, col, cb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_col2im_dev(g.d_a, channels, height, width, kh, kw, ph, pw, sh, sw, g.d_c, g.stream)) return;
+    if (check(cudaMemcpyAsync(im, g.d_c, ib, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+// The sizes of a convolution layer's batch: K = ich*k*k, P = oh*ow, N = batch*P.
+static bool conv_sizes(int batch, int ich, int h, int wd, int ch, int ksize, int pad, int stride, long long *K,
+                       long long *P, long long *N)
+{
+    if (batch <= 0 || ch <= 0 || !conv_geom_ok(ich, h, wd, ksize, ksize, pad, pad, stride, stride)) return false;
+    *K = (long long)ich * ksize * ksize;
+    *P = (long long)conv_out(h, ksize, pad, stride) * conv_out(wd, ksize, pad, stride);
+    *N = *P * batch;
+    // the GEMMs take int sizes
+    return *K < (1LL << 31) && *N < (1LL << 31) && *K * *N < (1LL << 40);
+}
+
+int cats_conv2d_backward_dev(const float *dout, const float *w, float *din, int batch, int ich, int h, int wd, int ch,
+                             int ksize, int pad, int stride, void *stream)
+{
+    const char *what = "cats_conv2d_backward_dev";
+    if (!ensure_init()) return g.last_err;
+    long long K, P, N;
+    if (!dout || !w || !din || !conv_sizes(batch, ich, h, wd, ch, ksize, pad, stride, &K, &P, &N))
+        return fail(CATS_ERR_ARG, what);
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    if (grow((void **)&g.d_tr, &g.cap_tr, (size_t)ch * N * 4) || grow((void **)&g.d_col, &g.cap_col, (size_t)K * N * 4))
+        return g.last_err;
+    // dOut as one [ch][batch*P] operand, then col[k][b*P + p] = sum_c w[c][k] dOut[b][c][p]
+    // (every sample's gemm_rtn at once), then col2im of every sample
+    if (check(launch_batch_to_channel_major(dout, batch, ch, (int)P, g.d_tr, st), what)) return g.last_err;
+    if (int rc = cats_sgemm_dev('T', 'N', (int)K, (int)N, ch, 1.f, w, (int)K, g.d_tr, (int)N, 0.f, g.d_col, (int)N, st))
+        return rc;
+    return check(launch_col2im(g.d_col, N, batch, ich, h, wd, ksize, ksize, pad, pad, stride, stride, din, st), what);
+}
+
+void cats_conv2d_backward(const float *dout, const float *w, float *din, int batch, int ich, int h, int wd, int ch,
+                          int ksize, int pad, int stride)
+{
+    const char *what = "cats_conv2d_backward";
+    if (!ensure_init()) return;
+    long long K, P, N;
+    if (!dout || !w || !din || !conv_sizes(batch, ich, h, wd, ch, ksize, pad, stride, &K, &P, &N)) {
+        fail(CATS_ERR_ARG, what);
+        return;
+    }
+    const size_t ob = (size_t)ch * N * 4, wb = (size_t)ch * K * 4, ib = (size_t)batch * ich * h * wd * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, ob) || grow((void **)&g.d_b, &g.cap_b, wb) || grow((void **)&g.d_c, &g.cap_c, ib))
+        return;
+    if (check(cudaMemcpyAsync(g.d_a, dout, ob, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_b, w, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_conv2d_backward_dev(g.d_a, g.d_b, g.d_c, batch, ich, h, wd, ch, ksize, pad, stride, g.stream)) return;
+    if (check(cudaMemcpyAsync(din, g.d_c, ib, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+int cats_conv2d_update_dev(const float *dout, const float *x, float *dw, int batch, int ich, int h, int wd, int ch,
+                           int ksize, int pad, int stride, void *stream)
+{
+    const char *what = "cats_conv2d_update_dev";
+    if (!ensure_init()) return g.last_err;
+    long long K, P, N;
+    if (!dout || !x || !dw || !conv_sizes(batch, ich, h, wd, ch, ksize, pad, stride, &K, &P, &N))
+        return fail(CATS_ERR_ARG, what);
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    if (grow((void **)&g.d_tr, &g.cap_tr, (size_t)ch * N * 4) || grow((void **)&g.d_col, &g.cap_col, (size_t)K * N * 4))
+        return g.last_err;
+    // dw[c][k] += (1/batch) * sum over every sample's pixels of dOut[b][c][p] im2col(x[b])[k][p]:
+    // the per-sample gemm_rnt calls with alpha = 1/batch (catseye.h:622-640) as one GEMM
+    if (check(launch_batch_to_channel_major(dout, batch, ch, (int)P, g.d_tr, st), what)) return g.last_err;
+    if (check(launch_im2col_cols(x, batch, ich, h, wd, ksize, ksize, pad, pad, stride, stride, g.d_col, st), what))
+        return g.last_err;
+    const float alpha = (float)(1.0 / batch);   // the reference's real alpha = 1.0/l->p->batch
+    return cats_sgemm_dev('N', 'T', ch, (int)K, (int)N, alpha, g.d_tr, (int)N, g.d_col, (int)N, 1.f, dw, (int)K, st);
+}
+
+void cats_conv2d_update(const float *dout, const float *x, float *dw, int batch, int ich, int h, int wd, int ch,
+                        int ksize, int pad, int stride)
+{
+    const char *what = "cats_conv2d_update";
+    if (!ensure_init()) return;
+    long long K, P, N;
+    if (!dout || !x || !dw || !conv_sizes(batch, ich, h, wd, ch, ksize, pad, stride, &K, &P, &N)) {
+        fail(CATS_ERR_ARG, what);
+        return;
+    }
+    const size_t ob = (size_t)ch * N * 4, xb = (size_t)batch * ich * h * wd * 4, wb = (size_t)ch * K * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, ob) || grow((void **)&g.d_b, &g.cap_b, xb) || grow((void **)&g.d_c, &g.cap_c, wb))
+        return;
+    if (check(cudaMemcpyAsync(g.d_a, dout, ob, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_b, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_c, dw, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_conv2d_update_dev(g.d_a, g.d_b, g.d_c, batch, ich, h, wd, ch, ksize, pad, stride, g.stream)) return;
+    if (check(cudaMemcpyAsync(dw, g.d_c, wb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+int cats_linear_backward_dev(const float *dout, const float *w, float *din, int batch, int in, int out, void *stream)
+{
+    const char *what = "cats_linear_backward_dev";
+    if (!ensure_init()) return g.last_err;
+    if (!dout || !w || !din || batch <= 0 || in <= 0 || out <= 0) return fail(CATS_ERR_ARG, what);
+    // dIn = dOut * W (gemm_rnn(batch, in, out), catseye.h:466)
+    return cats_sgemm_dev('N', 'N', batch, in, out, 1.f, dout, out, w, in, 0.f, din, in,
+                          stream ? (cudaStream_t)stream : g.stream);
+}
+
+void cats_linear_backward(const float *dout, const float *w, float *din, int batch, int in, int out)
+{
+    const char *what = "cats_linear_backward";
+    if (!ensure_init()) return;
+    if (!dout || !w || !din || batch <= 0 || in <= 0 || out <= 0) { fail(CATS_ERR_ARG, what); return; }
+    const size_t ob = (size_t)batch * out * 4, wb = (size_t)in * out * 4, ib = (size_t)batch * in * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, ob) || grow((void **)&g.d_b, &g.cap_b, wb) || grow((void **)&g.d_c, &g.cap_c, ib))
+        return;
+    if (check(cudaMemcpyAsync(g.d_a, dout, ob, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_b, w, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_linear_backward_dev(g.d_a, g.d_b, g.d_c, batch, in, out, g.stream)) return;
+    if (check(cudaMemcpyAsync(din, g.d_c, ib, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    check(cudaStreamSynchronize(g.stream), what);
+}
+
+int cats_linear_update_dev(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out,
+                           float eta, void *stream)
+{
+    const char *what = "cats_linear_update_dev";
+    if (!ensure_init()) return g.last_err;
+    if (!dout || !x || !w || !dw || batch <= 0 || in <= 0 || out <= 0) return fail(CATS_ERR_ARG, what);
+    cudaStream_t st = stream ? (cudaStream_t)stream : g.stream;
+    // dw += dOut^T x (gemm_rtn(out, in, batch, 1, dOut, x, 1, dw), catseye.h:490)
+    if (int rc = cats_sgemm_dev('T', 'N', out, in, batch, 1.f, dout, out, x, in, 1.f, dw, in, st)) return rc;
+    // the bias after the weights: w[in*out + o] -= eta * dOut[b][o], sample after sample (:494-496)
+    return check(launch_bias_update(w + (size_t)in * out, dout, batch, out, eta, st), what);
+}
+
+void cats_linear_update(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out, float eta)
+{
+    const char *what = "cats_linear_update";
+    if (!ensure_init()) return;
+    if (!dout || !x || !w || !dw || batch <= 0 || in <= 0 || out <= 0) { fail(CATS_ERR_ARG, what); return; }
+    const size_t ob = (size_t)batch * out * 4, xb = (size_t)batch * in * 4, wb = ((size_t)in * out + out) * 4,
+                 db = (size_t)in * out * 4;
+    if (grow((void **)&g.d_a, &g.cap_a, ob) || grow((void **)&g.d_b, &g.cap_b, xb) ||
+        grow((void **)&g.d_c, &g.cap_c, wb) || grow((void **)&g.d_d, &g.cap_d, db))
+        return;
+    if (check(cudaMemcpyAsync(g.d_a, dout, ob, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_b, x, xb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_c, w, wb, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(g.d_d, dw, db, cudaMemcpyHostToDevice, g.stream), what)) return;
+    if (cats_linear_update_dev(g.d_a, g.d_b, g.d_c, g.d_d, batch, in, out, eta, g.stream)) return;
+    if (check(cudaMemcpyAsync(w, g.d_c, wb, cudaMemcpyDeviceToHost, g.stream), what)) return;
+    if (check(cudaMemcpyAsync(dw, g.d_d, db, cudaMemcpyDeviceToHost, g.stream), what)) return;
     check(cudaStreamSynchronize(g.stream), what);
 }
 

@@ -204,4 +204,128 @@ cudaError_t launch_bias_rows(const float *bias, float *z, int batch, int out, cu
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------- training
+// col2im as a gather: each image element sums the column entries that cover
+// it, in the order the reference's scatter adds them (column row k =
+// (c*kh + i)*kw + j ascending, catseye.h:533-556), starting from zero as its
+// memset does, so the sums are the reference's bit for bit.  No atomics: the
+// result does not depend on scheduling.  Columns of sample b start at b*P
+// of each column row (row length col_ld): the batched layout [k][b][P].
+__global__ void k_col2im(const float *__restrict__ col, long long col_ld, int batch, int channels, int height,
+                         int width, int kh, int kw, int ph, int pw, int sh, int sw, int hc, int wc,
+                         float *__restrict__ im)
+{
+    const long long total = (long long)batch * channels * height * width;
+    const int P = hc * wc;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int x = (int)(idx % width);
+        long long r = idx / width;
+        const int y = (int)(r % height);
+        r /= height;
+        const int c = (int)(r % channels);
+        const int b = (int)(r / channels);
+        const float *cb = col + (long long)b * P;
+        float sum = 0.f;
+        for (int i = 0; i < kh; i++) {
+            const int ty = y + ph - i;
+            if (ty < 0 || ty % sh) continue;
+            const int oy = ty / sh;
+            if (oy >= hc) continue;
+            for (int j = 0; j < kw; j++) {
+                const int tx = x + pw - j;
+                if (tx < 0 || tx % sw) continue;
+                const int ox = tx / sw;
+                if (ox >= wc) continue;
+                sum += cb[(long long)((c * kh + i) * kw + j) * col_ld + oy * wc + ox];
+            }
+        }
+        im[idx] = sum;
+    }
+}
+
+cudaError_t launch_col2im(const float *col, long long col_ld, int batch, int channels, int height, int width, int kh,
+                          int kw, int ph, int pw, int sh, int sw, float *im, cudaStream_t st)
+{
+    const int hc = conv_out(height, kh, ph, sh), wc = conv_out(width, kw, pw, sw);
+    const long long total = (long long)batch * channels * height * width;
+    if (total <= 0) return cudaSuccess;
+    const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    k_col2im<<<grid, 256, 0, st>>>(col, col_ld, batch, channels, height, width, kh, kw, ph, pw, sh, sw, hc, wc, im);
+    return cudaGetLastError();
+}
+
+// im2col of a batch into the columns [k][b*P + p] (catseye.h:508-532 per sample)
+__global__ void k_im2col_cols(const float *__restrict__ x, int batch, int channels, int height, int width, int kh,
+                              int kw, int ph, int pw, int sh, int sw, int hc, int wc, float *__restrict__ col)
+{
+    const int P = hc * wc;
+    const long long N = (long long)batch * P;
+    const long long total = (long long)channels * kh * kw * N;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long n = idx % N;
+        const int k = (int)(idx / N);
+        const int b = (int)(n / P), p = (int)(n % P);
+        const int ox = p % wc, oy = p / wc;
+        const int j = k % kw, i = (k / kw) % kh, c = k / kh / kw;
+        const int yp = oy * sh - ph + i, xp = ox * sw - pw + j;
+        col[idx] = (yp >= 0 && yp < height && xp >= 0 && xp < width)
+                       ? x[(((size_t)b * channels + c) * height + yp) * width + xp]
+                       : 0.f;
+    }
+}
+
+cudaError_t launch_im2col_cols(const float *x, int batch, int channels, int height, int width, int kh, int kw, int ph,
+                               int pw, int sh, int sw, float *col, cudaStream_t st)
+{
+    const int hc = conv_out(height, kh, ph, sh), wc = conv_out(width, kw, pw, sw);
+    const long long total = (long long)channels * kh * kw * batch * hc * wc;
+    if (total <= 0) return cudaSuccess;
+    const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    k_im2col_cols<<<grid, 256, 0, st>>>(x, batch, channels, height, width, kh, kw, ph, pw, sh, sw, hc, wc, col);
+    return cudaGetLastError();
+}
+
+// dst[c][b][p] = src[b][c][p]: the per-sample CHW gradients as one [ch][batch*P] operand
+__global__ void k_batch_to_channel_major(const float *__restrict__ src, int batch, int ch, int P,
+                                         float *__restrict__ dst)
+{
+    const long long total = (long long)batch * ch * P;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int p = (int)(idx % P);
+        const long long r = idx / P;
+        const int b = (int)(r % batch), c = (int)(r / batch);
+        dst[idx] = src[((size_t)b * ch + c) * P + p];
+    }
+}
+
+cudaError_t launch_batch_to_channel_major(const float *src, int batch, int ch, int P, float *dst, cudaStream_t st)
+{
+    const long long total = (long long)batch * ch * P;
+    if (total <= 0) return cudaSuccess;
+    const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    k_batch_to_channel_major<<<grid, 256, 0, st>>>(src, batch, ch, P, dst);
+    return cudaGetLastError();
+}
+
+// bias[o] -= eta * dout[b][o] for b = 0, 1, ... in order (catseye.h:494-496)
+__global__ void k_bias_update(float *__restrict__ bias, const float *__restrict__ dout, int batch, int out, float eta)
+{
+    for (int o = blockIdx.x * blockDim.x + threadIdx.x; o < out; o += gridDim.x * blockDim.x) {
+        float v = bias[o];
+        for (int b = 0; b < batch; b++) v -= eta * dout[(size_t)b * out + o];
+        bias[o] = v;
+    }
+}
+
+cudaError_t launch_bias_update(float *bias, const float *dout, int batch, int out, float eta, cudaStream_t st)
+{
+    if (out <= 0 || batch <= 0) return cudaSuccess;
+    const int grid = std::min(cdiv(out, 256), 148 * 4);
+    k_bias_update<<<grid, 256, 0, st>>>(bias, dout, batch, out, eta);
+    return cudaGetLastError();
+}
+
 } // namespace cats

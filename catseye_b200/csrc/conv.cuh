@@ -31,4 +31,18 @@ cudaError_t launch_conv_tc(const float *x, const float *w, float *z, int batch, 
 // z[b][o] = w[in*out + o] (the bias the linear forward adds, catseye.h:416-444).
 cudaError_t launch_bias_rows(const float *bias, float *z, int batch, int out, cudaStream_t st);
 
+// ---- training (the GEMMs themselves run through launch_sgemm)
+// col2im (catseye.h:533-556) of `batch` images whose columns are [k][b*P + p]
+// with rows col_ld floats apart (one image: batch 1, col_ld = P); a gather in
+// the reference's summation order, so bit-exact.
+cudaError_t launch_col2im(const float *col, long long col_ld, int batch, int channels, int height, int width, int kh,
+                          int kw, int ph, int pw, int sh, int sw, float *im, cudaStream_t st);
+// im2col (catseye.h:508-532) of x[b][c][h][w] for every sample, into col[k][b*P + p]
+cudaError_t launch_im2col_cols(const float *x, int batch, int channels, int height, int width, int kh, int kw, int ph,
+                               int pw, int sh, int sw, float *col, cudaStream_t st);
+// dst[c][b][p] = src[b][c][p]
+cudaError_t launch_batch_to_channel_major(const float *src, int batch, int ch, int P, float *dst, cudaStream_t st);
+// bias[o] -= eta * dout[b][o], b in order (CatsEye_linear_update's bias step, catseye.h:494-496)
+cudaError_t launch_bias_update(float *bias, const float *dout, int batch, int out, float eta, cudaStream_t st);
+
 } // namespace cats

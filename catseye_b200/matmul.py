@@ -172,6 +172,67 @@ def linear_forward_dev(x, w, z, batch, n_in, n_out, stream=None):
     return z
 
 
+# ------------------------------------------------------------ CNN training
+def col2im(col, channels, height, width, kh, kw, ph, pw, sh, sw):
+    """col2im (catseye.h:533-556) of one image's columns -> im[c][h][w]."""
+    lib = _lib.init()
+    im = np.empty(channels * height * width, np.float32)
+    _lib.call_void(lib.cats_col2im, _p(np.ascontiguousarray(col, np.float32)), channels, height, width, kh, kw,
+                   ph, pw, sh, sw, _p(im), what="cats_col2im")
+    return im
+
+
+def conv2d_backward(dout, w, batch, ich, h, wd, ch, ksize, pad, stride):
+    """CatsEye_convolutional_backward for a batch -> dIn[b][ich][h][wd]."""
+    lib = _lib.init()
+    din = np.empty(batch * ich * h * wd, np.float32)
+    _lib.call_void(lib.cats_conv2d_backward, _p(np.ascontiguousarray(dout, np.float32)),
+                   _p(np.ascontiguousarray(w, np.float32)), _p(din), batch, ich, h, wd, ch, ksize, pad, stride,
+                   what="cats_conv2d_backward")
+    return din
+
+
+def conv2d_update(dout, x, dw, batch, ich, h, wd, ch, ksize, pad, stride):
+    """CatsEye_convolutional_update for a batch: dw (updated in place and returned)."""
+    lib = _lib.init()
+    _lib.call_void(lib.cats_conv2d_update, _p(np.ascontiguousarray(dout, np.float32)),
+                   _p(np.ascontiguousarray(x, np.float32)), _p(dw), batch, ich, h, wd, ch, ksize, pad, stride,
+                   what="cats_conv2d_update")
+    return dw
+
+
+def linear_backward(dout, w, batch, n_in, n_out):
+    """CatsEye_linear_backward -> dIn[b][in]."""
+    lib = _lib.init()
+    din = np.empty(batch * n_in, np.float32)
+    _lib.call_void(lib.cats_linear_backward, _p(np.ascontiguousarray(dout, np.float32)),
+                   _p(np.ascontiguousarray(w, np.float32)), _p(din), batch, n_in, n_out, what="cats_linear_backward")
+    return din
+
+
+def linear_update(dout, x, w, dw, batch, n_in, n_out, eta):
+    """CatsEye_linear_update: dw += dOut^T x, biases in w -= eta * dOut (w, dw updated in place)."""
+    lib = _lib.init()
+    _lib.call_void(lib.cats_linear_update, _p(np.ascontiguousarray(dout, np.float32)),
+                   _p(np.ascontiguousarray(x, np.float32)), _p(w), _p(dw), batch, n_in, n_out, float(eta),
+                   what="cats_linear_update")
+    return w, dw
+
+
+def conv2d_backward_dev(dout, w, din, batch, ich, h, wd, ch, ksize, pad, stride, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_conv2d_backward_dev(_dp(dout), _dp(w), _dp(din), batch, ich, h, wd, ch, ksize, pad, stride,
+                                            stream), "cats_conv2d_backward_dev")
+    return din
+
+
+def conv2d_update_dev(dout, x, dw, batch, ich, h, wd, ch, ksize, pad, stride, stream=None):
+    lib = _lib.init()
+    _lib.check(lib.cats_conv2d_update_dev(_dp(dout), _dp(x), _dp(dw), batch, ich, h, wd, ch, ksize, pad, stride,
+                                          stream), "cats_conv2d_update_dev")
+    return dw
+
+
 # ------------------------------------------------ batched product (tensor cores)
 def qgemm(w, x, T, n, d):
     """y[T][d] = x[T][n] * W^T for a registered Q4_0/Q8_0 weight w (host arrays)."""

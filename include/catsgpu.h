@@ -329,6 +329,45 @@ int cats_conv2d_forward_dev(const float *x, const float *w, float *z, int batch,
 void cats_linear_forward(const float *x, const float *w, float *z, int batch, int in, int out);
 int cats_linear_forward_dev(const float *x, const float *w, float *z, int batch, int in, int out, void *stream);
 
+/* ---- CNN training callers of the GEMM ---------------------------------------
+ * Replace col2im (catseye.h:533-556), CatsEye_convolutional_backward
+ * (catseye.h:589-620), CatsEye_convolutional_update (:622-640),
+ * CatsEye_linear_backward (:445-477) and CatsEye_linear_update (:478-505) for a
+ * whole batch, in the layouts the reference's layers keep: x, dIn
+ * [batch][ich][h][wd]; dOut [batch][ch][oh*ow] (convolution) or
+ * [batch][out] (linear); w [ch][ich*k*k] or [out][in] then the out biases.
+ * Plain forms take host pointers (copied in and out); _dev forms take device
+ * pointers and enqueue on `stream` (NULL: the library's stream). */
+
+/* im[c][y][x] = sum of the col entries covering it, in the reference's order
+ * (the inverse gather of cats_im2col; bit-exact). */
+void cats_col2im(const float *col, int channels, int height, int width, int kh, int kw, int ph, int pw, int sh,
+                 int sw, float *im);
+int cats_col2im_dev(const float *col, int channels, int height, int width, int kh, int kw, int ph, int pw, int sh,
+                    int sw, float *im, void *stream);
+/* dIn[b] = col2im(W^T dOut[b]) for every sample: one GEMM over the batch, then
+ * col2im.  (For ksize 1 the reference skips col2im, which equals this only for
+ * pad 0 and stride 1, the only 1x1 form its layers build.) */
+void cats_conv2d_backward(const float *dout, const float *w, float *din, int batch, int ich, int h, int wd, int ch,
+                          int ksize, int pad, int stride);
+int cats_conv2d_backward_dev(const float *dout, const float *w, float *din, int batch, int ich, int h, int wd, int ch,
+                             int ksize, int pad, int stride, void *stream);
+/* dw[c][k] += (1/batch) * sum_b sum_p dOut[b][c][p] * im2col(x[b])[k][p] (the
+ * reference's per-sample gemm_rnt with alpha = 1/batch, beta = 1, as one GEMM
+ * whose K runs over the whole batch's pixels). */
+void cats_conv2d_update(const float *dout, const float *x, float *dw, int batch, int ich, int h, int wd, int ch,
+                        int ksize, int pad, int stride);
+int cats_conv2d_update_dev(const float *dout, const float *x, float *dw, int batch, int ich, int h, int wd, int ch,
+                           int ksize, int pad, int stride, void *stream);
+/* dIn[b][i] = sum_o dOut[b][o] * w[o][i] (gemm_rnn(batch, in, out)). */
+void cats_linear_backward(const float *dout, const float *w, float *din, int batch, int in, int out);
+int cats_linear_backward_dev(const float *dout, const float *w, float *din, int batch, int in, int out, void *stream);
+/* dw[o][i] += sum_b dOut[b][o] * x[b][i] (gemm_rtn(out, in, batch), beta = 1);
+ * then the biases w[in*out + o] -= eta * dOut[b][o], sample after sample. */
+void cats_linear_update(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out, float eta);
+int cats_linear_update_dev(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out,
+                           float eta, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

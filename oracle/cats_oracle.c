@@ -479,6 +479,74 @@ void oracle_linear_forward(const float *x, const float *w, float *z, int batch, 
         for (int i = 0; i < out; i++) z[(size_t)b * out + i] += w[(size_t)in * out + i];
 }
 
+/* col2im (catseye.h:533-556): scatter-add of every column entry into the
+ * image, in column-row order, from a zeroed image. */
+void oracle_col2im(const float *col, int channels, int height, int width, int kh, int kw,
+                   int ph, int pw, int sh, int sw, float *im)
+{
+    int hc = (height + 2 * ph - kh) / sh + 1, wc = (width + 2 * pw - kw) / sw + 1;
+    int cc = channels * kh * kw;
+    memset(im, 0, sizeof(float) * (size_t)channels * height * width);
+    for (int c = 0; c < cc; c++) {
+        int wo = c % kw, ho = (c / kw) % kh, ci = c / kh / kw;
+        for (int h = 0; h < hc; h++)
+            for (int w = 0; w < wc; w++) {
+                int hp = h * sh - ph + ho, wp = w * sw - pw + wo;
+                if (hp >= 0 && hp < height && wp >= 0 && wp < width)
+                    im[((size_t)ci * height + hp) * width + wp] += col[((size_t)c * hc + h) * wc + w];
+            }
+    }
+}
+
+/* CatsEye_convolutional_backward (catseye.h:589-620), per sample:
+ * col = W^T dOut (gemm_rtn), dIn = col2im(col); ksize 1 writes W^T dOut. */
+void oracle_conv2d_backward(const float *dout, const float *w, float *din, int batch, int ich,
+                            int h, int wd, int ch, int k, int pad, int stride)
+{
+    int oh = (h + 2 * pad - k) / stride + 1, ow = (wd + 2 * pad - k) / stride + 1;
+    size_t K = (size_t)ich * k * k, Nn = (size_t)oh * ow;
+    float *col = (float *)malloc(K * Nn * sizeof(float));
+    for (int i = 0; i < batch; i++) {
+        float *di = din + (size_t)i * ich * h * wd;
+        float *ws = k != 1 ? col : di;
+        oracle_sgemm('T', 'N', (int)K, (int)Nn, ch, 1.f, w, dout + (size_t)i * ch * Nn, 0.f, ws);
+        if (k != 1) oracle_col2im(col, ich, h, wd, k, k, pad, pad, stride, stride, di);
+    }
+    free(col);
+}
+
+/* CatsEye_convolutional_update (catseye.h:622-640), per sample:
+ * dw += (1/batch) dOut im2col(x)^T (gemm_rnt, beta 1). */
+void oracle_conv2d_update(const float *dout, const float *x, float *dw, int batch, int ich,
+                          int h, int wd, int ch, int k, int pad, int stride)
+{
+    int oh = (h + 2 * pad - k) / stride + 1, ow = (wd + 2 * pad - k) / stride + 1;
+    size_t K = (size_t)ich * k * k, Nn = (size_t)oh * ow;
+    float *col = (float *)malloc(K * Nn * sizeof(float));
+    const float alpha = (float)(1.0 / batch);
+    for (int i = 0; i < batch; i++) {
+        oracle_im2col(x + (size_t)i * ich * h * wd, ich, h, wd, k, k, pad, pad, stride, stride, col);
+        oracle_sgemm('N', 'T', ch, (int)K, (int)Nn, alpha, dout + (size_t)i * ch * Nn, col, 1.f, dw);
+    }
+    free(col);
+}
+
+/* CatsEye_linear_backward (catseye.h:445-477): dIn = dOut W (gemm_rnn). */
+void oracle_linear_backward(const float *dout, const float *w, float *din, int batch, int in, int out)
+{
+    oracle_sgemm('N', 'N', batch, in, out, 1.f, dout, w, 0.f, din);
+}
+
+/* CatsEye_linear_update (catseye.h:478-505): dw += dOut^T x (gemm_rtn, beta 1),
+ * then the biases after the weights step by -eta dOut, sample after sample. */
+void oracle_linear_update(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out,
+                          float eta)
+{
+    oracle_sgemm('T', 'N', out, in, batch, 1.f, dout, x, 1.f, dw);
+    for (int b = 0; b < batch; b++)
+        for (int i = 0; i < out; i++) w[(size_t)in * out + i] -= eta * dout[(size_t)b * out + i];
+}
+
 /* ---- llama decode step (llm/catseye_llm.h:684-721, 1574-1772) ---------------- */
 
 static void rmsnorm(float *o, const float *x, const float *w, int n)

@@ -78,6 +78,15 @@ void oracle_conv2d_forward(const float *x, const float *w, float *z, int batch, 
                            int h, int wd, int ch, int k, int pad, int stride);
 /* CatsEye_linear_forward (catseye.h:416-444): z = x * W^T + bias, bias at w[in*out] */
 void oracle_linear_forward(const float *x, const float *w, float *z, int batch, int in, int out);
+void oracle_col2im(const float *col, int channels, int height, int width, int kh, int kw,
+                   int ph, int pw, int sh, int sw, float *im);
+void oracle_conv2d_backward(const float *dout, const float *w, float *din, int batch, int ich,
+                            int h, int wd, int ch, int k, int pad, int stride);
+void oracle_conv2d_update(const float *dout, const float *x, float *dw, int batch, int ich,
+                          int h, int wd, int ch, int k, int pad, int stride);
+void oracle_linear_backward(const float *dout, const float *w, float *din, int batch, int in, int out);
+void oracle_linear_update(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out,
+                          float eta);
 
 /* Llama decode step, restating cats_llama2_transformer (llm/catseye_llm.h:1625-1772).
  * Layer matrices of one kind are stored back to back: wq = L matrices [dim][dim] ... */

@@ -90,6 +90,11 @@ class Oracle:
         L.oracle_im2col.argtypes = [_vp] + [C.c_int] * 9 + [_vp]
         L.oracle_conv2d_forward.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8
         L.oracle_linear_forward.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int]
+        L.oracle_col2im.argtypes = [_vp] + [C.c_int] * 9 + [_vp]
+        L.oracle_conv2d_backward.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8
+        L.oracle_conv2d_update.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8
+        L.oracle_linear_backward.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int]
+        L.oracle_linear_update.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_float]
 
     # --- conversions / quantizers -------------------------------------------
     def fp16_to_fp32(self, h):
@@ -167,6 +172,37 @@ class Oracle:
                                        _ptr(z), batch, n_in, n_out)
         return z
 
+    # --- CNN training layers (catseye.h:445-505, 533-556, 589-640) ------------
+    def col2im(self, col, c, h, w, kh, kw, ph, pw, sh, sw):
+        im = np.zeros(c * h * w, dtype=np.float32)
+        self.lib.oracle_col2im(_ptr(np.ascontiguousarray(col, np.float32)), c, h, w, kh, kw, ph, pw, sh, sw, _ptr(im))
+        return im
+
+    def conv2d_backward(self, dout, w, batch, ich, h, wd, ch, k, pad, stride):
+        din = np.zeros(batch * ich * h * wd, dtype=np.float32)
+        self.lib.oracle_conv2d_backward(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                    _ptr(din), batch, ich, h, wd, ch, k, pad, stride)
+        return din
+
+    def conv2d_update(self, dout, x, dw0, batch, ich, h, wd, ch, k, pad, stride):
+        dw = np.array(dw0, dtype=np.float32, copy=True)
+        self.lib.oracle_conv2d_update(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(x, np.float32)),
+                                  _ptr(dw), batch, ich, h, wd, ch, k, pad, stride)
+        return dw
+
+    def linear_backward(self, dout, w, batch, n_in, n_out):
+        din = np.zeros(batch * n_in, dtype=np.float32)
+        self.lib.oracle_linear_backward(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                    _ptr(din), batch, n_in, n_out)
+        return din
+
+    def linear_update(self, dout, x, w0, dw0, batch, n_in, n_out, eta):
+        w = np.array(w0, dtype=np.float32, copy=True)
+        dw = np.array(dw0, dtype=np.float32, copy=True)
+        self.lib.oracle_linear_update(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(x, np.float32)),
+                                  _ptr(w), _ptr(dw), batch, n_in, n_out, float(eta))
+        return w, dw
+
     def argmax(self, v):
         v = np.ascontiguousarray(v, np.float32)
         return self.lib.oracle_argmax(_ptr(v), v.size)
@@ -242,6 +278,11 @@ class Reference:
             L.ref_im2col.argtypes = [_vp] + [C.c_int] * 9 + [_vp]
             L.ref_conv2d_forward.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8
             L.ref_linear_forward.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int]
+            L.ref_col2im.argtypes = [_vp] + [C.c_int] * 9 + [_vp]
+            L.ref_conv2d_backward.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8
+            L.ref_conv2d_update.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8 + [_vp]
+            L.ref_linear_backward.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int]
+            L.ref_linear_update.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_float]
 
     def is_avx(self):
         return bool(self.lib.ref_is_avx())
@@ -277,6 +318,37 @@ class Reference:
         if t in (Q3_K, Q6_K):
             return self.matmul_raw(t, self.quantize_q8_K(x), w, n, d)
         return self.matmul_raw(t, self.quantize_q8(x), w, n, d)
+
+    # --- CNN training layers (catseye.h:445-505, 533-556, 589-640) ------------
+    def col2im(self, col, c, h, w, kh, kw, ph, pw, sh, sw):
+        im = np.zeros(c * h * w, dtype=np.float32)
+        self.lib.ref_col2im(_ptr(np.ascontiguousarray(col, np.float32)), c, h, w, kh, kw, ph, pw, sh, sw, _ptr(im))
+        return im
+
+    def conv2d_backward(self, dout, w, batch, ich, h, wd, ch, k, pad, stride):
+        din = np.zeros(batch * ich * h * wd, dtype=np.float32)
+        self.lib.ref_conv2d_backward(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                    _ptr(din), batch, ich, h, wd, ch, k, pad, stride)
+        return din
+
+    def conv2d_update(self, dout, x, dw0, batch, ich, h, wd, ch, k, pad, stride):
+        dw = np.array(dw0, dtype=np.float32, copy=True)
+        self.lib.ref_conv2d_update(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(x, np.float32)),
+                                  _ptr(dw), batch, ich, h, wd, ch, k, pad, stride, _ptr(np.zeros(ch * ich * k * k, np.float32)))
+        return dw
+
+    def linear_backward(self, dout, w, batch, n_in, n_out):
+        din = np.zeros(batch * n_in, dtype=np.float32)
+        self.lib.ref_linear_backward(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                    _ptr(din), batch, n_in, n_out)
+        return din
+
+    def linear_update(self, dout, x, w0, dw0, batch, n_in, n_out, eta):
+        w = np.array(w0, dtype=np.float32, copy=True)
+        dw = np.array(dw0, dtype=np.float32, copy=True)
+        self.lib.ref_linear_update(_ptr(np.ascontiguousarray(dout, np.float32)), _ptr(np.ascontiguousarray(x, np.float32)),
+                                  _ptr(w), _ptr(dw), batch, n_in, n_out, float(eta))
+        return w, dw
 
     def argmax(self, v):
         v = np.ascontiguousarray(v, np.float32)

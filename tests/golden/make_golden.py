@@ -102,6 +102,32 @@ def cnn(rc, rng):
     np.savez_compressed(os.path.join(HERE, "cnn.npz"), **out)
 
 
+def cnn_train(rc, rng):
+    """The training layers: col2im, convolution backward / update (3x3 pad 1
+    stride 1, and 3x3 pad 1 stride 2), linear backward / update."""
+    out = {}
+    col = rng.uniform(-1, 1, 3 * 9 * 8 * 8).astype(np.float32)
+    out["col2im_col"] = col
+    out["col2im"] = rc.col2im(col, 3, 8, 8, 3, 3, 1, 1, 1, 1)
+    for name, (b, ich, h, wd, ch, k, pad, st) in (("s1", (2, 3, 8, 8, 4, 3, 1, 1)), ("s2", (2, 5, 9, 7, 6, 3, 1, 2))):
+        oh, ow = (h + 2 * pad - k) // st + 1, (wd + 2 * pad - k) // st + 1
+        x = rng.uniform(0, 1, b * ich * h * wd).astype(np.float32)
+        w = (rng.standard_normal(ch * ich * k * k) * np.sqrt(2 / (ich * k * k))).astype(np.float32)
+        dout = rng.uniform(-1, 1, b * ch * oh * ow).astype(np.float32)
+        dw0 = rng.uniform(-0.1, 0.1, ch * ich * k * k).astype(np.float32)
+        out[f"conv_{name}_x"], out[f"conv_{name}_w"], out[f"conv_{name}_dout"], out[f"conv_{name}_dw0"] = x, w, dout, dw0
+        out[f"conv_{name}_din"] = rc.conv2d_backward(dout, w, b, ich, h, wd, ch, k, pad, st)
+        out[f"conv_{name}_dw"] = rc.conv2d_update(dout, x, dw0, b, ich, h, wd, ch, k, pad, st)
+    xl = rng.uniform(0, 1, 3 * 20).astype(np.float32)
+    wl = (rng.standard_normal(20 * 7 + 7) * 0.3).astype(np.float32)
+    dl = rng.uniform(-1, 1, 3 * 7).astype(np.float32)
+    dwl = rng.uniform(-0.1, 0.1, 20 * 7).astype(np.float32)
+    out["lin_x"], out["lin_w"], out["lin_dout"], out["lin_dw0"] = xl, wl, dl, dwl
+    out["lin_din"] = rc.linear_backward(dl, wl, 3, 20, 7)
+    out["lin_w1"], out["lin_dw"] = rc.linear_update(dl, xl, wl, dwl, 3, 20, 7, 0.01)
+    np.savez_compressed(os.path.join(HERE, "cnn_train.npz"), **out)
+
+
 TINY = LlmConfig(dim=64, hidden=96, n_layers=2, n_heads=4, n_kv_heads=2, vocab=128, seq_len=32)
 
 
@@ -139,6 +165,8 @@ def main(only=None):
         quant(ref, refs, orc, rng)
         matvec(ref, refs, orc, rng)
         cnn(rc, rng)
+    if want("cnn_train"):
+        cnn_train(rc, np.random.default_rng(20241202))
     if want("llm_f32"):
         llm(ref, orc, F32, "llm_f32")
     if want("llm_q4_0"):

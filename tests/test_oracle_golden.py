@@ -84,6 +84,21 @@ def test_im2col_conv_linear_golden(orc):
     assert rel(orc.linear_forward(g["lin_x"], g["lin_w"], 3, 20, 7), g["lin_z"]) < 1e-5
 
 
+def test_cnn_training_layers_golden(orc):
+    """col2im bit-exact; convolution / linear backward and update within 1e-5
+    of the reference's layers (catseye.h:445-505, 533-556, 589-640)."""
+    g = load("cnn_train")
+    assert np.array_equal(orc.col2im(g["col2im_col"], 3, 8, 8, 3, 3, 1, 1, 1, 1), g["col2im"])
+    for name, (b, ich, h, wd, ch, k, pad, st) in (("s1", (2, 3, 8, 8, 4, 3, 1, 1)), ("s2", (2, 5, 9, 7, 6, 3, 1, 2))):
+        p = f"conv_{name}_"
+        assert rel(orc.conv2d_backward(g[p + "dout"], g[p + "w"], b, ich, h, wd, ch, k, pad, st), g[p + "din"]) < 1e-5
+        assert rel(orc.conv2d_update(g[p + "dout"], g[p + "x"], g[p + "dw0"], b, ich, h, wd, ch, k, pad, st),
+                   g[p + "dw"]) < 1e-5
+    assert rel(orc.linear_backward(g["lin_dout"], g["lin_w"], 3, 20, 7), g["lin_din"]) < 1e-5
+    w1, dw = orc.linear_update(g["lin_dout"], g["lin_x"], g["lin_w"], g["lin_dw0"], 3, 20, 7, 0.01)
+    assert rel(w1, g["lin_w1"]) < 1e-6 and rel(dw, g["lin_dw"]) < 1e-5
+
+
 class _MW:
     def __init__(self, g):
         from catseye_b200.llm import LlmConfig

@@ -53,6 +53,8 @@ SIGNATURES = {
     "cats_gpu_llm_destroy": (None, [_vp]),
     "cats_gpu_llm_set_weights": (_i, [_vp] + [_vp] * 12),
     "cats_gpu_llm_init_random": (_i, [_vp, _u64, _f]),
+    "cats_gpu_llm_file_config": (_i, [C.c_char_p, C.POINTER(LlmConfigC)]),
+    "cats_gpu_llm_load": (_vp, [C.c_char_p, _i, _i, _i]),
     "cats_gpu_llama2_transformer": (_vp, [_i, _i, _vp, _vp]),
     "cats_gpu_llm_generate": (_i, [_vp, _i, _i, _i, _vp]),
     "cats_gpu_llm_enqueue": (_i, [_vp, _i]),

@@ -5,6 +5,7 @@
 // buffers for the host-pointer drop-ins, and the sticky error status that the
 // void drop-in signatures cannot return.
 #include "../../include/catsgpu.h"
+#include "loader.cuh"
 #include "conv.cuh"
 #include "kquant.cuh"
 #include "llm.cuh"
@@ -503,6 +504,49 @@ void cats_gpu_llm_destroy(cats_gpu_llm *h)
     llm_free(&h->m);
     if (h->tok_log) cudaFree(h->tok_log);
     delete h;
+}
+
+int cats_gpu_llm_file_config(const char *path, cats_gpu_llm_config *cfg)
+{
+    if (!path || !cfg) return fail(CATS_ERR_ARG, "cats_gpu_llm_file_config");
+    ModelFile f;
+    std::string why;
+    if (model_file_open(path, f, &why) != E_OK) return fail(CATS_ERR_ARG, ("cats_gpu_llm_file_config: " + why).c_str());
+    const LlmConfig &c = f.cfg;
+    *cfg = cats_gpu_llm_config{c.dim, c.hidden, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab, c.seq_len, c.wtype, 0, 1};
+    model_file_close(f);
+    return CATS_OK;
+}
+
+cats_gpu_llm *cats_gpu_llm_load(const char *path, int tp_rank, int tp_size, int seq_len)
+{
+    if (!ensure_init()) return nullptr;
+    if (!path || tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || seq_len < 0) {
+        fail(CATS_ERR_ARG, "cats_gpu_llm_load");
+        return nullptr;
+    }
+    ModelFile f;
+    std::string why;
+    if (model_file_open(path, f, &why) != E_OK) {
+        fail(CATS_ERR_ARG, ("cats_gpu_llm_load: " + why).c_str());
+        return nullptr;
+    }
+    const LlmConfig &c = f.cfg;
+    cats_gpu_llm_config cc{c.dim, c.hidden, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab, seq_len ? seq_len : c.seq_len,
+                           c.wtype, tp_rank, tp_size};
+    cats_gpu_llm *h = nullptr;
+    if (cc.wtype != CATS_TYPE_F32 && cc.wtype != CATS_TYPE_Q4_0 && cc.wtype != CATS_TYPE_Q8_0) {
+        fail(CATS_ERR_UNSUPPORTED, "cats_gpu_llm_load: layer weight type (F32, Q4_0 or Q8_0 models run on the device)");
+    } else if ((h = cats_gpu_llm_create(&cc)) != nullptr) {
+        const int rc = model_file_load(&h->m, f, &why);
+        if (rc != E_OK) {
+            fail(rc, ("cats_gpu_llm_load: " + why).c_str());
+            cats_gpu_llm_destroy(h);
+            h = nullptr;
+        }
+    }
+    model_file_close(f);
+    return h;
 }
 
 int cats_gpu_llm_set_weights(cats_gpu_llm *h, const float *emb, const float *rms_att, const float *rms_ffn,

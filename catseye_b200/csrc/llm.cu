@@ -466,6 +466,30 @@ int llm_set_weights(LlmModel *m, const float *emb, const float *rms_att, const f
     return rc;
 }
 
+int llm_set_weights_layers(LlmModel *m, const float *emb, const float *rms_att, const float *rms_ffn,
+                           const float *rms_final, const void *const *layer_w, const void *wcls)
+{
+    const LlmConfig &c = m->c;
+    cudaStream_t st = m->stream;
+    if (cudaMemcpyAsync(m->emb, emb, (size_t)c.vocab * c.dim * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(m->rms_att, rms_att, (size_t)c.n_layers * c.dim * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(m->rms_ffn, rms_ffn, (size_t)c.n_layers * c.dim * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(m->rms_final, rms_final, (size_t)c.dim * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return E_CUDA;
+    uint8_t *stg = nullptr;
+    if (cudaMalloc(&stg, staging_bytes(c)) != cudaSuccess) return E_NOMEM;
+    int rc = E_OK;
+    for (int l = 0; l < c.n_layers && rc == E_OK; l++) {
+        const void *const *w = layer_w + 7 * (size_t)l;
+        auto h = [](const void *p) { return Src{static_cast<const uint8_t *>(p), true}; };
+        rc = build_layer(m, l, h(w[0]), h(w[1]), h(w[2]), h(w[3]), h(w[4]), h(w[5]), h(w[6]), stg);
+    }
+    if (rc == E_OK) rc = build_cls(m, Src{static_cast<const uint8_t *>(wcls), true}, stg);
+    cudaFree(stg);
+    m->weights_ready = rc == E_OK;
+    return rc;
+}
+
 // tensor ids of the synthetic generator (fixed so every TP rank regenerates the same tensors)
 enum { T_EMB = 0, T_RMS_ATT = 1, T_RMS_FFN = 2, T_RMS_FINAL = 3, T_WCLS = 4, T_LAYER0 = 16 };
 static int layer_tid(int l, int k) { return T_LAYER0 + l * 8 + k; }   // k: 0 wq 1 wk 2 wv 3 wo 4 w1 5 w2 6 w3

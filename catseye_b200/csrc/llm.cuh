@@ -128,6 +128,11 @@ void llm_free(LlmModel *m);
 int llm_set_weights(LlmModel *m, const float *emb, const float *rms_att, const float *rms_ffn,
                     const float *rms_final, const void *wq, const void *wk, const void *wv,
                     const void *wo, const void *w1, const void *w2, const void *w3, const void *wcls);
+// the same from one host pointer per tensor: layer_w[7 * l + k] for k = wq, wk,
+// wv, wo, w1, w2, w3 of layer l (a loader's memory-mapped file); only this
+// rank's slices of each matrix are read
+int llm_set_weights_layers(LlmModel *m, const float *emb, const float *rms_att, const float *rms_ffn,
+                           const float *rms_final, const void *const *layer_w, const void *wcls);
 // synthetic weights generated on the device: N(0, std) then block-quantized
 int llm_init_random(LlmModel *m, unsigned long long seed, float std);
 // enqueue one decode step (token/pos from m->params) on m->stream (graph if captured)

@@ -67,6 +67,24 @@ class GpuLLM:
             raise _lib.CatsGpuError("cats_gpu_llm_create failed")
         self._logits = np.zeros(cfg.vocab, dtype=np.float32)
 
+    @classmethod
+    def load(cls, path, tp_rank=0, tp_size=1, seq_len=0):
+        """A model straight from a GGUF v2/v3, ggjt v3 or llama2.c .bin file
+        (cats_gpu_llm_load): this rank's slices uploaded a layer at a time."""
+        lib = _lib.init()
+        c = _lib.LlmConfigC()
+        _lib.check(lib.cats_gpu_llm_file_config(str(path).encode(), C.byref(c)), "file_config")
+        self = cls.__new__(cls)
+        self.lib = lib
+        self.cfg = LlmConfig(c.dim, c.hidden, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab,
+                             seq_len or c.seq_len, c.wtype)
+        self.h = lib.cats_gpu_llm_load(str(path).encode(), tp_rank, tp_size, seq_len)
+        if not self.h:
+            _lib.check(None, "cats_gpu_llm_load")
+            raise _lib.CatsGpuError("cats_gpu_llm_load failed")
+        self._logits = np.zeros(self.cfg.vocab, dtype=np.float32)
+        return self
+
     def set_weights(self, mw):
         """mw: object with numpy blobs emb, rms_att, rms_ffn, rms_final, wq, wk, wv, wo, w1, w2, w3, wcls."""
         ptrs = [C.c_void_p(np.ascontiguousarray(getattr(mw, n)).ctypes.data)

@@ -151,6 +151,23 @@ int cats_gpu_llm_set_weights(cats_gpu_llm *m, const float *emb, const float *rms
                              const float *rms_ffn, const float *rms_final, const void *wq,
                              const void *wk, const void *wv, const void *wo, const void *w1,
                              const void *w2, const void *w3, const void *wcls);
+/* Model files straight to the device, the formats the reference's loaders
+ * read: GGUF v2/v3 (cats_gguf_load, llm/catseye_llm.h:2678-2895), the legacy
+ * llama.cpp 'ggjt' v3 files (cats_ggml_load, :2326-2550) and llama2.c .bin
+ * checkpoints (cats_checkpoint_load, :2900-2993).  The file is mapped and
+ * every header, metadata and tensor-table read is checked against its size
+ * (the reference copies metadata strings into 64-byte buffers, :2653, :2714).
+ * cats_gpu_llm_file_config parses only (no GPU) and reports the model's
+ * hyperparameters: wtype is the layer matrices' ggml type, tp fields 0 / 1.
+ * cats_gpu_llm_load creates the model (tp_rank of tp_size: each rank uploads
+ * only its slices; seq_len 0 = the file's context) and uploads the weights a
+ * layer at a time.  The device model takes F32, Q4_0 or Q8_0 layer matrices
+ * with a classifier of the same type (output.weight, or the embedding when
+ * the file has none); the embedding may be F32, F16, Q4_0 or Q8_0 (expanded to
+ * fp32 once, exactly); norms F32.  Other mixes fail with CATS_ERR_UNSUPPORTED
+ * and a reason printed once. */
+int cats_gpu_llm_file_config(const char *path, cats_gpu_llm_config *cfg);
+cats_gpu_llm *cats_gpu_llm_load(const char *path, int tp_rank, int tp_size, int seq_len);
 /* Synthetic weights generated on the device: N(0, std) (norms = 1), then
  * block-quantized to the model's type; deterministic in seed. */
 int cats_gpu_llm_init_random(cats_gpu_llm *m, unsigned long long seed, float std);

@@ -272,6 +272,9 @@ class Reference:
                 L.ref_llm_use_f32_activations.argtypes = [_vp]
             if hasattr(L, "ref_llm_use_q8_activations"):
                 L.ref_llm_use_q8_activations.argtypes = [_vp]
+            if hasattr(L, "ref_llm_load"):
+                L.ref_llm_load.restype = _vp
+                L.ref_llm_load.argtypes = [C.c_char_p, C.c_int, _vp]
         else:
             L.ref_sgemm.argtypes = [C.c_char, C.c_char, C.c_int, C.c_int, C.c_int, C.c_float,
                                     _vp, _vp, C.c_float, _vp]
@@ -382,6 +385,16 @@ class Reference:
     def llm(self, mw, f32_act=False):
         return RefLLM(self, mw, f32_act)
 
+    def load(self, path, fmt):
+        """The reference's own loader on a model file (fmt 1 GGUF, 2 ggjt, 3
+        llama2.c .bin): (a stepper, [dim, hidden, layers, heads, kv_heads,
+        vocab, seq_len])."""
+        hp = np.zeros(7, np.int32)
+        h = self.lib.ref_llm_load(str(path).encode(), fmt, _ptr(hp))
+        if not h:
+            raise ValueError(f"the reference's loader refused {path}")
+        return RefLoaded(self, h, int(hp[5])), [int(v) for v in hp]
+
 
 class RefLLM:
     """cats_llama2_transformer itself, on a model bound to the given weight blobs.
@@ -416,3 +429,14 @@ class RefLLM:
             self.ref.lib.ref_llm_destroy(self.h)
         except Exception:
             pass
+
+
+class RefLoaded:
+    """cats_llama2_transformer on a model the reference's own loader read."""
+
+    def __init__(self, ref, h, vocab):
+        self.ref, self.h, self.vocab = ref, h, vocab
+
+    def step(self, token, pos):
+        p = self.ref.lib.ref_llm_step(self.h, token, pos)
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()

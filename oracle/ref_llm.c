@@ -118,6 +118,26 @@ void *ref_llm_create(int dim, int hidden, int n_layers, int n_heads, int n_kv_he
     return r;
 }
 
+/* The reference's own loaders on a model file: fmt 1 cats_gguf_load
+ * (llm/catseye_llm.h:2678-2895), 2 cats_ggml_load (:2326-2550), 3
+ * cats_checkpoint_load (:2900-2993); then cats_llm_malloc.  hp receives
+ * n_embd, n_hidden, n_layer, n_head, n_kv_head, n_vocab, seq_len. */
+void *ref_llm_load(const char *path, int fmt, int *hp)
+{
+    ref_model *r = calloc(1, sizeof(ref_model));
+    cats_llm_model *m = &r->m;
+    int rc = 0;
+    if (fmt == 1) rc = cats_gguf_load((char *)path, m);
+    else if (fmt == 2) rc = cats_ggml_load((char *)path, m);
+    else rc = cats_checkpoint_load((char *)path, m) > 0 ? 0 : 1;
+    if (rc != 0) { free(r); return NULL; }
+    if (fmt != 1) m->n_kv_head = m->n_kv_head ? m->n_kv_head : m->n_head;
+    hp[0] = m->n_embd; hp[1] = m->n_hidden; hp[2] = m->n_layer; hp[3] = m->n_head;
+    hp[4] = m->n_kv_head; hp[5] = m->n_vocab; hp[6] = m->seq_len;
+    cats_llm_malloc(m);
+    return r;
+}
+
 float *ref_llm_step(void *h, int token, int pos)
 {
     ref_model *r = h;

@@ -385,6 +385,24 @@ void cats_linear_update(const float *dout, const float *x, float *w, float *dw, 
 int cats_linear_update_dev(const float *dout, const float *x, float *w, float *dw, int batch, int in, int out,
                            float eta, void *stream);
 
+/* ---- the OpenCL backend's host API over this library ----------------------
+ * What include/cats_ocl_cuda.h maps ocl.h's calls onto, so catseye's OpenCL
+ * sgemm backend (sgemm_ocl2.h) runs unchanged on the GPU
+ * (cc -DCATS_OPENCL -include cats_ocl_cuda.h ...).  cats_ocl_setup replaces
+ * oclSetup (ocl.h:142-195): initialises the device and returns the size of
+ * the backend's one device buffer ($CATS_OCL_BUFFER_BYTES, default 1 GiB).
+ * cats_ocl_alloc / _free / _write / _read replace the buffer calls
+ * (ocl.h:229-320, blocking).  cats_ocl_run replaces oclRun (ocl.h:322-355)
+ * for the backend's kernels by name ("gemm_rnn", "transpose", "im2col";
+ * sgemm_ocl2.h:14-169) with their int8 / float4 argument blocks; float
+ * offsets into the buffer as the kernels take them. */
+unsigned long cats_ocl_setup(int device);
+void *cats_ocl_alloc(size_t bytes);
+void cats_ocl_free(void *buf);
+int cats_ocl_write(void *buf, size_t offset, size_t size, const void *host);
+int cats_ocl_read(void *buf, size_t offset, size_t size, void *host);
+int cats_ocl_run(const char *kernel, void *buf, const int *info, const float *param);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -272,6 +272,9 @@ class Reference:
                 L.ref_llm_use_f32_activations.argtypes = [_vp]
             if hasattr(L, "ref_llm_use_q8_activations"):
                 L.ref_llm_use_q8_activations.argtypes = [_vp]
+            if hasattr(L, "ref_llm_dropin_tables"):   # libcatsgpu dropped into the reference runtime
+                L.ref_llm_dropin_tables.argtypes = []
+                L.ref_llm_dropin_tables()
             if hasattr(L, "ref_llm_load"):
                 L.ref_llm_load.restype = _vp
                 L.ref_llm_load.argtypes = [C.c_char_p, C.c_int, _vp]
@@ -286,6 +289,9 @@ class Reference:
             L.ref_conv2d_update.argtypes = [_vp, _vp, _vp] + [C.c_int] * 8 + [_vp]
             L.ref_linear_backward.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int]
             L.ref_linear_update.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_float]
+            if hasattr(L, "ref_cnn_init"):   # the OpenCL backend over libcatsgpu: sgemm_init first
+                L.ref_cnn_init.argtypes = []
+                L.ref_cnn_init()
 
     def is_avx(self):
         return bool(self.lib.ref_is_avx())

@@ -7,6 +7,12 @@
  */
 #include "catseye.h"
 
+#ifdef CATS_OPENCL
+/* The OpenCL backend built over libcatsgpu (include/cats_ocl_cuda.h is
+ * force-included): sgemm_init as catseye's network constructor calls it. */
+void ref_cnn_init(void) { sgemm_init(0); }
+#endif
+
 void ref_sgemm(char ta, char tb, int m, int n, int k, float alpha, float *a, float *b,
                float beta, float *c)
 {

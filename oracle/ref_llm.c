@@ -183,6 +183,27 @@ int ref_llm_use_q8_activations(void *h)
     return k;
 }
 
+#ifdef CATS_DROPIN
+/* The drop-in in place: the runtime's dispatch tables (llm/catseye_llm.h:
+ * 2583-2607) rebound to libcatsgpu's matmuls and quantizers, as a program
+ * binding the library would do before loading a model.  Tensors bound after
+ * this (ref_llm_create, the loaders) call the GPU; the reference's own
+ * cats_llama2_transformer drives them. */
+#include "catsgpu.h"
+void ref_llm_dropin_tables(void)
+{
+    cats_gpu_init(-1);
+    gguf_matmul[GGML_TYPE_F32] = cats_gpu_matmul_f32;
+    gguf_matmul[GGML_TYPE_Q4_0] = cats_gpu_matmul_q4_0_q8;
+    gguf_quantize[GGML_TYPE_Q4_0] = cats_gpu_quantize_q8;
+    gguf_dequantize[GGML_TYPE_Q4_0] = cats_gpu_dequantize_q4_0;
+    gguf_matmul[GGML_TYPE_Q3_K] = cats_gpu_matmul_q3_K_q8_K;
+    gguf_matmul[GGML_TYPE_Q6_K] = cats_gpu_matmul_q6_K_q8_K;
+    gguf_quantize[GGML_TYPE_Q3_K] = cats_gpu_quantize_q8_K;
+    gguf_quantize[GGML_TYPE_Q6_K] = cats_gpu_quantize_q8_K;
+}
+#endif
+
 void ref_llm_destroy(void *h)
 {
     ref_model *r = h;

@@ -1,6 +1,7 @@
 """Phase timeline of one step of the persistent decode kernel.
 
     python -m catseye_b200.decode_trace [--type 2] [--layers 32] [--pos 8] [--reps 3]
+    torchrun --nproc-per-node N -m catseye_b200.decode_trace ...   (tensor parallel, rank 0 prints)
 
 Runs a Llama-2-7B-shaped model (random weights, the given weight type and
 layer count), feeds a few prompt tokens, then traces single steps: thread 0
@@ -57,16 +58,36 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--pos", type=int, default=8)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--model", default="LLAMA2_7B", choices=["LLAMA2_7B", "LLAMA2_70B"])
     args = ap.parse_args()
-    _lib.init(0)
-    cfg = replace(llm.LLAMA2_7B.with_type(args.type), n_layers=args.layers)
-    m = llm.GpuLLM(cfg)
+    import os
+    ws, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    _lib.init(local)
+    cfg = replace(getattr(llm, args.model).with_type(args.type), n_layers=args.layers)
+    dist = None
+    if ws > 1:   # every rank traces the same steps of one sharded model
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("gloo")
+        m = llm.GpuLLM(cfg, rank, ws)
+        m.tp_connect(llm.tp_share_id())
+        assert m.tp_persistent(), "the sharded model did not map its peers"
+    else:
+        m = llm.GpuLLM(cfg)
     m.init_random(7)
+    if dist:
+        dist.barrier()
     for pos in range(args.pos):
         m.step(pos + 1, pos)
     per_cta = 1 + len(PHASES) * args.layers + len(TAIL) + 8
     for rep in range(args.reps):
+        if dist:
+            dist.barrier()
         ns, clk = m.trace_step(5, args.pos + rep, per_cta)
+        if rank:
+            continue
         tab, total, mhz = phase_table(ns, clk, args.layers)
         print(f"step at pos {args.pos + rep}: {total:.1f} us, SM clock {mhz:.0f} MHz")
         for name, (mean, mean_c, crit) in tab.items():
@@ -74,6 +95,9 @@ def main():
             print(f"  {name:18s} mean/CTA {mean / per:6.2f} us (clock64 {mean_c / per:6.2f})  "
                   f"critical {crit / per:6.2f} us   [per layer; total {mean:7.1f} us]")
     m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

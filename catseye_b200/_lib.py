@@ -91,6 +91,12 @@ SIGNATURES = {
     "cats_conv2d_forward_dev": (_i, [_vp, _vp, _vp] + [_i] * 8 + [_vp]),
     "cats_linear_forward": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "cats_linear_forward_dev": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "cats_ocl_setup": (C.c_ulong, [_i]),
+    "cats_ocl_alloc": (_vp, [_sz]),
+    "cats_ocl_free": (None, [_vp]),
+    "cats_ocl_write": (_i, [_vp, _sz, _sz, _vp]),
+    "cats_ocl_read": (_i, [_vp, _sz, _sz, _vp]),
+    "cats_ocl_run": (_i, [C.c_char_p, _vp, _vp, _vp]),
     "cats_col2im": (None, [_vp] + [_i] * 9 + [_vp]),
     "cats_col2im_dev": (_i, [_vp] + [_i] * 9 + [_vp, _vp]),
     "cats_conv2d_backward": (None, [_vp, _vp, _vp] + [_i] * 8),

@@ -31,15 +31,18 @@
 //  * Tensor parallelism (one process and one GPU per rank): each rank runs
 //    this kernel over its weight slices (llm.cu shards them).  wo and w2 give
 //    partial sums of every row; a CTA keeps its rows in shared memory and, at
-//    the phase's end, stores them with plain 64-byte stores straight into
-//    every rank's exchange buffer over NVLink (peer memory mapped with CUDA
-//    IPC), then counts itself in on every rank with a system-scope atomic and
-//    waits (bounded) until all CTAs of all ranks have done so.  The next
-//    staging adds the residual and the ranks' partial rows in rank order, so
-//    every rank holds the same residual stream bit for bit.  The classifier
-//    rows go to every rank's logits the same way, and the greedy key is a
-//    system-scope max on every rank's word.  No collective library call, no
-//    bulk copy from peer memory, no multicast.
+//    the phase's end, stores them straight into every rank's exchange buffer
+//    over NVLink (peer memory mapped with CUDA IPC) as 8-byte words that
+//    carry the exchange's sequence number beside the value, and moves on: no
+//    fence, no flag.  Each CTA then builds its slice of the next residual
+//    stream, waiting (bounded) per row until every rank's word is current and
+//    adding the ranks' values in rank order, so every rank holds the same
+//    residual stream bit for bit; the phase's grid barrier publishes it.  The
+//    classifier rows go to every rank's logits with plain stores, the greedy
+//    key is a system-scope max on every rank's word, and one counted barrier
+//    across the ranks (a system-scope fence, then arrival atomics) ends the
+//    token.  No collective library call, no bulk copy from peer memory, no
+//    multicast.
 //
 // Shared memory: a fixed 1 KB header (the mbarriers at offset 0, reduction
 // scratch, flags), the weight descriptors, then the two rings (group g's
@@ -98,7 +101,8 @@ struct DecodeArgs {
     int trace_stride;
     // tensor parallelism (tp_size > 1; see TpXchg for the exchange buffers)
     int tp_size, tp_rank, vocab_off;
-    unsigned int tp_epoch;                // arrivals per source rank counted before this launch
+    unsigned int tp_epoch;                // classifier arrivals per source rank counted before this launch
+    unsigned int tp_seq;                  // tag of this launch's first partial-row exchange (never 0)
     uint8_t *tp_peer[TP_MAX_RANKS];       // rank r's exchange buffer, mapped here (this rank's at tp_rank)
     unsigned long long tp_logits_off;     // byte offset of the logits in an exchange buffer
     float *x_alt;                         // the residual stream alternates between x and x_alt
@@ -235,55 +239,92 @@ __device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p)
     return v;
 }
 
-// The partial rows of every rank for one exchange: the residual stream plus
-// rank 0's rows, plus rank 1's, ... in rank order (identical on every rank),
-// with all loads of a round issued before any is used.
-struct ReduceSrc {
-    const float4 *x;      // residual stream before the block
-    const float4 *recv;   // [ranks][n4] partial rows
-    int ranks;
-    __device__ __forceinline__ static float4 add4(float4 a, float4 b)
-    {
-        return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-    }
-    template <int V>
-    __device__ __forceinline__ void fill(float4 (&v)[V], int i0, int stride, int n4) const
-    {
-        constexpr int RB = V >= 4 ? 2 : (V == 2 ? 4 : 8);   // partial vectors per round of loads
-        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < V; k++) {
-            const int i = i0 + k * stride;
-            v[k] = i < n4 ? __ldcg(x + i) : z;
-        }
-        for (int r0 = 0; r0 < ranks; r0 += RB) {
-            float4 p[RB][V];
-#pragma unroll
-            for (int rr = 0; rr < RB; rr++)
-#pragma unroll
-                for (int k = 0; k < V; k++) {
-                    const int i = i0 + k * stride;
-                    p[rr][k] = (r0 + rr < ranks && i < n4) ? __ldcg(recv + (size_t)(r0 + rr) * n4 + i) : z;
-                }
-#pragma unroll
-            for (int rr = 0; rr < RB; rr++)
-                if (r0 + rr < ranks)
-#pragma unroll
-                    for (int k = 0; k < V; k++) v[k] = add4(v[k], p[rr][k]);
-        }
-    }
-};
-
-__device__ __forceinline__ float *tp_recv(const DecodeArgs &a, int rank, int slot)
+// Tagged words of the partial-row exchange: the fp32 value in the low half,
+// the exchange's sequence number in the high half.  One aligned 8-byte store
+// is single-copy atomic, so a reader that sees the current sequence number
+// holds that exchange's value: no fence and no separate flag.
+__device__ __forceinline__ unsigned long long *tp_recv(const DecodeArgs &a, int rank, int slot)
 {
-    return reinterpret_cast<float *>(a.tp_peer[rank] + TpXchg::recv) + (size_t)slot * a.tp_size * a.dim;
+    return reinterpret_cast<unsigned long long *>(a.tp_peer[rank] + TpXchg::recv) + (size_t)slot * a.tp_size * a.dim;
 }
 
-// Store this CTA's rows of weight W (sm.push, 16 per owned tile) into every
-// rank's buffer: the partial rows of this rank in slot `slot` (logits = false)
-// or the logits rows at the rank's vocabulary offset.  Four consecutive
-// threads write one tile's 64 bytes to one rank.
-__device__ __forceinline__ void tp_push(const DecodeArgs &a, const Smem &sm, const WDesc &W, bool logits, int slot)
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// This CTA's slice of the residual-stream rows (all CTAs together: dim).
+__device__ __forceinline__ void tp_slice(int dim, int &r0, int &r1)
+{
+    r0 = (int)((long long)dim * blockIdx.x / gridDim.x);
+    r1 = (int)((long long)dim * (blockIdx.x + 1) / gridDim.x);
+}
+
+// The exchange after wo or w2 (tensor parallelism).  The CTA's partial rows
+// (sm.push, 16 per owned tile) go to every rank's slot `slot` as tagged words
+// (16 consecutive threads store a tile's 128 bytes to one rank; nothing
+// waits for them).  Then the CTA builds its slice of the next residual
+// stream: for each of its rows it waits (bounded) until every rank's word
+// carries `seq`, and xnext[row] = xcur[row] + rank 0's value + rank 1's + ...
+// in rank order, so every rank computes the same sums.  The caller's grid
+// barrier then publishes xnext.  Returns false when a wait gave up.
+__device__ __forceinline__ bool tp_exchange(const DecodeArgs &a, const Smem &sm, const WDesc &W, int slot,
+                                            unsigned seq, const float *xcur, float *xnext)
+{
+    constexpr int R = DEC_GW * DEC_RPW;
+    named_bar_sync(1, DEC_NC);   // the CTA's rows are in shared memory
+    const unsigned long long tag = (unsigned long long)seq << 32;
+    if (*sm.abort_s == 0) {
+        const int items = my_tiles(W) * a.tp_size * R;
+        for (int it = threadIdx.x; it < items; it += DEC_NC) {
+            const int q = it % R, rest = it / R;
+            const int r = rest % a.tp_size, j = rest / a.tp_size;
+            const int row = (blockIdx.x + j * gridDim.x) * R + q;
+            if (row >= W.d) continue;
+            const unsigned long long w = tag | __float_as_uint(sm.push[j * R + q]);
+            tp_recv(a, r, slot)[(size_t)a.tp_rank * a.dim + row] = w;
+        }
+    }
+    named_bar_sync(1, DEC_NC);   // sm.push is free again: it holds the gathered values below
+    int r0, r1;
+    tp_slice(a.dim, r0, r1);
+    const int n = (r1 - r0) * a.tp_size;
+    const unsigned long long *recv = tp_recv(a, a.tp_rank, slot);
+    bool ok = *sm.abort_s == 0;
+    for (int p = threadIdx.x; p < n && ok; p += DEC_NC) {
+        const int row = r0 + p / a.tp_size, r = p % a.tp_size;
+        const unsigned long long *src = recv + (size_t)r * a.dim + row;
+        unsigned long long v = ld_volatile_u64(src);
+        for (uint32_t i = 0; (v & 0xffffffff00000000ull) != tag; i++) {
+            if ((i & 63) == 63 && (i > GRID_SPIN_LIMIT || ld_volatile_i32(a.abort_flag))) {
+                ok = false;
+                break;
+            }
+            __nanosleep(32);
+            v = ld_volatile_u64(src);
+        }
+        sm.push[p] = __uint_as_float((uint32_t)v);
+    }
+    if (!ok) {
+        if (a.err) atomicOr(a.err, CATS_DEVERR_PEER_WAIT);
+        atomicExch(a.abort_flag, 1);
+        *sm.abort_s = 1;
+    }
+    named_bar_sync(1, DEC_NC);
+    for (int t = threadIdx.x; t < r1 - r0 && *sm.abort_s == 0; t += DEC_NC) {
+        float s = __ldcg(xcur + r0 + t);
+        for (int r = 0; r < a.tp_size; r++) s = __fadd_rn(s, sm.push[t * a.tp_size + r]);
+        xnext[r0 + t] = s;
+    }
+    return *sm.abort_s == 0;
+}
+
+// Store this CTA's classifier rows (sm.push, 16 per owned tile) into every
+// rank's logits at this rank's vocabulary offset.  Four consecutive threads
+// write one tile's 64 bytes to one rank.
+__device__ __forceinline__ void tp_push_logits(const DecodeArgs &a, const Smem &sm, const WDesc &W)
 {
     constexpr int R = DEC_GW * DEC_RPW;
     const int items = my_tiles(W) * a.tp_size * (R / 4);
@@ -292,8 +333,7 @@ __device__ __forceinline__ void tp_push(const DecodeArgs &a, const Smem &sm, con
         const int r = rest % a.tp_size, j = rest / a.tp_size;
         const int row = (blockIdx.x + j * gridDim.x) * R + q * 4;
         if (row >= W.d) continue;
-        float *dst = logits ? reinterpret_cast<float *>(a.tp_peer[r] + a.tp_logits_off) + a.vocab_off + row
-                            : tp_recv(a, r, slot) + (size_t)a.tp_rank * a.dim + row;
+        float *dst = reinterpret_cast<float *>(a.tp_peer[r] + a.tp_logits_off) + a.vocab_off + row;
         const float *src = sm.push + j * R + q * 4;
         if (row + 4 <= W.d && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
             *reinterpret_cast<float4 *>(dst) = *reinterpret_cast<const float4 *>(src);
@@ -303,16 +343,17 @@ __device__ __forceinline__ void tp_push(const DecodeArgs &a, const Smem &sm, con
     }
 }
 
-// Exchange among the ranks (and grid barrier of this rank's CTAs): push the
-// CTA's rows of W (when given), publish them and the CTA's greedy key (the
-// classifier, key != 0) with a system-scope fence, count in on every rank,
-// then wait until every CTA of every rank has counted in.  Bounded like
-// grid_sync, with the same CTA-wide decision.
-__device__ __forceinline__ bool tp_sync(const DecodeArgs &a, const Smem &sm, unsigned &target, const WDesc *W,
-                                        bool logits, int slot, unsigned long long key)
+// The classifier's exchange among the ranks (and grid barrier of this rank's
+// CTAs): push the CTA's logits rows to every rank, max the CTA's greedy key
+// (thread 0's `key`) into every rank's word, publish both with a
+// system-scope fence, count in on every rank, then wait until every CTA of
+// every rank has counted in.  Bounded like grid_sync, with the same CTA-wide
+// decision.  Once per token: the per-layer exchanges use tp_exchange.
+__device__ __forceinline__ bool tp_sync(const DecodeArgs &a, const Smem &sm, unsigned &target, const WDesc &W,
+                                        unsigned long long key)
 {
     named_bar_sync(1, DEC_NC);   // the CTA's rows are in shared memory
-    if (W && *sm.abort_s == 0) tp_push(a, sm, *W, logits, slot);
+    if (*sm.abort_s == 0) tp_push_logits(a, sm, W);
     named_bar_sync(1, DEC_NC);   // every store of the CTA issued
     if (threadIdx.x == 0) {
         bool ok = *sm.abort_s == 0;
@@ -758,16 +799,17 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
     const float no_rows[2] = {0.f, 0.f};
     float *xcur = a.x, *xnext = a.x_alt;   // tensor parallelism: the residual stream's two buffers
     int slot = 0;                          // tensor parallelism: the slot the next partial rows go to
+    unsigned seq = a.tp_seq;               // tensor parallelism: the next exchange's tag
     int tk = 0;
-    // staging after an exchange: residual + every rank's partial rows of `slot`
-    auto stage_sum = [&](const float *norm_w) {
-        stage_act<WT, DEC_STAGE_V>(ReduceSrc{reinterpret_cast<const float4 *>(xcur),
-                                             reinterpret_cast<const float4 *>(tp_recv(a, a.tp_rank, slot)), a.tp_size},
-                                   a.dim, norm_w, blockIdx.x == 0 ? xnext : nullptr, sm.xs, sm.red, tid, DEC_NC);
+    // the exchange after wo / w2, then the grid barrier that publishes the new residual stream
+    auto exchange = [&](const WDesc &W) -> bool {
+        const bool ok = tp_exchange(a, sm, W, slot, seq, xcur, xnext);
         float *t = xcur;
         xcur = xnext;
         xnext = t;
         slot ^= 1;
+        seq++;
+        return grid_sync(a, sm, target) && ok;
     };
     trace_mark(a, tk);
     for (int step = 0; step < a.steps; step++) {
@@ -786,11 +828,9 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             if (l == 0)
                 stage_act<WT, DEC_STAGE_V>(Float4Src{reinterpret_cast<const float4 *>(a.emb + (size_t)token * a.dim), false},
                                            a.dim, a.rms_att, blockIdx.x == 0 ? xcur : nullptr, sm.xs, sm.red, tid, DEC_NC);
-            else if (tp)
-                stage_sum(a.rms_att + (size_t)l * a.dim);
             else
-                stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_att + (size_t)l * a.dim, nullptr, sm.xs,
-                                           sm.red, tid, DEC_NC);
+                stage_act<WT, DEC_STAGE_V>(Float4Src{tp ? reinterpret_cast<const float4 *>(xcur) : x4, true}, a.dim,
+                                           a.rms_att + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[0], rg, DE_QKV, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
@@ -814,15 +854,12 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[1], rg, tp ? DE_PUSH : DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
-            if (!(alive = tp ? tp_sync(a, sm, xtarget, &wl[1], false, slot, 0ull) : grid_sync(a, sm, target))) break;
+            if (!(alive = tp ? exchange(wl[1]) : grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
             if (!tp) residual_first(a, wl[3], xr);   // x is final until the w2 epilogue
             // w1/w3 + SwiGLU
-            if (tp)
-                stage_sum(a.rms_ffn + (size_t)l * a.dim);
-            else
-                stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs,
-                                           sm.red, tid, DEC_NC);
+            stage_act<WT, DEC_STAGE_V>(Float4Src{tp ? reinterpret_cast<const float4 *>(xcur) : x4, true}, a.dim,
+                                       a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
@@ -834,15 +871,13 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[3], rg, tp ? DE_PUSH : DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
-            alive = tp ? tp_sync(a, sm, xtarget, &wl[3], false, slot, 0ull) : grid_sync(a, sm, target);
+            alive = tp ? exchange(wl[3]) : grid_sync(a, sm, target);
             trace_mark(a, tk);
         }
         if (!alive) break;
         // classifier + greedy argmax
-        if (tp)
-            stage_sum(a.rms_final);
-        else
-            stage_act<WT, DEC_STAGE_V>(Float4Src{x4, true}, a.dim, a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
+        stage_act<WT, DEC_STAGE_V>(Float4Src{tp ? reinterpret_cast<const float4 *>(xcur) : x4, true}, a.dim,
+                                   a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
         best = 0ull;
         trace_mark(a, tk);
         const WDesc &wc = sm.wd[4 * a.n_layers];
@@ -858,7 +893,7 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
         }
         // tensor parallelism: the logits rows go to every rank and the key is
         // maxed into every rank's word (thread 0 holds the CTA's key)
-        if (!(tp ? tp_sync(a, sm, xtarget, &wc, true, 0, mk) : grid_sync(a, sm, target))) break;
+        if (!(tp ? tp_sync(a, sm, xtarget, wc, mk) : grid_sync(a, sm, target))) break;
         if (blockIdx.x == 0 && tid == 0) {
             const unsigned long long k = atomicAdd(a.argmax, 0ull);
             int idx = 0x7fffffff - (int)(uint32_t)(k & 0xffffffffu);
@@ -961,7 +996,9 @@ int decode_prepare(LlmModel *m)
     if (c.tp_size > 1) {
         const int R = DEC_GW * DEC_RPW, grid = matvec_num_sms();
         const int rows = std::max(c.dim, m->vocab_loc);
-        push = (uint32_t)round_up((size_t)cdiv(cdiv(rows, R), grid) * R * 4, 128);
+        const size_t tiles = (size_t)cdiv(cdiv(rows, R), grid) * R;                    // rows of the CTA's tiles
+        const size_t slice = (size_t)cdiv(c.dim, grid) * c.tp_size;                    // its slice, every rank
+        push = (uint32_t)round_up(std::max(tiles, slice) * 4, 128);
     }
     const size_t cap = 227 * 1024;
     const size_t fixed = decode_smem_bytes((int)v.size(), 0, slot, xs, push);
@@ -1069,6 +1106,7 @@ cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, uns
     a.tp_rank = 0;
     a.vocab_off = 0;
     a.tp_epoch = 0;
+    a.tp_seq = 1;
     a.tp_logits_off = 0;
     a.x_alt = m->x2;
     a.push_bytes = m->dec_push;
@@ -1079,6 +1117,7 @@ cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, uns
         a.tp_rank = c.tp_rank;
         a.vocab_off = m->vocab_off;
         a.tp_epoch = m->tp_epoch;
+        a.tp_seq = m->tp_seq;
         a.tp_logits_off = TpXchg::logits(c.tp_size, c.dim);
         for (int r = 0; r < c.tp_size; r++) a.tp_peer[r] = m->tp_peer[r];
         a.argmax = reinterpret_cast<unsigned long long *>(m->tp_xchg + TpXchg::argmax);
@@ -1097,10 +1136,13 @@ cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, uns
                         : launch_decode_t<W_Q8_0, false>(a, smem, grid, m->stream); break;
     default: return cudaErrorInvalidValue;
     }
-    // every step of a launch runs 2 exchanges per layer and the classifier's,
-    // each counting one arrival per CTA of every rank on every rank
-    if (e == cudaSuccess && c.tp_size > 1)
-        m->tp_epoch += (unsigned)steps * (unsigned)(2 * c.n_layers + 1) * (unsigned)grid;
+    // every step of a launch runs 2 tagged exchanges per layer and the
+    // classifier's counted barrier (one arrival per CTA of every rank)
+    if (e == cudaSuccess && c.tp_size > 1) {
+        m->tp_epoch += (unsigned)steps * (unsigned)grid;
+        m->tp_seq += (unsigned)steps * (unsigned)(2 * c.n_layers);
+        if (m->tp_seq == 0) m->tp_seq = 1;   // the buffer starts zeroed: tag 0 never marks a current word
+    }
     return e;
 }
 

@@ -101,16 +101,17 @@ struct LlmModel {
     uint8_t *tp_xchg = nullptr;           // this rank's buffer (cudaMalloc, exported)
     uint8_t *tp_peer[TP_MAX_RANKS] = {};  // rank r's buffer in this process (tp_peer[tp_rank] = tp_xchg)
     bool tp_p2p = false;                  // ranks on distinct GPUs, buffers mapped: the persistent engine may run
-    unsigned int tp_epoch = 0;            // arrivals per source rank counted by the launches so far (wraps)
+    unsigned int tp_epoch = 0;            // classifier arrivals per source rank counted so far (wraps)
+    unsigned int tp_seq = 1;              // tag of the next partial-row exchange (wraps, never 0)
     float *logits_own = nullptr;          // the model's own logits buffer while m->logits points into tp_xchg
 };
 
 // offsets into a tensor-parallel exchange buffer (LlmModel::tp_xchg)
 struct TpXchg {
-    static constexpr size_t bar = 0;         // unsigned int [TP_MAX_RANKS]: arrivals from each source rank
+    static constexpr size_t bar = 0;         // unsigned int [TP_MAX_RANKS]: classifier arrivals per source rank
     static constexpr size_t argmax = 128;    // unsigned long long: greedy key, max over every rank's rows
-    static constexpr size_t recv = 256;      // float [2][tp_size][dim]: partial rows of wo / w2
-    static size_t logits(int tp_size, int dim) { return recv + round_up((size_t)2 * tp_size * dim * 4, 256); }
+    static constexpr size_t recv = 256;      // u64 [2][tp_size][dim]: partial rows of wo / w2, tagged words
+    static size_t logits(int tp_size, int dim) { return recv + round_up((size_t)2 * tp_size * dim * 8, 256); }
     static size_t bytes(int tp_size, int dim, int vocab) { return logits(tp_size, dim) + round_up((size_t)vocab * 4, 256); }
 };
 

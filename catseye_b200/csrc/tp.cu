@@ -172,6 +172,7 @@ int tp_map_peers(LlmModel *m, TpComm *t)
     m->logits_own = m->logits;
     m->logits = reinterpret_cast<float *>(m->tp_xchg + TpXchg::logits(n, c.dim));
     m->tp_epoch = 0;
+    m->tp_seq = 1;
     m->tp_p2p = true;
     return E_OK;
 }
@@ -193,6 +194,7 @@ int tp_loopback(LlmModel *m)
     m->logits_own = m->logits;
     m->logits = reinterpret_cast<float *>(m->tp_xchg + TpXchg::logits(c.tp_size, c.dim));
     m->tp_epoch = 0;
+    m->tp_seq = 1;
     m->tp_p2p = true;
     return E_OK;
 }

@@ -127,6 +127,10 @@ void *ref_llm_load(const char *path, int fmt, int *hp)
     ref_model *r = calloc(1, sizeof(ref_model));
     cats_llm_model *m = &r->m;
     int rc = 0;
+    /* the runtime's global dequantizer starts as the plain copy (catseye_llm.h:521);
+     * the GGUF and ggml loaders reassign it, the .bin loader relies on the
+     * default: restore it, as a fresh process would have it */
+    dequantize = _dequantize_memcpy;
     if (fmt == 1) rc = cats_gguf_load((char *)path, m);
     else if (fmt == 2) rc = cats_ggml_load((char *)path, m);
     else rc = cats_checkpoint_load((char *)path, m) > 0 ? 0 : 1;

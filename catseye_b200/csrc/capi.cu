@@ -194,6 +194,8 @@ namespace cats {
 // the sticky status, for entry points defined in other files
 int capi_fail(int code, const char *what) { return fail(code, what); }
 int noalloc_device_error(bool clear);   // noalloc.cu: the no-allocation sgemm's status word
+// the library's stream (after cats_gpu_init), for entry points in other files
+cudaStream_t capi_stream() { return g.stream; }
 }
 
 // ===================================================================== C ABI

@@ -17,6 +17,7 @@
 
 namespace cats {
 int capi_fail(int code, const char *what);
+cudaStream_t capi_stream();
 }
 using namespace cats;
 
@@ -64,20 +65,27 @@ void cats_ocl_free(void *p)
     g_npending = 0;
 }
 
+// Copies go on the library's stream, the one the GEMMs run on, and are waited
+// for: a plain cudaMemcpy from pageable memory may return before its data has
+// landed, and it is not ordered with that (non-blocking) stream.
 int cats_ocl_write(void *buf, size_t off, size_t size, const void *host)
 {
     if (!buf || !host) return capi_fail(CATS_ERR_ARG, "cats_ocl_write");
-    return cudaMemcpy(static_cast<uint8_t *>(buf) + off, host, size, cudaMemcpyHostToDevice) == cudaSuccess
-               ? CATS_OK
-               : capi_fail(CATS_ERR_CUDA, "cats_ocl_write");
+    cudaStream_t st = capi_stream();
+    const bool ok = cudaMemcpyAsync(static_cast<uint8_t *>(buf) + off, host, size, cudaMemcpyHostToDevice, st) ==
+                        cudaSuccess &&
+                    cudaStreamSynchronize(st) == cudaSuccess;
+    return ok ? CATS_OK : capi_fail(CATS_ERR_CUDA, "cats_ocl_write");
 }
 
 int cats_ocl_read(void *buf, size_t off, size_t size, void *host)
 {
     if (!buf || !host) return capi_fail(CATS_ERR_ARG, "cats_ocl_read");
-    return cudaMemcpy(host, static_cast<const uint8_t *>(buf) + off, size, cudaMemcpyDeviceToHost) == cudaSuccess
-               ? CATS_OK
-               : capi_fail(CATS_ERR_CUDA, "cats_ocl_read");
+    cudaStream_t st = capi_stream();
+    const bool ok = cudaMemcpyAsync(host, static_cast<const uint8_t *>(buf) + off, size, cudaMemcpyDeviceToHost, st) ==
+                        cudaSuccess &&
+                    cudaStreamSynchronize(st) == cudaSuccess;
+    return ok ? CATS_OK : capi_fail(CATS_ERR_CUDA, "cats_ocl_read");
 }
 
 int cats_ocl_run(const char *kernel, void *buf, const int *info, const float *param)
@@ -100,13 +108,13 @@ int cats_ocl_run(const char *kernel, void *buf, const int *info, const float *pa
                                 param[1], gm + info[5], N, nullptr);
         g_npending = 0;
         if (rc) return rc;
-        return cudaDeviceSynchronize() == cudaSuccess ? CATS_OK : capi_fail(CATS_ERR_CUDA, "cats_ocl_run");
+        return cudaStreamSynchronize(capi_stream()) == cudaSuccess ? CATS_OK : capi_fail(CATS_ERR_CUDA, "cats_ocl_run");
     }
     if (!strcmp(kernel, "im2col")) {   // sgemm_ocl2.h:128-168 (square kernel, pad and stride)
         int rc = cats_im2col_dev(gm + info[0], info[1], info[2], info[3], info[4], info[4], info[5], info[5], info[6],
                                  info[6], gm + info[7], nullptr);
         if (rc) return rc;
-        return cudaDeviceSynchronize() == cudaSuccess ? CATS_OK : capi_fail(CATS_ERR_CUDA, "cats_ocl_run");
+        return cudaStreamSynchronize(capi_stream()) == cudaSuccess ? CATS_OK : capi_fail(CATS_ERR_CUDA, "cats_ocl_run");
     }
     return capi_fail(CATS_ERR_UNSUPPORTED, "cats_ocl_run: kernel name");
 }

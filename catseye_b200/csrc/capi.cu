@@ -279,7 +279,9 @@ int cats_gpu_register_weight(const void *w, int type, int n, int d)
         r.W.L.d = d;
         r.W.L.total_bytes = bytes;
         if (cudaMalloc(&r.W.ptr, bytes) != cudaSuccess) return fail(CATS_ERR_NOMEM, "cats_gpu_register_weight");
-        int rc = check(cudaMemcpy(r.W.ptr, w, bytes, cudaMemcpyHostToDevice), "cats_gpu_register_weight");
+        // on the library's stream and waited for: the matvecs read it from that stream
+        int rc = check(cudaMemcpyAsync(r.W.ptr, w, bytes, cudaMemcpyHostToDevice, g.stream), "cats_gpu_register_weight");
+        if (!rc) rc = check(cudaStreamSynchronize(g.stream), "cats_gpu_register_weight");
         if (rc) { cudaFree(r.W.ptr); return rc; }
         g.weights[w] = r;
         return CATS_OK;

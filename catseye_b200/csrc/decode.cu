@@ -1070,7 +1070,9 @@ int decode_prepare(LlmModel *m)
         if (wd) cudaFree(wd);
         return E_NOMEM;
     }
-    if (cudaMemcpy(wd, v.data(), v.size() * sizeof(WDesc), cudaMemcpyHostToDevice) != cudaSuccess) {
+    // on the model's (non-blocking) stream and waited for, before any launch reads it
+    if (cudaMemcpyAsync(wd, v.data(), v.size() * sizeof(WDesc), cudaMemcpyHostToDevice, m->stream) != cudaSuccess ||
+        cudaStreamSynchronize(m->stream) != cudaSuccess) {
         cudaFree(wd);
         return E_CUDA;
     }

@@ -133,7 +133,7 @@ int tp_map_peers(LlmModel *m, TpComm *t)
     // and the caller has to tear down every rank: the others wait in NCCL)
     if (cudaMalloc(&d, sizeof(PeerInfo) * n) != cudaSuccess) return E_NOMEM;
     std::vector<PeerInfo> all(n);
-    cudaError_t e = cudaMemcpy(d + c.tp_rank, &me, sizeof me, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpyAsync(d + c.tp_rank, &me, sizeof me, cudaMemcpyHostToDevice, m->stream);
     ncclResult_t nr = nccl().all_gather(d + c.tp_rank, d, sizeof(PeerInfo), ncclUint8, t->comm, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e == cudaSuccess) e = cudaMemcpy(all.data(), d, sizeof(PeerInfo) * n, cudaMemcpyDeviceToHost);
@@ -159,7 +159,7 @@ int tp_map_peers(LlmModel *m, TpComm *t)
     int *v = nullptr;
     int verdict = use ? 0 : 1;
     if (cudaMalloc(&v, 4) != cudaSuccess) { unmap_peers(m); return E_NOMEM; }
-    cudaMemcpy(v, &verdict, 4, cudaMemcpyHostToDevice);
+    cudaMemcpyAsync(v, &verdict, 4, cudaMemcpyHostToDevice, m->stream);   // ordered before the collective
     nr = nccl().all_reduce(v, v, 1, ncclInt32, ncclSum, t->comm, m->stream);
     e = cudaStreamSynchronize(m->stream);
     if (e == cudaSuccess) e = cudaMemcpy(&verdict, v, 4, cudaMemcpyDeviceToHost);

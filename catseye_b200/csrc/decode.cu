@@ -68,7 +68,6 @@ constexpr int DEC_MAX_HS = 128;                               // head size held 
 constexpr int DEC_STAGE_V = 4;                                // staging loads in flight per thread (512 threads)
 constexpr int DEC_STAGE_V_WIDE = 6;                           // the same without rmsnorm: the hidden vector in one pass
 constexpr uint32_t DEC_HEADER = 1024;                         // mbarriers + scratch at the start of smem
-constexpr uint32_t DEC_SSQ_OFF = 832;                         // the warps' sums of squares in the header
 constexpr uint32_t GRID_SPIN_LIMIT = 1u << 22;                // polls of ~0.5-1 us each (with a 50 ns pause): seconds at most
 
 // One weight in the tile-chunk layout (16-row tiles, 64-unit segments).
@@ -107,12 +106,6 @@ struct DecodeArgs {
     uint8_t *tp_peer[TP_MAX_RANKS];       // rank r's exchange buffer, mapped here (this rank's at tp_rank)
     unsigned long long tp_logits_off;     // byte offset of the logits in an exchange buffer
     float *x_alt;                         // the residual stream alternates between x and x_alt
-    // Sums of squares of the residual stream, per CTA, written at the grid
-    // barrier after each phase that updates it ([2][grid]: after wo, after
-    // w2): the next rmsnorm adds them up instead of reducing over its staged
-    // vector.  pre_ssq = 0 keeps the in-staging reduction.
-    float *ssq;
-    int pre_ssq;
     uint32_t push_bytes;                  // shared memory for the CTA's rows to push
 };
 
@@ -164,7 +157,6 @@ struct Smem {
     volatile int *sync_ok;   // grid_sync's decision, written by thread 0 between its two CTA barriers
     WDesc *wd;               // the weight descriptors, copied in at the start (global reads cost microseconds)
     float *push;             // tensor parallelism: this CTA's rows of the phase, 16 per tile it owns
-    float *ssq_w;            // per consumer warp: sum of squares of the residual rows it wrote this phase
 };
 
 __host__ __device__ inline size_t desc_bytes(int n_wd)
@@ -180,15 +172,13 @@ __device__ __forceinline__ Smem smem_layout(uint8_t *base, const DecodeArgs &a)
     s.red = reinterpret_cast<float *>(s.empty + DEC_GROUPS * DEC_MAX_STAGES);   // 64 floats (16 u64 keys at +32)
     s.abort_s = reinterpret_cast<volatile int *>(s.red + 64);
     s.sync_ok = s.abort_s + 1;
-    s.ssq_w = reinterpret_cast<float *>(base + DEC_SSQ_OFF);
     s.wd = reinterpret_cast<WDesc *>(base + DEC_HEADER);
     s.ring = base + DEC_HEADER + desc_bytes(a.n_wd);
     s.xs = s.ring + (size_t)DEC_GROUPS * a.stages * a.slot_bytes;
     s.push = reinterpret_cast<float *>(s.xs + a.xs_bytes);
     return s;
 }
-static_assert(2 * DEC_GROUPS * DEC_MAX_STAGES * 8 + 64 * 4 + 8 <= DEC_SSQ_OFF, "smem header overflow");
-static_assert(DEC_SSQ_OFF + DEC_WARPS * 4 <= DEC_HEADER, "smem header overflow");
+static_assert(2 * DEC_GROUPS * DEC_MAX_STAGES * 8 + 64 * 4 + 8 <= DEC_HEADER, "smem header overflow");
 static_assert(sizeof(WDesc) % 16 == 0, "descriptors are copied as 16-byte words");
 
 size_t decode_smem_bytes(int n_wd, int stages, uint32_t slot, uint32_t xs, uint32_t push = 0)
@@ -200,21 +190,11 @@ size_t decode_smem_bytes(int n_wd, int stages, uint32_t slot, uint32_t xs, uint3
 // this or another CTA gave up waiting; every consumer thread of the CTA gets
 // the same answer (thread 0 decides and publishes it between two CTA
 // barriers), so the CTA's warps always leave the step loop together.
-// ssq_dst (may be null): this CTA's sum of squares of the residual rows its
-// warps wrote in the phase (sm.ssq_w, added in warp order) goes to
-// ssq_dst[blockIdx.x] before the arrival, so the next phase's rmsnorm can
-// read every CTA's part.
-__device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, unsigned &target,
-                                          float *ssq_dst = nullptr)
+__device__ __forceinline__ bool grid_sync(const DecodeArgs &a, const Smem &sm, unsigned &target)
 {
     named_bar_sync(1, DEC_NC);
     if (threadIdx.x == 0) {
         bool ok = *sm.abort_s == 0;
-        if (ssq_dst) {
-            float t = 0.f;
-            for (int w = 0; w < DEC_WARPS; w++) t += sm.ssq_w[w];
-            __stcg(ssq_dst + blockIdx.x, t);
-        }
         if (ok) {
             target += gridDim.x;
             // the release covers the CTA's writes ordered before it by the CTA
@@ -333,15 +313,11 @@ __device__ __forceinline__ bool tp_exchange(const DecodeArgs &a, const Smem &sm,
         *sm.abort_s = 1;
     }
     named_bar_sync(1, DEC_NC);
-    float ssq = 0.f;
     for (int t = threadIdx.x; t < r1 - r0 && *sm.abort_s == 0; t += DEC_NC) {
         float s = __ldcg(xcur + r0 + t);
         for (int r = 0; r < a.tp_size; r++) s = __fadd_rn(s, sm.push[t * a.tp_size + r]);
         xnext[r0 + t] = s;
-        ssq = fmaf(s, s, ssq);
     }
-    ssq = warp_sum(ssq);
-    if ((threadIdx.x & 31) == 0) sm.ssq_w[threadIdx.x >> 5] = ssq;   // the slice's squares, for the next rmsnorm
     return *sm.abort_s == 0;
 }
 
@@ -503,7 +479,6 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
     // tracing: when thread 0 first had a chunk, and when it finished its last dot
     unsigned long long ns_first = 0, ns_dots = 0;
     long long ck_first = 0, ck_dots = 0;
-    float ssq = 0.f;   // DE_ADD: squares of the residual rows this warp writes (lane 0)
     for (int p = 0; 2 * p + grp < nt && ok; p++) {
         const int t = blockIdx.x + (2 * p + grp) * gridDim.x;
         {
@@ -544,14 +519,8 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
                             c[1] = v1;
                         }
                     } else if (epi == DE_ADD) {   // residual (:1731-1733, :1759-1761)
-                        const float x0 = xr[0] + v0;
-                        a.x[row0] = x0;
-                        ssq = fmaf(x0, x0, ssq);
-                        if (row0 + 1 < W.d) {
-                            const float x1 = xr[1] + v1;
-                            a.x[row0 + 1] = x1;
-                            ssq = fmaf(x1, x1, ssq);
-                        }
+                        a.x[row0] = xr[0] + v0;
+                        if (row0 + 1 < W.d) a.x[row0 + 1] = xr[1] + v1;
                     } else if (epi == DE_PUSH) {
                         float *pr = sm.push + (2 * p + grp) * R + gw * DEC_RPW;
                         pr[0] = v0;
@@ -577,7 +546,6 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
             }
         }
     }
-    if (epi == DE_ADD && lane == 0) sm.ssq_w[warp] = ssq;   // every warp, also one without tiles
     trace_put(a, tk, ns_first, ck_first);
     trace_put(a, tk, ns_dots, ck_dots);
     return ok;
@@ -834,19 +802,15 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
     unsigned seq = a.tp_seq;               // tensor parallelism: the next exchange's tag
     int tk = 0;
     // the exchange after wo / w2, then the grid barrier that publishes the new residual stream
-    auto exchange = [&](const WDesc &W, float *ssq_dst) -> bool {
+    auto exchange = [&](const WDesc &W) -> bool {
         const bool ok = tp_exchange(a, sm, W, slot, seq, xcur, xnext);
         float *t = xcur;
         xcur = xnext;
         xnext = t;
         slot ^= 1;
         seq++;
-        return grid_sync(a, sm, target, ssq_dst) && ok;
+        return grid_sync(a, sm, target) && ok;
     };
-    // sums of squares of the residual stream: after wo (read by the w1/w3
-    // rmsnorm), after w2 (read by the next qkv rmsnorm and the final one)
-    float *const ssq_wo = a.pre_ssq ? a.ssq : nullptr;
-    float *const ssq_w2 = a.pre_ssq ? a.ssq + gridDim.x : nullptr;
     trace_mark(a, tk);
     for (int step = 0; step < a.steps; step++) {
         const int pos = ld_volatile_i32(&a.params->pos);
@@ -866,8 +830,7 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
                                            a.dim, a.rms_att, blockIdx.x == 0 ? xcur : nullptr, sm.xs, sm.red, tid, DEC_NC);
             else
                 stage_act<WT, DEC_STAGE_V>(Float4Src{tp ? reinterpret_cast<const float4 *>(xcur) : x4, true}, a.dim,
-                                           a.rms_att + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid, DEC_NC, ssq_w2,
-                                           gridDim.x);
+                                           a.rms_att + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[0], rg, DE_QKV, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
@@ -891,13 +854,12 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[1], rg, tp ? DE_PUSH : DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
-            if (!(alive = tp ? exchange(wl[1], ssq_wo) : grid_sync(a, sm, target, ssq_wo))) break;
+            if (!(alive = tp ? exchange(wl[1]) : grid_sync(a, sm, target))) break;
             trace_mark(a, tk);
             if (!tp) residual_first(a, wl[3], xr);   // x is final until the w2 epilogue
             // w1/w3 + SwiGLU
             stage_act<WT, DEC_STAGE_V>(Float4Src{tp ? reinterpret_cast<const float4 *>(xcur) : x4, true}, a.dim,
-                                       a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid, DEC_NC, ssq_wo,
-                                       gridDim.x);
+                                       a.rms_ffn + (size_t)l * a.dim, nullptr, sm.xs, sm.red, tid, DEC_NC);
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[2], rg, DE_SWIGLU, l, pos, best, tk, no_rows);
             trace_mark(a, tk);
@@ -909,13 +871,13 @@ __device__ __forceinline__ void consume(const DecodeArgs &a, const Smem &sm)
             trace_mark(a, tk);
             run_matvec<WT>(a, sm, wl[3], rg, tp ? DE_PUSH : DE_ADD, l, pos, best, tk, xr);
             trace_mark(a, tk);
-            alive = tp ? exchange(wl[3], ssq_w2) : grid_sync(a, sm, target, ssq_w2);
+            alive = tp ? exchange(wl[3]) : grid_sync(a, sm, target);
             trace_mark(a, tk);
         }
         if (!alive) break;
         // classifier + greedy argmax
         stage_act<WT, DEC_STAGE_V>(Float4Src{tp ? reinterpret_cast<const float4 *>(xcur) : x4, true}, a.dim,
-                                   a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC, ssq_w2, gridDim.x);
+                                   a.rms_final, nullptr, sm.xs, sm.red, tid, DEC_NC);
         best = 0ull;
         trace_mark(a, tk);
         const WDesc &wc = sm.wd[4 * a.n_layers];
@@ -1061,11 +1023,6 @@ int decode_prepare(LlmModel *m)
     bool ok = cudaMalloc(&wd, v.size() * sizeof(WDesc)) == cudaSuccess;
     ok = ok && (m->dec_part || cudaMalloc(&m->dec_part, part_bytes) == cudaSuccess);
     ok = ok && (m->dec_bar || cudaMalloc(&m->dec_bar, 16) == cudaSuccess);
-    ok = ok && (m->dec_ssq || cudaMalloc(&m->dec_ssq, (size_t)2 * matvec_num_sms() * 4) == cudaSuccess);
-    // the rmsnorms add the per-CTA sums of squares the barriers wrote
-    // (CATS_DECODE_PRE_SSQ=0: reduce over the staged vector instead; tuning)
-    const char *ps = getenv("CATS_DECODE_PRE_SSQ");
-    m->dec_pre_ssq = !(ps && atoi(ps) == 0);
     if (!ok) {
         if (wd) cudaFree(wd);
         return E_NOMEM;
@@ -1154,8 +1111,6 @@ cudaError_t decode_launch(LlmModel *m, int steps, int *tok_log, int tok_cap, uns
     a.tp_seq = 1;
     a.tp_logits_off = 0;
     a.x_alt = m->x2;
-    a.ssq = m->dec_ssq;
-    a.pre_ssq = m->dec_pre_ssq;
     a.push_bytes = m->dec_push;
     for (int r = 0; r < TP_MAX_RANKS; r++) a.tp_peer[r] = nullptr;
     if (c.tp_size > 1) {

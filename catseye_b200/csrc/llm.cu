@@ -338,8 +338,6 @@ void llm_free(LlmModel *m)
     if (m->wdesc) cudaFree(m->wdesc);
     if (m->dec_part) cudaFree(m->dec_part);
     if (m->dec_bar) cudaFree(m->dec_bar);
-    if (m->dec_ssq) cudaFree(m->dec_ssq);
-    m->dec_ssq = nullptr;
     m->wdesc = nullptr;
     m->dec_part = nullptr;
     m->dec_bar = nullptr;

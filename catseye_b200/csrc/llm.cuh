@@ -66,8 +66,6 @@ struct LlmModel {
     unsigned int *dec_bar = nullptr;      // [0] grid barrier counter, [1] abort flag
     int dec_stages = 0, dec_max_splits = 32;
     uint32_t dec_slot = 0, dec_xs = 0, dec_push = 0;
-    float *dec_ssq = nullptr;             // per-CTA sums of squares of the residual stream [2][grid]
-    int dec_pre_ssq = 1;
     // batched step (batch.cu): prefill and batched decode on the tensor cores
     int n_seqs = 1;                       // KV sequences: kcache is [seq][layer][seq_len][kv_dim]
     int bt_cap = 0;                       // tokens per batched step (0: not reserved)

@@ -78,13 +78,9 @@ struct Float4Src {
 constexpr int STAGE_V = 8;
 
 // NORM = false compiles the form without rmsnorm (norm_w must be null).
-// pre_ssq (may be null, with rmsnorm): n_pre partial sums of squares of x
-// (one per CTA of the kernel that wrote x): their total replaces the
-// reduction over the staged vector; every warp adds them in the same order.
 template <int WT, int V = STAGE_V, bool NORM = true, class Src>
 __device__ __forceinline__ void stage_act(const Src &src, int n, const float *norm_w, float *writeback,
-                                          uint8_t *xs, float *red, int tid, int nthr, const float *pre_ssq = nullptr,
-                                          int n_pre = 0)
+                                          uint8_t *xs, float *red, int tid, int nthr)
 {
     if (!NORM) norm_w = nullptr;
     const int lane = tid & 31, warp = tid >> 5;
@@ -102,24 +98,17 @@ __device__ __forceinline__ void stage_act(const Src &src, int n, const float *no
             const int i = base + tid + k * nthr;
             g[k] = (norm_w && i < n4) ? nw4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
         }
-        float pre = 0.f;
-        if (NORM && pre_ssq && norm_w)
-            for (int k = lane; k < n_pre; k += 32) pre += __ldcg(pre_ssq + k);
         src.template fill<V>(v, base + tid, nthr, n4);
         float scale = 1.f;
         if (norm_w) {
-            float tot = 0.f;
-            if (pre_ssq) {
-                tot = warp_sum(pre);
-            } else {
-                float ss = 0.f;
+            float ss = 0.f;
 #pragma unroll
-                for (int k = 0; k < V; k++) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
-                ss = warp_sum(ss);
-                if (lane == 0) red[warp] = ss;
-                named_bar_sync(1, nthr);
-                for (int w = 0; w < nthr / 32; w++) tot += red[w];
-            }
+            for (int k = 0; k < V; k++) ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            named_bar_sync(1, nthr);
+            float tot = 0.f;
+            for (int w = 0; w < nthr / 32; w++) tot += red[w];
             tot = __fdiv_rn(tot, (float)n);
             tot = __fadd_rn(tot, 1e-5f);
             scale = __fdiv_rn(1.f, __fsqrt_rn(tot));

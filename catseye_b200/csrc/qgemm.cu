@@ -33,6 +33,14 @@
 #include "qgemm.cuh"
 #include "tc.cuh"
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <array>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 namespace cats {
 
@@ -354,6 +362,232 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
     }
 }
 
+// ---------------------------------------------------------------------------
+// Q4_0 weights through the tensor-memory-access engine.  The producers above
+// fetch weight words with ordinary loads, which cap near 8 GB/s per SM (the
+// few bytes one SM keeps in flight at the loaded latency); at small T that is
+// the bound.  Here a warp of its own (the TMA warp) brings 4 K slices of a
+// 128-row tile at a time straight from the matvec's tile layout into a ring
+// of raw stages: the codes with one 4-D tensor-map copy (128 bytes of each
+// row's segment x 16 rows x 1 segment x 8 tiles, 128-byte swizzled so the
+// producers' reads are conflict-free) and the fp16 scales with another (16
+// bytes x 16 x 1 x 8).  A weight whose last segment is short has a second
+// pair of maps for that segment; coordinates past its end read zeros.  The
+// producers dequantize from shared memory as before; the MMA warp and the
+// epilogue are unchanged.
+constexpr int QT_THREADS = QG_PROD + 64;      // + the MMA warp + the TMA warp
+constexpr int QT_TMA_WARP = QG_MMA_WARP + 1;
+constexpr int QT_GROUP = 4;                    // K slices per raw stage
+constexpr uint32_t QT_CODE_BYTES = QG_M * 128;   // 128 rows x 4 slices x 32 bytes
+constexpr uint32_t QT_SCALE_BYTES = QG_M * 16;   // 128 rows x 4 slices x 2 blocks x 2 bytes
+constexpr uint32_t QT_RAW_BYTES = QT_CODE_BYTES + QT_SCALE_BYTES;
+
+__host__ __device__ constexpr int qt_raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 6; }
+
+struct QgemmTmaArgs {
+    CUtensorMap codes, scales;             // full segments
+    CUtensorMap codes_tail, scales_tail;   // the short last segment (when there is one)
+    int full_segs;                         // segments of MV_SEG_UNITS units
+    int n, d, T, Tpad, kper, splits, accumulate;
+    const __half *x;
+    float *y, *ws;
+    int *err;
+};
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+          "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <int BN>
+__global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_constant__ QgemmTmaArgs a)
+{
+    constexpr int ST = qg_stages(BN);
+    constexpr int RS = qt_raw_stages(BN);
+    constexpr uint32_t B_BYTES = BN * 128;
+    constexpr uint32_t STAGE = QG_A_BYTES + B_BYTES;
+    constexpr int TCOLS = BN < 32 ? 32 : BN;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+    uint8_t *rawst = smem + ST * STAGE;                 // RS raw stages: codes then scales
+    uint64_t *full = reinterpret_cast<uint64_t *>(rawst + RS * QT_RAW_BYTES);
+    uint64_t *empty = full + ST;
+    uint64_t *rfull = empty + ST;
+    uint64_t *rempty = rfull + RS;
+    uint64_t *done = rempty + RS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *commits = const_cast<int *>(abort_s) + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * BN, m0 = blockIdx.y * QG_M, z = blockIdx.z;
+    const int ksteps = a.n / QG_K;
+    const int kbeg = z * a.kper, nk = max(0, min(ksteps, kbeg + a.kper) - kbeg);
+    const int ngroups = (nk + QT_GROUP - 1) / QT_GROUP;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; s++) {
+            mbar_init(&full[s], QG_PROD / 32);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < RS; s++) {
+            mbar_init(&rfull[s], 1);
+            mbar_init(&rempty[s], QG_PROD / 32);   // every producer warp, after its last read of the stage
+        }
+        mbar_init(done, 1);
+        *abort_s = 0;
+        for (int s = 0; s < ST; s++) commits[s] = 0;
+        fence_barrier_init();
+    }
+    if (warp == QG_MMA_WARP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TCOLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == QT_TMA_WARP) {
+        // ---------------- raw weight stages through the TMA engine
+        if (lane == 0) {
+            int issued = 0;
+            for (int g = 0; g < ngroups; g++) {
+                const int rs = g % RS;
+                const uint32_t rph = (uint32_t)(g / RS) & 1u;
+                if (!tc_wait(&rempty[rs], rph ^ 1u, abort_s, a.err, CATS_DEVERR_MBAR_EMPTY)) break;
+                const int slice = kbeg + g * QT_GROUP;
+                const int seg = slice / (MV_SEG_UNITS / 2), in_seg = slice % (MV_SEG_UNITS / 2);
+                const bool tail = seg >= a.full_segs;
+                uint8_t *dst = rawst + rs * QT_RAW_BYTES;
+                mbar_arrive_expect_tx(&rfull[rs], QT_RAW_BYTES);
+                tma_load_4d(dst, tail ? &a.codes_tail : &a.codes, in_seg * 32, 0, tail ? 0 : seg, m0 / 16, &rfull[rs]);
+                tma_load_4d(dst + QT_CODE_BYTES, tail ? &a.scales_tail : &a.scales, in_seg * 4, 0, tail ? 0 : seg,
+                            m0 / 16, &rfull[rs]);
+                issued = g + 1;
+            }
+            // every copy lands before the CTA exits (the last phase of each stage)
+            for (int g = max(0, issued - RS); g < issued; g++)
+                mbar_wait_bounded(&rfull[g % RS], (uint32_t)(g / RS) & 1u, nullptr, 0);
+        }
+    } else if (warp == QG_MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc(0, QG_M, BN);
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % ST;
+                const uint32_t ph = (uint32_t)(kb / ST) & 1u;
+                if (!tc_wait(&full[s], ph, abort_s, a.err, CATS_DEVERR_MBAR_FULL)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + QG_A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < QG_K / 16; kk++) {
+                    const uint64_t da = umma_desc_sw128(sa + kk * 32), db = umma_desc_sw128(sb + kk * 32);
+                    const uint32_t acc = (kb | kk) != 0;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\t"
+                        "setp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+                        ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u)
+                        : "memory");
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                             ::"r"(smem_u32(&empty[s])) : "memory");
+                commits[s]++;
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"(smem_u32(done)) : "memory");
+        }
+    } else {
+        // ---------------- producers: thread p dequantizes block p & 1 of row p >> 1 from the raw stage
+        const int p = threadIdx.x, r = p >> 1, h = p & 1;
+        uint32_t off[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) off[i] = sw128(r, 4 * h + i);
+        int s = 0;
+        uint32_t ph = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int g = kb / QT_GROUP, k4 = kb % QT_GROUP, rs = g % RS;
+            if (k4 == 0 && !tc_wait(&rfull[rs], (uint32_t)(g / RS) & 1u, abort_s, a.err, CATS_DEVERR_MBAR_FULL)) break;
+            if (!tc_wait(&empty[s], ph ^ 1u, abort_s, a.err, CATS_DEVERR_MBAR_EMPTY)) break;
+            uint8_t *sa = smem + s * STAGE, *sb = sa + QG_A_BYTES;
+            if (p == 0) bulk_g2s_keep(sb, a.x + ((size_t)(kbeg + kb) * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
+            const uint8_t *rb = rawst + rs * QT_RAW_BYTES;
+            RawBlk blk;
+            // the codes of this slice's block: 16-byte chunk 2 k4 + h of row r, 128-byte swizzled by the copy
+            blk.w[0] = *reinterpret_cast<const uint4 *>(rb + r * 128 + (((2 * k4 + h) ^ (r & 7)) << 4));
+            blk.sc = *reinterpret_cast<const unsigned short *>(rb + QT_CODE_BYTES + r * 16 + k4 * 4 + h * 2);
+            dequant_store<W_Q4_0>(blk, sa, off);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
+                else mbar_arrive(&full[s]);
+                if (k4 == QT_GROUP - 1 || kb == nk - 1) mbar_arrive(&rempty[rs]);   // the warp is done with it
+            }
+            if (++s == ST) { s = 0; ph ^= 1u; }
+        }
+        bool ok = false;
+        for (uint32_t i = 0; i < CATS_SPIN_LIMIT; i++) {
+            if (mbar_try_wait(done, 0)) { ok = true; break; }
+            if (i > 64) __nanosleep(32);
+        }
+        if (!ok && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_FULL);
+        tc_fence_after();
+        if (ok && !*abort_s && nk > 0) {
+            const int q = warp & 3, half = warp >> 2;
+            const int orow = m0 + q * 32 + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+            float *out = a.splits > 1 ? a.ws + (size_t)z * a.T * a.d : a.y;
+            const bool acc = a.splits == 1 && a.accumulate;
+#pragma unroll 1
+            for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 8) {
+                uint32_t v[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                               "=r"(v[7])
+                             : "r"(taddr + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (orow < a.d) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int tok = t0 + c0 + j;
+                        if (tok < a.T) {
+                            float *yp = out + (size_t)tok * a.d + orow;
+                            *yp = acc ? *yp + __uint_as_float(v[j]) : __uint_as_float(v[j]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == QG_MMA_WARP) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; s++)
+            if (commits[s] > 0) mbar_wait_bounded(&empty[s], (uint32_t)(commits[s] - 1) & 1u, nullptr, 0);
+        for (int s = 0; s < ST; s++) {
+            mbar_inval(&full[s]);
+            mbar_inval(&empty[s]);
+        }
+        for (int s = 0; s < RS; s++) {
+            mbar_inval(&rfull[s]);
+            mbar_inval(&rempty[s]);
+        }
+        mbar_inval(done);
+    }
+}
+
 // y (=, or +=) the sum of the K splits' partials, in split order.
 __global__ void k_splitk_sum(const float *__restrict__ ws, int splits, long long count, float *__restrict__ y,
                              int accumulate)
@@ -497,6 +731,119 @@ static cudaError_t launch_bn(const QgemmArgs &a, int bn, cudaStream_t st)
     }
 }
 
+// ---------------------------------------------------------------- TMA path
+size_t qgemm_tma_smem_bytes(int bn)
+{
+    const int st = qg_stages(bn), rs = qt_raw_stages(bn);
+    return 1024 + (size_t)st * (QG_A_BYTES + (size_t)bn * 128) + (size_t)rs * QT_RAW_BYTES + (2 * st + 2 * rs + 1) * 8 +
+           8 + 4 * st;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// The layouts the TMA path reads: Q4_0 in 16-row tiles, and a short last
+// segment (if any) of at least 8 units, so every box's inner extent (128
+// bytes of codes, 16 of scales) fits the segment's row.  CATS_QGEMM_TMA=0
+// keeps the load-fed kernel (tuning).
+static bool tma_layout_ok(const WeightLayout &L)
+{
+    static const bool enabled = [] {
+        const char *e = getenv("CATS_QGEMM_TMA");
+        return !(e && atoi(e) == 0);
+    }();
+    if (!enabled || L.type != W_Q4_0 || L.R != 16 || L.units % 2) return false;
+    const int tail = L.units % MV_SEG_UNITS;
+    return (tail == 0 || tail >= 8) && encode_fn() != nullptr;
+}
+
+// 4-D map over the tile layout: dim 0 the bytes of one row's part of a
+// segment, dim 1 the 16 rows of a tile, dim 2 the segments, dim 3 the tiles.
+static bool encode4(CUtensorMap *m, const void *base, uint64_t d0, uint64_t stride1, uint64_t d2, uint64_t stride2,
+                    uint64_t d3, uint64_t stride3, uint32_t box0, bool swizzle)
+{
+    const cuuint64_t dims[4] = {d0, 16, d2, d3};
+    const cuuint64_t strides[3] = {stride1, stride2, stride3};
+    const cuuint32_t box[4] = {box0, 16, 1, 8};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The four maps of a weight, encoded once per (address, layout) and kept.
+static bool tma_maps(const WeightLayout &L, const uint8_t *w, QgemmTmaArgs &a)
+{
+    using Key = std::tuple<const void *, int, int, int, unsigned long long>;
+    static std::map<Key, std::array<CUtensorMap, 4>> cache;
+    static std::mutex mu;
+    const Key key{w, L.n, L.d, L.units, (unsigned long long)L.tile_bytes};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it == cache.end()) {
+        std::array<CUtensorMap, 4> m;
+        const int full = L.units / MV_SEG_UNITS, tail = L.units % MV_SEG_UNITS;
+        const uint64_t fs = (uint64_t)std::max(full, 1);
+        const uint32_t code_row = MV_SEG_UNITS * 16, scale_row = (uint32_t)round_up(MV_SEG_UNITS * 2, 16);
+        bool ok = encode4(&m[0], w, code_row, code_row, fs, L.full_chunk, L.n_tiles, L.tile_bytes, 128, true) &&
+                  encode4(&m[1], w + (size_t)16 * code_row, scale_row, scale_row, fs, L.full_chunk, L.n_tiles,
+                          L.tile_bytes, 16, false);
+        if (ok && tail) {
+            const uint8_t *tb = w + (size_t)full * L.full_chunk;
+            const uint32_t crow = (uint32_t)tail * 16, srow = (uint32_t)round_up((size_t)tail * 2, 16);
+            ok = encode4(&m[2], tb, crow, crow, 1, L.last_chunk, L.n_tiles, L.tile_bytes, 128, true) &&
+                 encode4(&m[3], tb + (size_t)16 * crow, srow, srow, 1, L.last_chunk, L.n_tiles, L.tile_bytes, 16, false);
+        } else {
+            m[2] = m[0];
+            m[3] = m[1];
+        }
+        if (!ok) return false;
+        it = cache.emplace(key, m).first;
+    }
+    a.codes = it->second[0];
+    a.scales = it->second[1];
+    a.codes_tail = it->second[2];
+    a.scales_tail = it->second[3];
+    a.full_segs = L.units / MV_SEG_UNITS;
+    return true;
+}
+
+template <int BN>
+static cudaError_t launch_tma_t(const QgemmTmaArgs &a, cudaStream_t st)
+{
+    static unsigned long long attr = 0;   // one bit per device
+    const size_t smem = qgemm_tma_smem_bytes(BN);
+    cudaError_t e = once_per_device(attr, [smem] {
+        return cudaFuncSetAttribute(k_qgemm_tma<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
+    if (e) return e;
+    dim3 grid(cdiv(a.T, BN), cdiv(a.d, QG_M), a.splits);
+    k_qgemm_tma<BN><<<grid, QT_THREADS, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_tma_bn(const QgemmTmaArgs &a, int bn, cudaStream_t st)
+{
+    switch (bn) {
+    case 256: return launch_tma_t<256>(a, st);
+    case 128: return launch_tma_t<128>(a, st);
+    case 64: return launch_tma_t<64>(a, st);
+    case 32: return launch_tma_t<32>(a, st);
+    default: return launch_tma_t<16>(a, st);
+    }
+}
+
 bool qgemm_supported(const WeightLayout &L)
 {
     return (L.type == W_Q4_0 || L.type == W_Q8_0) && L.n % QG_K == 0 && L.units % 2 == 0;
@@ -541,7 +888,26 @@ cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __ha
     a.kper = cdiv(ksteps, splits);
     a.ws = ws;
     const int bn = pick_bn(T);
-    cudaError_t e = L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
+    cudaError_t e;
+    QgemmTmaArgs ta;
+    if (tma_layout_ok(L) && tma_maps(L, w, ta)) {
+        // K splits start on raw-stage boundaries (4 slices): the scale copy's
+        // first coordinate is then 16-byte aligned
+        ta.kper = (int)round_up((size_t)cdiv(ksteps, splits), QT_GROUP);
+        ta.splits = splits = cdiv(ksteps, ta.kper);
+        ta.n = L.n;
+        ta.d = L.d;
+        ta.T = T;
+        ta.Tpad = a.Tpad;
+        ta.accumulate = a.accumulate;
+        ta.x = x16;
+        ta.y = y;
+        ta.ws = ws;
+        ta.err = err;
+        e = launch_tma_bn(ta, bn, st);
+    } else {
+        e = L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
+    }
     if (e || splits == 1) return e;
     if (defer) {   // the caller's next kernel adds the partials
         *defer = SplitOut{ws, splits};

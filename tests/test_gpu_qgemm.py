@@ -89,3 +89,25 @@ def test_qgemm_refuses_f32_weights(mm):
             mm.qgemm(w, np.zeros((2, 64), np.float32), 2, 64, 16)
     finally:
         mm.unregister_weight(w)
+
+
+# Q4_0 weights in 16-row tiles (registered weights of 4736 rows and more,
+# and every model weight) take the path that brings raw weight bytes in with
+# tensor-map copies (four K slices a stage): full segments; a short last
+# segment of 24 units (11008) and of exactly 8 (4352); a last segment too
+# short for it (4160: 2 units, the load-fed kernel); ragged rows past the
+# last 128-row tile; K splits that start on four-slice boundaries; 1 to 512
+# tokens.
+TMA_SHAPES = [(4096, 8192, 16), (11008, 8192, 16), (4096, 5000, 512), (28672, 4736, 100), (4352, 4800, 40),
+              (4160, 4800, 16), (11008, 4864, 1), (8192, 4736, 256), (2048, 6000, 33)]
+
+
+@pytest.mark.parametrize("n,d,T", TMA_SHAPES)
+def test_qgemm_tma_path_matches_exact_product(mm, orc, n, d, T):
+    w, x, ref = _case(orc, Q4_0, n, d, T, n * 11 + d + T)
+    mm.register_weight(w, Q4_0, n, d)
+    try:
+        y = mm.qgemm(w, x, T, n, d)
+    finally:
+        mm.unregister_weight(w)
+    assert rel(y, ref) < TOL, rel(y, ref)

@@ -20,8 +20,10 @@ e2e   : tokens/s through the public C API cats_gpu_llama2_transformer(token,
         pos, m, logits) — token/pos copied in, the logits copied out, every step.
 roofline : that kernel (it is the whole step): algorithmic bytes (every weight
         once per step + the K/V rows attention reads) / its event-timed duration.
-cpu_baseline : the reference's own CPU step (oracle/_ref, all cores) on a
-        bounded sample (1- and 2-layer models of the same shapes, extrapolated).
+cpu_baseline : the reference's own CPU step (oracle/_ref, OpenMP on every
+        host core) on the full model at its own context, 12 real greedy
+        steps after the prompt (a model larger than the host's free memory:
+        a quarter and a half of its layers, per-layer slope stated).
 
 --impl reference times only that CPU reference on the same workload.
 
@@ -46,15 +48,16 @@ e2e = the host-pointer API with its copies; roofline against the 3xTF32
 tensor peak (the measured bf16 peak / 2 for tf32 / 3 products per fp32
 product), since both run on k_sgemm_tc; cpu_baseline = the reference's gemm_rnn / layer forwards
 (oracle/_ref, OpenMP on all cores) on a bounded sample.
-With torchrun (N > 1) every rank decodes its own replica (no collective on
-the data path): value = sum over ranks, time = max over ranks.  With --tp
-the N ranks instead hold one model sharded by tensor parallelism (wq/wk/wv
-and w1/w3 by rows, wo and w2 by input columns, the classifier by vocabulary
-rows) and decode one sequence: the per-phase kernels in a CUDA graph with an
-NCCL allreduce after wo and after w2, on the library's own communicator
+With torchrun (N > 1) the N ranks hold one model sharded by tensor
+parallelism (wq/wk/wv and w1/w3 by rows, wo and w2 by input columns, the
+classifier by vocabulary rows) and decode one sequence in the persistent
+kernel, the partial rows of wo and w2 pushed to every rank over NVLink
 (value = that sequence's tokens/s, "strong" scaling; roofline per GPU over
-the rank's weight slice).  torch.distributed then runs on gloo and only
-shares the NCCL id, aligns the ranks and takes the max of their times.
+the rank's weight slice).  Before timing, rank 0 runs the same model
+unsharded and the line's `parity` compares the prompt steps' logits.
+torch.distributed runs on gloo and only shares the NCCL id, aligns the
+ranks and takes the max of their times.  --replicas runs N independent
+copies instead (value = the tokens of all ranks, "weak").
 """
 import argparse
 import json

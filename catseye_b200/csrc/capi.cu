@@ -474,6 +474,8 @@ struct cats_gpu_llm {
     int engine = CATS_ENGINE_PERSISTENT;
     int *tok_log = nullptr;   // device: argmax ids of generate()
     int bt_T = 0, bt_nb = 0;  // the batch set last (cats_gpu_llm_batch_set)
+    cudaEvent_t params_sent = nullptr;   // the last copy out of the pinned step parameters
+    int *err_host = nullptr;              // pinned: the device error word, read with the logits
 };
 
 cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg)
@@ -492,6 +494,9 @@ cats_gpu_llm *cats_gpu_llm_create(const cats_gpu_llm_config *cfg)
     if (c.tp_size > 1) h->engine = CATS_ENGINE_GRAPH;
     int rc = llm_alloc(&h->m, c);
     if (rc == CATS_OK && cudaMalloc(&h->tok_log, (size_t)(c.seq_len + 1) * 4) != cudaSuccess) rc = CATS_ERR_NOMEM;
+    if (rc == CATS_OK && (cudaEventCreateWithFlags(&h->params_sent, cudaEventDisableTiming) != cudaSuccess ||
+                          cudaMallocHost(&h->err_host, 4) != cudaSuccess))
+        rc = CATS_ERR_CUDA;
     if (rc != CATS_OK) {
         fail(rc, "cats_gpu_llm_create");
         llm_free(&h->m);
@@ -507,6 +512,8 @@ void cats_gpu_llm_destroy(cats_gpu_llm *h)
     if (h->m.stream) cudaStreamSynchronize(h->m.stream);
     llm_free(&h->m);
     if (h->tok_log) cudaFree(h->tok_log);
+    if (h->params_sent) cudaEventDestroy(h->params_sent);
+    if (h->err_host) cudaFreeHost(h->err_host);
     delete h;
 }
 
@@ -642,15 +649,17 @@ int cats_gpu_llm_set_position(cats_gpu_llm *h, int token, int pos)
 {
     if (!h || token < 0 || token >= h->m.c.vocab || pos < 0 || pos >= h->m.c.seq_len)
         return fail(CATS_ERR_ARG, "cats_gpu_llm_set_position");
-    // the pinned staging struct may still be the source of an earlier async copy
-    if (check(cudaStreamSynchronize(h->m.stream), "cats_gpu_llm_set_position")) return g.last_err;
+    // the pinned staging struct may still be the source of the previous copy
+    if (check(cudaEventSynchronize(h->params_sent), "cats_gpu_llm_set_position")) return g.last_err;
     StepParams *p = h->m.params_host;
     p->token = token;
     p->pos = pos;
     p->next = 0;
     p->steps = 0;
-    return check(cudaMemcpyAsync(h->m.params, p, sizeof(StepParams), cudaMemcpyHostToDevice, h->m.stream),
-                 "cats_gpu_llm_set_position");
+    if (check(cudaMemcpyAsync(h->m.params, p, sizeof(StepParams), cudaMemcpyHostToDevice, h->m.stream),
+              "cats_gpu_llm_set_position"))
+        return g.last_err;
+    return check(cudaEventRecord(h->params_sent, h->m.stream), "cats_gpu_llm_set_position");
 }
 
 float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *h, float *logits_host)
@@ -661,12 +670,12 @@ float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *h, float *l
     if (cats_gpu_llm_set_position(h, token, pos)) return nullptr;
     LlmModel &m = h->m;
     if (run_steps(h, 1, nullptr, what)) return nullptr;
+    // the logits and the error word come back in one wait
     if (check(cudaMemcpyAsync(m.logits_host, m.logits, (size_t)m.c.vocab * 4, cudaMemcpyDeviceToHost, m.stream), what))
         return nullptr;
+    if (check(cudaMemcpyAsync(h->err_host, m.err, 4, cudaMemcpyDeviceToHost, m.stream), what)) return nullptr;
     if (check(cudaStreamSynchronize(m.stream), what)) return nullptr;
-    int e = 0;
-    cudaMemcpy(&e, m.err, 4, cudaMemcpyDeviceToHost);
-    if (e) { cudaMemset(m.err, 0, 4); fail(CATS_ERR_TIMEOUT, what); return nullptr; }
+    if (*h->err_host) { cudaMemset(m.err, 0, 4); fail(CATS_ERR_TIMEOUT, what); return nullptr; }
     memcpy(logits_host, m.logits_host, (size_t)m.c.vocab * 4);
     return logits_host;
 }

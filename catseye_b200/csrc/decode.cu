@@ -1041,8 +1041,13 @@ int decode_prepare(LlmModel *m)
 template <int WT, bool TP>
 static cudaError_t launch_decode_t(const DecodeArgs &a, size_t smem, int grid, cudaStream_t st)
 {
-    cudaError_t e = cudaFuncSetAttribute(k_decode<WT, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // the largest dynamic shared memory a CTA may take, raised once per device
+    static unsigned long long attr = 0;
+    cudaError_t e = once_per_device(attr, [] {
+        return cudaFuncSetAttribute(k_decode<WT, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    });
     if (e) return e;
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(DEC_THREADS);

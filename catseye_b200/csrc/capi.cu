@@ -217,7 +217,12 @@ int cats_gpu_init(int device)
     cudaDeviceProp prop;
     if (check(cudaGetDeviceProperties(&prop, device), "cats_gpu_init")) return g.last_err;
     if (prop.major != 10) return fail(CATS_ERR_UNSUPPORTED, "cats_gpu_init: libcatsgpu needs an sm_100 (B200) device");
-    if (check(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "cats_gpu_init")) return g.last_err;
+    // A blocking stream: the device-pointer entry points called with stream
+    // NULL run here, ordered after the caller's work on the legacy default
+    // stream (where the caller's inputs were most likely written) and before
+    // its later work there.  A non-blocking stream let a product start before
+    // the kernels writing its operands had finished.
+    if (check(cudaStreamCreateWithFlags(&g.stream, cudaStreamDefault), "cats_gpu_init")) return g.last_err;
     if (check(cudaMalloc(&g.d_err, 4), "cats_gpu_init")) return g.last_err;
     cudaMemset(g.d_err, 0, 4);
     g.device = device;

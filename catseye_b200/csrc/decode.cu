@@ -546,6 +546,10 @@ __device__ __forceinline__ bool run_matvec(const DecodeArgs &a, const Smem &sm, 
             }
         }
     }
+    if (a.trace && ns_first == 0) {   // no tile for this CTA's first group: zero-length wait and dots
+        ns_first = ns_dots = global_ns();
+        ck_first = ck_dots = clock64();
+    }
     trace_put(a, tk, ns_first, ck_first);
     trace_put(a, tk, ns_dots, ck_dots);
     return ok;
@@ -989,7 +993,11 @@ int decode_prepare(LlmModel *m)
             if (!add(*w)) return E_UNSUPPORTED;
     if (!add(m->cls)) return E_UNSUPPORTED;
     slot = (uint32_t)round_up(slot, 128);
-    const uint32_t xs = (uint32_t)round_up(c.wtype == W_F32 ? (size_t)maxn * 4 : (size_t)(maxn / 32) * 40, 128);
+    // the staged activations, and room for the one-CTA-per-head attention's
+    // scratch (which reuses them): a sharded model's short slices would
+    // otherwise leave short contexts on the split attention
+    const size_t act = c.wtype == W_F32 ? (size_t)maxn * 4 : (size_t)(maxn / 32) * 40;
+    const uint32_t xs = (uint32_t)round_up(std::max(act, (size_t)local_attn_scratch_bytes(m->head_size)), 128);
     // tensor parallelism: the rows of the CTA's tiles of wo / w2 (dim rows) and
     // of the classifier slice, held until they are pushed
     uint32_t push = 0;

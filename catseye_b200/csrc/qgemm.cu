@@ -382,7 +382,13 @@ constexpr uint32_t QT_CODE_BYTES = QG_M * 128;   // 128 rows x 4 slices x 32 byt
 constexpr uint32_t QT_SCALE_BYTES = QG_M * 16;   // 128 rows x 4 slices x 2 blocks x 2 bytes
 constexpr uint32_t QT_RAW_BYTES = QT_CODE_BYTES + QT_SCALE_BYTES;
 
-__host__ __device__ constexpr int qt_raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 6; }
+// Stages of the TMA-fed kernel: fp16 operand stages and raw weight stages.
+// Wide tiles (prefill) run one CTA per SM with deep rings; tiles of up to 64
+// tokens (batched decode) are sized so two CTAs share an SM (<= 113 KB each):
+// at small T a product is one wave of (M tile, K split) units fitted to two
+// CTAs per SM, and one CTA per SM would run it in two.
+__host__ __device__ constexpr int qt_stages(int bn) { return bn >= 128 ? qg_stages(bn) : 3; }
+__host__ __device__ constexpr int qt_raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : bn >= 32 ? 2 : 3; }
 
 struct QgemmTmaArgs {
     CUtensorMap codes, scales;             // full segments
@@ -407,7 +413,7 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
 template <int BN>
 __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_constant__ QgemmTmaArgs a)
 {
-    constexpr int ST = qg_stages(BN);
+    constexpr int ST = qt_stages(BN);
     constexpr int RS = qt_raw_stages(BN);
     constexpr uint32_t B_BYTES = BN * 128;
     constexpr uint32_t STAGE = QG_A_BYTES + B_BYTES;
@@ -684,12 +690,15 @@ static int resident_per_sm(int type, int bn)
 // K splits for a product: when the (N tile, M tile) grid leaves SMs idle or
 // ends in a partial wave, splitting K gives every SM work.  The estimate
 // weighs waves of K slices against the partials' extra traffic.
-static int pick_splits(int type, int n, int d, int T)
+static int resident_for(const WeightLayout &L, int bn);
+
+static int pick_splits(const WeightLayout &L, int T)
 {
     const int bn = pick_bn(T);
+    const int n = L.n, d = L.d;
     const int ksteps = n / QG_K;
     const long long tiles = (long long)cdiv(d, QG_M) * cdiv(T, bn);
-    const long long slots = 148LL * resident_per_sm(type, bn);
+    const long long slots = 148LL * resident_for(L, bn);
     const double t_k = 0.4e-6 * std::max(bn, 64) / 256.0 + 0.05e-6;   // seconds per K slice of one CTA
     int best = 1;
     double best_t = 1e30;
@@ -706,7 +715,7 @@ static int pick_splits(int type, int n, int d, int T)
 size_t qgemm_workspace_bytes(const WeightLayout &L, int T)
 {
     if (T <= 0 || !qgemm_supported(L)) return 0;
-    const int s = pick_splits(L.type, L.n, L.d, T);
+    const int s = pick_splits(L, T);
     return s > 1 ? (size_t)s * T * L.d * 4 : 0;
 }
 
@@ -734,7 +743,7 @@ static cudaError_t launch_bn(const QgemmArgs &a, int bn, cudaStream_t st)
 // ---------------------------------------------------------------- TMA path
 size_t qgemm_tma_smem_bytes(int bn)
 {
-    const int st = qg_stages(bn), rs = qt_raw_stages(bn);
+    const int st = qt_stages(bn), rs = qt_raw_stages(bn);
     return 1024 + (size_t)st * (QG_A_BYTES + (size_t)bn * 128) + (size_t)rs * QT_RAW_BYTES + (2 * st + 2 * rs + 1) * 8 +
            8 + 4 * st;
 }
@@ -820,16 +829,54 @@ static bool tma_maps(const WeightLayout &L, const uint8_t *w, QgemmTmaArgs &a)
 }
 
 template <int BN>
+static cudaError_t prepare_tma_t(int *per_sm)
+{
+    const size_t smem = qgemm_tma_smem_bytes(BN);
+    cudaError_t e = cudaFuncSetAttribute(k_qgemm_tma<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_qgemm_tma<BN>, QT_THREADS, smem);
+}
+
+static cudaError_t prepare_tma_bn(int bn, int *per_sm)
+{
+    switch (bn) {
+    case 256: return prepare_tma_t<256>(per_sm);
+    case 128: return prepare_tma_t<128>(per_sm);
+    case 64: return prepare_tma_t<64>(per_sm);
+    case 32: return prepare_tma_t<32>(per_sm);
+    default: return prepare_tma_t<16>(per_sm);
+    }
+}
+
+// CTAs of a TMA-fed instance resident per SM, queried once per device and
+// instance (raising its shared-memory limit on the way).
+static int resident_tma(int bn)
+{
+    static int cache[5][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int bi = bn == 256 ? 0 : bn == 128 ? 1 : bn == 64 ? 2 : bn == 32 ? 3 : 4;
+    int spare = 0;
+    int &c = dev >= 0 && dev < 64 ? cache[bi][dev] : spare;
+    if (c == 0) {
+        int n = 0;
+        c = (prepare_tma_bn(bn, &n) == cudaSuccess && n > 0) ? n : 1;
+    }
+    return c;
+}
+
+// the residency of the kernel a weight's products run on
+static int resident_for(const WeightLayout &L, int bn)
+{
+    return tma_layout_ok(L) ? resident_tma(bn) : resident_per_sm(L.type, bn);
+}
+
+template <int BN>
 static cudaError_t launch_tma_t(const QgemmTmaArgs &a, cudaStream_t st)
 {
-    static unsigned long long attr = 0;   // one bit per device
-    const size_t smem = qgemm_tma_smem_bytes(BN);
-    cudaError_t e = once_per_device(attr, [smem] {
-        return cudaFuncSetAttribute(k_qgemm_tma<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    });
-    if (e) return e;
+    resident_tma(BN);   // raises the kernel's shared-memory limit once per device
     dim3 grid(cdiv(a.T, BN), cdiv(a.d, QG_M), a.splits);
-    k_qgemm_tma<BN><<<grid, QT_THREADS, smem, st>>>(a);
+    k_qgemm_tma<BN><<<grid, QT_THREADS, qgemm_tma_smem_bytes(BN), st>>>(a);
     return cudaGetLastError();
 }
 
@@ -882,7 +929,7 @@ cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __ha
     a.accumulate = accumulate ? 1 : 0;
     a.err = err;
     const int ksteps = L.n / QG_K;
-    int splits = pick_splits(L.type, L.n, L.d, T);
+    int splits = pick_splits(L, T);
     if (splits > 1 && (!ws || ws_bytes < (size_t)splits * T * L.d * 4)) splits = 1;   // no room: one pass over K
     a.splits = splits;
     a.kper = cdiv(ksteps, splits);

@@ -294,7 +294,10 @@ void cats_sgemm(char ta, char tb, int m, int n, int k, float alpha, const float 
 void cats_gemm_rnn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C);
 void cats_gemm_rnt(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C);
 void cats_gemm_rtn(int M, int N, int K, float alpha, float *A, float *B, float beta, float *C);
-/* Device pointers with explicit leading dimensions. */
+/* Device pointers with explicit leading dimensions.  stream: the CUDA stream
+ * to queue on; NULL = the library's own stream, which is ordered with the
+ * legacy default stream (it starts after work queued there and later work
+ * there waits for it), as are the other *_dev entry points given NULL. */
 int cats_sgemm_dev(char ta, char tb, int m, int n, int k, float alpha, const float *a, int lda,
                    const float *b, int ldb, float beta, float *c, int ldc, void *stream);
 

@@ -26,6 +26,8 @@ pytestmark = pytest.mark.gpu
 
 # GQA (16 query heads over 8 kv heads) that shards over 2, 4 and 8 ranks
 CFG = dict(dim=512, hidden=1536, n_layers=2, n_heads=16, n_kv_heads=8, vocab=4096, seq_len=64)
+# the 70B shapes, one layer and a cut vocabulary
+CFG70 = dict(dim=8192, hidden=28672, n_layers=1, n_heads=64, n_kv_heads=8, vocab=8192, seq_len=64)
 FEED = [3, 17, 400, 4095, 5, 123, 77, 9]
 SEED = 31
 PERSISTENT, GRAPH = 0, 1
@@ -56,7 +58,7 @@ def _batch_run(m):
     return [row.copy() for row in lg], [int(t) for t in np.asarray(gen).reshape(-1)]
 
 
-def _rank(rank, world, port, wtype, batched, engine, out):
+def _rank(rank, world, port, cfg, wtype, batched, engine, out):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -65,7 +67,7 @@ def _rank(rank, world, port, wtype, batched, engine, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         _lib.init(rank)
-        m = llm.GpuLLM(llm.LlmConfig(**CFG, wtype=wtype), rank, world)
+        m = llm.GpuLLM(llm.LlmConfig(**cfg, wtype=wtype), rank, world)
         m.tp_connect(llm.tp_share_id())
         p2p = m.tp_persistent()          # the peers were mapped (every rank on its own GPU)
         m.set_engine(engine)
@@ -80,12 +82,12 @@ def _rank(rank, world, port, wtype, batched, engine, out):
         dist.destroy_process_group()
 
 
-def _sharded(wtype, world=2, batched=False, engine=PERSISTENT):
+def _sharded(wtype, world=2, batched=False, engine=PERSISTENT, cfg=CFG):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, wtype, batched, engine, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, cfg, wtype, batched, engine, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -146,6 +148,29 @@ def test_sharded_decode_matches_one_gpu_and_reference(one_gpu_runs, world, engin
     for r in range(1, world):
         assert res[0][1] == res[r][1]
         assert all(np.array_equal(a, b) for a, b in zip(res[0][0], res[r][0])), r
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_sharded_70b_shapes_fp32(gpu, world):
+    """The 70B shapes sharded (dim 8192, hidden 28672 in 3584-row slices at 8
+    ranks, 64 query heads over 8 kv heads: one kv head per rank at 8), one
+    layer, fp32 weights, so only the fp32 order of the partial sums differs
+    from the unsharded model: every rank's logits within 1e-4 at every step
+    and the same greedy tokens."""
+    _need(world)
+    from catseye_b200 import llm
+    one = llm.GpuLLM(llm.LlmConfig(**CFG70, wtype=0))
+    one.init_random(SEED)
+    ref, ref_toks = _decode_run(one)
+    one.close()
+    res = _sharded(0, world, cfg=CFG70)
+    for r, (logits, toks, p2p) in res.items():
+        assert p2p
+        errs = [rel(a, b) for a, b in zip(logits, ref)]
+        print("rank", r, "max logit error %.2e" % max(errs))
+        assert max(errs) < 1e-4, (r, errs)
+        assert [int(np.argmax(a)) for a in logits] == [int(np.argmax(b)) for b in ref]
+        assert toks == ref_toks, r
 
 
 def test_two_rank_batched_step_matches_one_gpu(gpu):

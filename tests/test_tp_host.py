@@ -1,8 +1,12 @@
 """Host logic of tensor parallelism on CPU (gloo, world size 2): every rank
-receives rank 0's unique id, and the sharding rule refuses shapes whose
-slices do not fall on 32-element blocks."""
+receives rank 0's unique id; a rank whose peer never reaches the handshake
+gives up with an error after the group's timeout instead of waiting for
+good; and the sharding rule refuses shapes whose slices do not fall on
+32-element blocks."""
+import datetime
 import os
 import socket
+import time
 
 import pytest
 import torch.multiprocessing as mp
@@ -41,6 +45,45 @@ def test_unique_id_reaches_every_rank():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert res[0] == res[1] == bytes(range(128))
+
+
+def _absent_peer_rank(rank, world, port, out, done):
+    """Rank 1 joins the group and then never takes part in the handshake (a
+    rank stuck or lost before it); rank 0 runs the handshake and reports how
+    it ended."""
+    import torch.distributed as dist
+    from catseye_b200.llm import tp_share_id
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 0:
+        t0 = time.monotonic()
+        try:
+            tp_share_id(make_id=lambda: bytes(128))
+            out.put(("returned", time.monotonic() - t0))
+        except Exception as e:   # the group's timeout: the handshake gives up
+            out.put((type(e).__name__, time.monotonic() - t0))
+    else:
+        done.wait(120)   # alive but silent until rank 0 has its answer
+    os._exit(0)          # no collective teardown with a peer that never answered
+
+
+def test_handshake_gives_up_when_a_peer_never_arrives():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    done = ctx.Event()
+    port = _free_port()
+    procs = [ctx.Process(target=_absent_peer_rank, args=(r, 2, port, q, done)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        how, waited = q.get(timeout=120)
+    finally:
+        done.set()
+        for p in procs:
+            p.join(timeout=60)
+    assert how != "returned", "the handshake completed without its peer"
+    assert waited < 60, waited
 
 
 @pytest.mark.parametrize("dim,heads,kv,hidden,tp,ok", [

@@ -48,6 +48,8 @@ SIGNATURES = {
     "cats_gpu_quantize_q8_dev": (_i, [_vp, _vp, _i, _i, _vp]),
     "cats_gpu_qgemm_dev": (_i, [_vp, _vp, _vp, _i, _vp]),
     "cats_gpu_qgemm": (_i, [_vp, _vp, _vp, _i]),
+    "cats_gpu_qgemm_plan": (_i, [_vp, _i, _vp]),
+    "cats_gpu_qgemm_trace": (_i, [_vp, _vp, _vp, _i, _vp, _i]),
     "cats_gpu_dequantize_dev": (_i, [_i, _vp, _vp, _i, _i, _vp]),
     "cats_gpu_llm_create": (_vp, [C.POINTER(LlmConfigC)]),
     "cats_gpu_llm_destroy": (None, [_vp]),

@@ -436,6 +436,52 @@ int cats_gpu_qgemm_dev(const void *w, const float *d_x, float *d_y, int T, void 
     return check(launch_qgemm(r.W.L, r.W.ptr, d_x, g.d_x16, d_y, T, g.d_ws, g.cap_ws, g.d_err, st), what);
 }
 
+int cats_gpu_qgemm_plan(const void *w, int T, int *plan)
+{
+    const char *what = "cats_gpu_qgemm_plan";
+    if (!ensure_init()) return g.last_err;
+    auto it = g.weights.find(w);
+    if (it == g.weights.end() || !plan || T <= 0) return fail(CATS_ERR_ARG, what);
+    if (!qgemm_supported(it->second.W.L)) return fail(CATS_ERR_UNSUPPORTED, what);
+    const QgemmPlan p = qgemm_plan(it->second.W.L, T);
+    plan[0] = p.bn;
+    plan[1] = p.splits;
+    plan[2] = p.resident;
+    plan[3] = p.tma;
+    plan[4] = p.kper;
+    plan[5] = p.occupancy;
+    plan[6] = p.occupancy_err;
+    return CATS_OK;
+}
+
+int cats_gpu_qgemm_trace(const void *w, const float *d_x, float *d_y, int T, unsigned long long *trace_host,
+                         int trace_slices)
+{
+    const char *what = "cats_gpu_qgemm_trace";
+    if (!ensure_init()) return g.last_err;
+    auto it = g.weights.find(w);
+    if (it == g.weights.end()) return fail(CATS_ERR_ARG, "cats_gpu_qgemm_trace: weight not registered");
+    Reg &r = it->second;
+    if (!d_x || !d_y || T <= 0 || ((uintptr_t)d_x % 16) || !trace_host || trace_slices <= 0)
+        return fail(CATS_ERR_ARG, what);
+    if (!qgemm_supported(r.W.L)) return fail(CATS_ERR_UNSUPPORTED, what);
+    if (grow((void **)&g.d_x16, &g.cap_x16, qgemm_x16_bytes(r.n, T))) return g.last_err;
+    const size_t wsb = qgemm_workspace_bytes(r.W.L, T);
+    if (wsb && grow((void **)&g.d_ws, &g.cap_ws, wsb)) return g.last_err;
+    const size_t tb = (size_t)(trace_slices + 1) * QG_TRACE_FIELDS * 8;
+    unsigned long long *d_tr = nullptr;
+    if (check(cudaMalloc(&d_tr, tb), what)) return g.last_err;
+    QgemmTrace tr;
+    tr.buf = d_tr;
+    tr.slices = trace_slices;
+    int rc = check(cudaMemsetAsync(d_tr, 0, tb, g.stream), what);
+    if (!rc) rc = check(launch_qgemm(r.W.L, r.W.ptr, d_x, g.d_x16, d_y, T, g.d_ws, g.cap_ws, g.d_err, g.stream, &tr), what);
+    if (!rc) rc = check(cudaMemcpyAsync(trace_host, d_tr, tb, cudaMemcpyDeviceToHost, g.stream), what);
+    if (!rc) rc = check(cudaStreamSynchronize(g.stream), what);
+    cudaFree(d_tr);
+    return rc;
+}
+
 int cats_gpu_qgemm(const void *w, const float *x, float *y, int T)
 {
     const char *what = "cats_gpu_qgemm";

@@ -382,11 +382,10 @@ constexpr uint32_t QT_CODE_BYTES = QG_M * 128;   // 128 rows x 4 slices x 32 byt
 constexpr uint32_t QT_SCALE_BYTES = QG_M * 16;   // 128 rows x 4 slices x 2 blocks x 2 bytes
 constexpr uint32_t QT_RAW_BYTES = QT_CODE_BYTES + QT_SCALE_BYTES;
 
-// Stages of the TMA-fed kernel: fp16 operand stages and raw weight stages.
-// Wide tiles (prefill) run one CTA per SM with deep rings; tiles of up to 64
-// tokens (batched decode) are sized so two CTAs share an SM (<= 113 KB each):
-// at small T a product is one wave of (M tile, K split) units fitted to two
-// CTAs per SM, and one CTA per SM would run it in two.
+// Stages of the TMA-fed kernel: fp16 operand stages (weight rows and the
+// stage's activation rows) and raw weight stages.  Wide tiles (prefill) run
+// one CTA per SM with deep rings; tiles of up to 64 tokens (batched decode)
+// are sized so two CTAs share an SM (<= 113 KB each).
 __host__ __device__ constexpr int qt_stages(int bn) { return bn >= 128 ? qg_stages(bn) : 3; }
 __host__ __device__ constexpr int qt_raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : bn >= 32 ? 2 : 3; }
 
@@ -398,6 +397,8 @@ struct QgemmTmaArgs {
     const __half *x;
     float *y, *ws;
     int *err;
+    unsigned long long *trace;   // QgemmTrace: CTA (0, 0, 0)'s timeline, or null
+    int trace_slices;
 };
 
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
@@ -436,6 +437,10 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
     const int ksteps = a.n / QG_K;
     const int kbeg = z * a.kper, nk = max(0, min(ksteps, kbeg + a.kper) - kbeg);
     const int ngroups = (nk + QT_GROUP - 1) / QT_GROUP;
+    const bool tr = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+    auto stamp = [&](int k, int e) {
+        if (tr && k >= 0 && k <= a.trace_slices) a.trace[(size_t)k * QG_TRACE_FIELDS + e] = (unsigned long long)clock64();
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; s++) {
@@ -460,6 +465,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) stamp(a.trace_slices, 0);
 
     if (warp == QT_TMA_WARP) {
         // ---------------- raw weight stages through the TMA engine
@@ -478,6 +484,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
                 tma_load_4d(dst + QT_CODE_BYTES, tail ? &a.scales_tail : &a.scales, in_seg * 4, 0, tail ? 0 : seg,
                             m0 / 16, &rfull[rs]);
                 issued = g + 1;
+                if (g * QT_GROUP < a.trace_slices) stamp(g * QT_GROUP, 0);
             }
             // every copy lands before the CTA exits (the last phase of each stage)
             for (int g = max(0, issued - RS); g < issued; g++)
@@ -490,6 +497,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
                 const int s = kb % ST;
                 const uint32_t ph = (uint32_t)(kb / ST) & 1u;
                 if (!tc_wait(&full[s], ph, abort_s, a.err, CATS_DEVERR_MBAR_FULL)) break;
+                if (kb < a.trace_slices) stamp(kb, 12);
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + s * STAGE), sb = sa + QG_A_BYTES;
 #pragma unroll
@@ -506,6 +514,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                              ::"r"(smem_u32(&empty[s])) : "memory");
                 commits[s]++;
+                if (kb < a.trace_slices) stamp(kb, 13);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                          ::"r"(smem_u32(done)) : "memory");
@@ -521,9 +530,14 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
         for (int kb = 0; kb < nk; kb++) {
             const int g = kb / QT_GROUP, k4 = kb % QT_GROUP, rs = g % RS;
             if (k4 == 0 && !tc_wait(&rfull[rs], (uint32_t)(g / RS) & 1u, abort_s, a.err, CATS_DEVERR_MBAR_FULL)) break;
+            if (k4 == 0 && p == 0 && kb < a.trace_slices) stamp(kb, 2);
             if (!tc_wait(&empty[s], ph ^ 1u, abort_s, a.err, CATS_DEVERR_MBAR_EMPTY)) break;
-            uint8_t *sa = smem + s * STAGE, *sb = sa + QG_A_BYTES;
-            if (p == 0) bulk_g2s_keep(sb, a.x + ((size_t)(kbeg + kb) * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
+            if (p == 0 && kb < a.trace_slices) stamp(kb, 3);
+            uint8_t *sa = smem + s * STAGE;
+            if (p == 0) {   // the stage's activation rows, with its weights
+                bulk_g2s_keep(sa + QG_A_BYTES, a.x + ((size_t)(kbeg + kb) * a.Tpad + t0) * QG_K, B_BYTES, &full[s]);
+                if (kb < a.trace_slices) stamp(kb, 1);
+            }
             const uint8_t *rb = rawst + rs * QT_RAW_BYTES;
             RawBlk blk;
             // the codes of this slice's block: 16-byte chunk 2 k4 + h of row r, 128-byte swizzled by the copy
@@ -536,6 +550,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
                 if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
                 else mbar_arrive(&full[s]);
                 if (k4 == QT_GROUP - 1 || kb == nk - 1) mbar_arrive(&rempty[rs]);   // the warp is done with it
+                if (kb < a.trace_slices) stamp(kb, 4 + warp);
             }
             if (++s == ST) { s = 0; ph ^= 1u; }
         }
@@ -545,6 +560,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
             if (i > 64) __nanosleep(32);
         }
         if (!ok && a.err) atomicOr(a.err, CATS_DEVERR_MBAR_FULL);
+        if (p == 0) stamp(a.trace_slices, 1);
         tc_fence_after();
         if (ok && !*abort_s && nk > 0) {
             const int q = warp & 3, half = warp >> 2;
@@ -573,6 +589,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
             }
         }
     }
+    if (threadIdx.x == 0) stamp(a.trace_slices, 2);
     tc_fence_before();
     __syncthreads();
     if (warp == QG_MMA_WARP) {
@@ -682,7 +699,8 @@ static int resident_per_sm(int type, int bn)
     if (c == 0) {
         int n = 0;
         const cudaError_t e = type == W_Q4_0 ? prepare_bn<W_Q4_0>(bn, &n) : prepare_bn<W_Q8_0>(bn, &n);
-        c = (e == cudaSuccess && n > 0) ? n : 1;
+        if (e != cudaSuccess || n <= 0) return 1;   // not kept: asked again next time
+        c = n;
     }
     return c;
 }
@@ -691,6 +709,7 @@ static int resident_per_sm(int type, int bn)
 // ends in a partial wave, splitting K gives every SM work.  The estimate
 // weighs waves of K slices against the partials' extra traffic.
 static int resident_for(const WeightLayout &L, int bn);
+static bool tma_layout_ok(const WeightLayout &L);
 
 static int pick_splits(const WeightLayout &L, int T)
 {
@@ -699,11 +718,13 @@ static int pick_splits(const WeightLayout &L, int T)
     const int ksteps = n / QG_K;
     const long long tiles = (long long)cdiv(d, QG_M) * cdiv(T, bn);
     const long long slots = 148LL * resident_for(L, bn);
+    // the tensor-map path starts splits on raw-stage boundaries (4 slices)
+    const int kq = tma_layout_ok(L) ? QT_GROUP : 1;
     const double t_k = 0.4e-6 * std::max(bn, 64) / 256.0 + 0.05e-6;   // seconds per K slice of one CTA
     int best = 1;
     double best_t = 1e30;
     for (int s = 1; s <= QG_MAX_SPLITS && (s == 1 || ksteps / s >= 4); s++) {
-        const int kper = cdiv(ksteps, s);
+        const int kper = (int)round_up((size_t)cdiv(ksteps, s), kq);
         if (cdiv(ksteps, kper) != s) continue;   // every split gets work
         const double waves = (double)((tiles * s + slots - 1) / slots);
         const double t = waves * kper * t_k + (s > 1 ? 8.0 * s * T * (double)d / 5e12 : 0.0);
@@ -744,6 +765,7 @@ static cudaError_t launch_bn(const QgemmArgs &a, int bn, cudaStream_t st)
 size_t qgemm_tma_smem_bytes(int bn)
 {
     const int st = qt_stages(bn), rs = qt_raw_stages(bn);
+    // alignment slack, fp16 stages, raw stages, barriers, TMEM slot, abort flag, commit counts
     return 1024 + (size_t)st * (QG_A_BYTES + (size_t)bn * 128) + (size_t)rs * QT_RAW_BYTES + (2 * st + 2 * rs + 1) * 8 +
            8 + 4 * st;
 }
@@ -860,7 +882,8 @@ static int resident_tma(int bn)
     int &c = dev >= 0 && dev < 64 ? cache[bi][dev] : spare;
     if (c == 0) {
         int n = 0;
-        c = (prepare_tma_bn(bn, &n) == cudaSuccess && n > 0) ? n : 1;
+        if (prepare_tma_bn(bn, &n) != cudaSuccess || n <= 0) return 1;   // not kept: asked again next time
+        c = n;
     }
     return c;
 }
@@ -906,8 +929,26 @@ cudaError_t launch_x16(const float *x, __half *x16, int T, int n, cudaStream_t s
     return cudaGetLastError();
 }
 
+QgemmPlan qgemm_plan(const WeightLayout &L, int T)
+{
+    QgemmPlan p{};
+    if (T <= 0 || !qgemm_supported(L)) return p;
+    p.bn = pick_bn(T);
+    p.splits = pick_splits(L, T);
+    p.resident = resident_for(L, p.bn);
+    p.tma = tma_layout_ok(L) ? 1 : 0;
+    const int ksteps = L.n / QG_K;
+    p.kper = (int)round_up((size_t)cdiv(ksteps, p.splits), p.tma ? QT_GROUP : 1);
+    int n = 0;
+    p.occupancy_err = (int)(p.tma ? prepare_tma_bn(p.bn, &n)
+                                  : L.type == W_Q4_0 ? prepare_bn<W_Q4_0>(p.bn, &n) : prepare_bn<W_Q8_0>(p.bn, &n));
+    p.occupancy = n;
+    return p;
+}
+
 cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
-                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st, SplitOut *defer)
+                             bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st, SplitOut *defer,
+                             const QgemmTrace *trace)
 {
     if (defer) *defer = SplitOut{};
     if (T <= 0) return cudaSuccess;
@@ -951,6 +992,8 @@ cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __ha
         ta.y = y;
         ta.ws = ws;
         ta.err = err;
+        ta.trace = trace ? trace->buf : nullptr;
+        ta.trace_slices = trace ? trace->slices : 0;
         e = launch_tma_bn(ta, bn, st);
     } else {
         e = L.type == W_Q4_0 ? launch_bn<W_Q4_0>(a, bn, st) : launch_bn<W_Q8_0>(a, bn, st);
@@ -967,13 +1010,13 @@ cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __ha
 }
 
 cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
-                         float *ws, size_t ws_bytes, int *err, cudaStream_t st)
+                         float *ws, size_t ws_bytes, int *err, cudaStream_t st, const QgemmTrace *trace)
 {
     if (T <= 0) return cudaSuccess;
     if (!qgemm_supported(L)) return cudaErrorInvalidValue;
     cudaError_t e = launch_x16(x, x16, T, L.n, st);
     if (e) return e;
-    return launch_qgemm_x16(L, w, x16, y, T, false, ws, ws_bytes, err, st);
+    return launch_qgemm_x16(L, w, x16, y, T, false, ws, ws_bytes, err, st, nullptr, trace);
 }
 
 } // namespace cats

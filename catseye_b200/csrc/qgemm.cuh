@@ -62,13 +62,38 @@ struct SplitOut {
     int splits = 1;
 };
 
+// Per-K-slice timeline of CTA (0, 0, 0) of the tensor-map-fed kernel (a
+// tuning diagnostic).  buf holds (slices + 1) rows of QG_TRACE_FIELDS SM
+// clock64 stamps; row k < slices is the CTA's k-th K slice:
+//   0 the raw group copy issued (a group's first slice), 1 the activation
+//   rows' copy issued (narrow tiles), 2 producer warp 0 saw the raw group
+//   land, 3 producer warp 0 found the fp16 stage free, 4..11 producer warp
+//   0..7 arrived on the stage's full barrier, 12 the MMA thread found the
+//   operands ready, 13 it issued the slice's commit;
+// row `slices`: 0 the CTA's start, 1 producer warp 0 saw the last MMA
+// complete, 2 producer warp 0 finished its epilogue.
+constexpr int QG_TRACE_FIELDS = 16;
+struct QgemmTrace {
+    unsigned long long *buf = nullptr;   // device
+    int slices = 0;
+};
+
 cudaError_t launch_qgemm_x16(const WeightLayout &L, const uint8_t *w, const __half *x16, float *y, int T,
                              bool accumulate, float *ws, size_t ws_bytes, int *err, cudaStream_t st,
-                             SplitOut *defer = nullptr);
+                             SplitOut *defer = nullptr, const QgemmTrace *trace = nullptr);
 
 // The same from fp32 x (converted into the x16 scratch, qgemm_x16_bytes, first).
 cudaError_t launch_qgemm(const WeightLayout &L, const uint8_t *w, const float *x, __half *x16, float *y, int T,
-                         float *ws, size_t ws_bytes, int *err, cudaStream_t st);
+                         float *ws, size_t ws_bytes, int *err, cudaStream_t st, const QgemmTrace *trace = nullptr);
+
+// The plan a product of L at T tokens runs with: token tile, K splits (before
+// any cap by the workspace), CTAs of the chosen kernel resident per SM,
+// whether the weights come through tensor-map copies, K slices per split.
+struct QgemmPlan {
+    int bn, splits, resident, tma, kper;
+    int occupancy, occupancy_err;   // the occupancy query asked afresh, and its CUDA error
+};
+QgemmPlan qgemm_plan(const WeightLayout &L, int T);
 
 size_t qgemm_smem_bytes(int bn);
 

@@ -246,3 +246,22 @@ def qgemm_dev(w, x, y, T, stream=None):
     lib = _lib.init()
     _lib.check(lib.cats_gpu_qgemm_dev(_p(w), _dp(x), _dp(y), T, stream), "cats_gpu_qgemm_dev")
     return y
+
+
+def qgemm_plan(w, T):
+    """(token tile, K splits, CTAs resident per SM, tensor-map-fed, K slices per split,
+    occupancy asked afresh, its CUDA error)."""
+    lib = _lib.init()
+    plan = np.zeros(7, np.int32)
+    _lib.check(lib.cats_gpu_qgemm_plan(_p(w), T, _p(plan)), "cats_gpu_qgemm_plan")
+    return tuple(int(v) for v in plan)
+
+
+def qgemm_trace(w, x, y, T, slices):
+    """Runs the product once on device tensors x (T x n) and y (T x d);
+    returns CTA (0, 0, 0)'s clock64 stamps, (slices + 1) x 16 (see
+    cats_gpu_qgemm_trace)."""
+    lib = _lib.init()
+    tr = np.zeros((slices + 1) * 16, np.uint64)
+    _lib.check(lib.cats_gpu_qgemm_trace(_p(w), _dp(x), _dp(y), T, _p(tr), slices), "cats_gpu_qgemm_trace")
+    return tr.reshape(slices + 1, 16)

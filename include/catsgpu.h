@@ -125,6 +125,22 @@ int cats_gpu_matvec_dev(const void *w, float *d_out, const void *d_x, int x_is_q
  * cats_gpu_qgemm takes host pointers and returns after the copy back. */
 int cats_gpu_qgemm_dev(const void *w, const float *d_x, float *d_y, int T, void *stream);
 int cats_gpu_qgemm(const void *w, const float *x, float *y, int T);
+/* Tuning diagnostics of the batched product for a registered weight at T
+ * tokens.  cats_gpu_qgemm_plan: plan[0..6] = token tile, K splits, CTAs of
+ * the kernel resident per SM, 1 if the weights come through tensor-map
+ * copies, K slices per split, and the occupancy query asked afresh with its
+ * CUDA error code.  cats_gpu_qgemm_trace: runs the product once
+ * (d_x device, T x n fp32; d_y device, T x d) on the library's stream, with
+ * CTA (0, 0, 0) of the tensor-map-fed kernel stamping its SM clock at each
+ * step of its first trace_slices K slices; trace_host receives
+ * (trace_slices + 1) x 16 values: per slice k, [k*16 + 0] raw weight copy
+ * issued, 1 activation copy issued, 2 raw copy seen landed, 3 fp16 stage
+ * free, 4..11 producer warps 0..7 done, 12 operands ready at the MMA
+ * thread, 13 its commit issued; row trace_slices: 0 start, 1 last MMA seen
+ * complete, 2 epilogue done.  Zero = not stamped. */
+int cats_gpu_qgemm_plan(const void *w, int T, int *plan);
+int cats_gpu_qgemm_trace(const void *w, const float *d_x, float *d_y, int T, unsigned long long *trace_host,
+                         int trace_slices);
 /* quantize_q8 on device buffers; scalar_mode selects the plain-C build's
  * rounding (llm/catseye_llm.h:227-251). */
 int cats_gpu_quantize_q8_dev(int8_t *d_q, const float *d_x, int n, int scalar_mode, void *stream);

@@ -29,9 +29,10 @@ def _case(orc, t, n, d, T, seed):
 # (n, d, T): full 128 x 256 tiles; ragged rows and tokens; a partial last
 # 64-block segment (11008 = 5 x 2048 + 768); the smallest shapes; grids small
 # enough that K is split across CTAs (long K, few rows: 16 splits; the 7B w2
-# shape at batch 16).  T <= 32 with n a multiple of 256 runs the narrow-tile
-# kernel (four K slices per stage): 16 and 32 tokens, 17 (ragged tokens in a
-# 32-wide tile), one token, and d = 1000 (a last tile whose rows + 32 i run out)
+# shape at batch 16); 16 and 32 tokens, 17 (ragged tokens in a 32-wide
+# tile), one token, and d = 1000 (a last 128-row tile that runs out).  These
+# registered weights have fewer than 4736 rows, so their tile layout is not
+# the 16-row one and they run on the kernel that loads weights itself.
 SHAPES = [(4096, 4096, 512), (4096, 1000, 16), (11008, 4096, 100), (64, 128, 1), (8192, 256, 300),
           (2048, 11008, 33), (128, 17, 7), (28672, 256, 16), (11008, 4096, 16), (4096, 2048, 32),
           (8192, 640, 17), (4096, 256, 1)]
@@ -111,3 +112,34 @@ def test_qgemm_tma_path_matches_exact_product(mm, orc, n, d, T):
     finally:
         mm.unregister_weight(w)
     assert rel(y, ref) < TOL, rel(y, ref)
+
+
+def test_qgemm_plan_and_slice_timeline(mm, orc):
+    """The plan the library reports for a 16-row-tile Q4_0 weight (tensor-map
+    fed, K splits on four-slice boundaries), and the per-slice timeline of
+    one product: every stamped slice's events in their causal order (warp 0
+    finds the stage free before it arrives, the MMA thread finds the
+    operands ready after that and commits after that; each warp's own stamp
+    follows its arrival, so it may trail the MMA thread's), the product's
+    result still exact."""
+    import torch
+    n, d, T = 4096, 4736, 16
+    w, x, ref = _case(orc, Q4_0, n, d, T, 77)
+    mm.register_weight(w, Q4_0, n, d)
+    try:
+        bn, splits, resident, tma, kper, occ, occ_err = mm.qgemm_plan(w, T)
+        assert (bn, tma) == (16, 1) and splits >= 1 and resident >= 1 and occ_err == 0
+        assert kper % 4 == 0 and splits * kper >= n // 64 > (splits - 1) * kper
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty((T, d), device="cuda")
+        torch.cuda.synchronize()
+        slices = min(8, kper)
+        tr = mm.qgemm_trace(w, xd, yd, T, slices).astype(np.int64)
+        assert rel(yd.cpu().numpy(), ref) < TOL
+        for k in range(slices):
+            free, done0, ready, commit = tr[k, 3], tr[k, 4], tr[k, 12], tr[k, 13]
+            assert 0 < free <= done0 and free < ready <= commit, (k, tr[k])
+            assert tr[k, 4:12].min() > 0, (k, tr[k])
+        assert tr[slices, 0] <= tr[0, 3] and tr[slices, 1] <= tr[slices, 2]
+    finally:
+        mm.unregister_weight(w)

@@ -716,7 +716,7 @@ int cats_gpu_llm_set_position(cats_gpu_llm *h, int token, int pos)
 float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *h, float *logits_host)
 {
     const char *what = "cats_gpu_llama2_transformer";
-    if (!h || !logits_host) { fail(CATS_ERR_ARG, what); return nullptr; }
+    if (!h) { fail(CATS_ERR_ARG, what); return nullptr; }
     if (ensure_graph(h)) return nullptr;
     if (cats_gpu_llm_set_position(h, token, pos)) return nullptr;
     LlmModel &m = h->m;
@@ -727,6 +727,7 @@ float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *h, float *l
     if (check(cudaMemcpyAsync(h->err_host, m.err, 4, cudaMemcpyDeviceToHost, m.stream), what)) return nullptr;
     if (check(cudaStreamSynchronize(m.stream), what)) return nullptr;
     if (*h->err_host) { cudaMemset(m.err, 0, 4); fail(CATS_ERR_TIMEOUT, what); return nullptr; }
+    if (!logits_host) return m.logits_host;   // the model's own copy, as the reference returns s->logits
     memcpy(logits_host, m.logits_host, (size_t)m.c.vocab * 4);
     return logits_host;
 }

@@ -66,6 +66,7 @@ class GpuLLM:
             _lib.check(None, "cats_gpu_llm_create")
             raise _lib.CatsGpuError("cats_gpu_llm_create failed")
         self._logits = np.zeros(cfg.vocab, dtype=np.float32)
+        self._view, self._view_ptr = None, None
 
     @classmethod
     def load(cls, path, tp_rank=0, tp_size=1, seq_len=0):
@@ -83,6 +84,7 @@ class GpuLLM:
             _lib.check(None, "cats_gpu_llm_load")
             raise _lib.CatsGpuError("cats_gpu_llm_load failed")
         self._logits = np.zeros(self.cfg.vocab, dtype=np.float32)
+        self._view, self._view_ptr = None, None
         return self
 
     def set_weights(self, mw):
@@ -101,13 +103,21 @@ class GpuLLM:
         _lib.check(self.lib.cats_gpu_llm_tp_connect(self.h, buf), "tp_connect")
 
     def step(self, token, pos, out=None):
-        """cats_llama2_transformer(token, pos): logits of this step (host numpy)."""
-        out = self._logits if out is None else out
-        p = self.lib.cats_gpu_llama2_transformer(token, pos, self.h, C.c_void_p(out.ctypes.data))
+        """cats_llama2_transformer(token, pos): logits of this step (host numpy).
+        Into `out` when given; otherwise a view of the model's own page-locked
+        copy, which the model's next step overwrites (copy it to keep it), as
+        the reference returns its state's logits array."""
+        p = self.lib.cats_gpu_llama2_transformer(token, pos, self.h,
+                                                 None if out is None else C.c_void_p(out.ctypes.data))
         if not p:
             _lib.check(None, "llama2_transformer")
             raise _lib.CatsGpuError("llama2_transformer failed")
-        return out
+        if out is not None:
+            return out
+        if self._view is None or self._view_ptr != p:
+            self._view = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), shape=(self.cfg.vocab,))
+            self._view_ptr = p
+        return self._view
 
     def generate(self, token, pos, steps):
         """Greedy decode fully on the device; returns the argmax ids of the steps."""

@@ -189,7 +189,10 @@ cats_gpu_llm *cats_gpu_llm_load(const char *path, int tp_rank, int tp_size, int 
 int cats_gpu_llm_init_random(cats_gpu_llm *m, unsigned long long seed, float std);
 /* One decode step, cats_llama2_transformer(token, pos, m) (llm/catseye_llm.h:
  * 1625-1772): token and pos go in, the logits come back in logits_host
- * (vocab floats).  Returns logits_host, or NULL on error. */
+ * (vocab floats).  Returns logits_host, or NULL on error.  With logits_host
+ * NULL it returns the model's own host copy of the logits (page-locked,
+ * overwritten by the model's next step), as the reference returns its state's
+ * logits array (:1772), and copies nothing more. */
 float *cats_gpu_llama2_transformer(int token, int pos, cats_gpu_llm *m, float *logits_host);
 /* Device-resident greedy decoding: run `steps` steps starting at (token, pos),
  * each step's argmax (sample_argmax, :1944-1956) feeding the next, with no

@@ -25,6 +25,11 @@ cpu_baseline : the reference's own CPU step (oracle/_ref, OpenMP on every
         steps after the prompt (a model larger than the host's free memory:
         a quarter and a half of its layers, per-layer slope stated).
 
+vs_baseline : value / the reference's own published decode rate of the same
+        model shape and weight type (llm/README.md:259: Llama-2-7B-chat GGUF
+        Q4_0, 5.47 tok/s on a CPU whose hardware it does not state), named in
+        vs_baseline_of; null for the workloads it publishes nothing for.
+
 --impl reference times only that CPU reference on the same workload.
 
 --workload llama70b_q4_0_prefill512 | llama7b_q4_0_batch16 measure the
@@ -81,6 +86,15 @@ WORKLOADS = {
 }
 PROMPT = 8
 SEED = 20241201
+# The reference's own published decode rate for the same model shape and
+# weight type (CPU, hardware not stated): the denominator of vs_baseline.
+PUBLISHED = {"llama7b_q4_0": (5.47, "llm/README.md:259, Llama-2-7B-chat GGUF Q4_0 decode on a CPU")}
+
+
+def vs_published(args, value):
+    """value / the published rate of this exact workload (full layer count), else None."""
+    pub = PUBLISHED.get(args.workload)
+    return round(value / pub[0], 2) if pub and not args.layers else None
 
 
 def cfg_for(workload, layers=0):
@@ -818,12 +832,16 @@ def main():
                 "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(1e3 / cb["value"], 3), "higher_is_better": True,
                 "scaling": "strong" if ws > 1 and not args.replicas else "weak",
-                "vs_baseline": None, "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)",
+                "vs_baseline": vs_published(args, cb["value"]),
+                "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)",
                                                8: "q8_0 x q8"}[cfg.wtype],
                 "data": "synthetic", "config": decode_config(args, cfg, ws, ws > 1 and not args.replicas),
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+        if line["vs_baseline"] is not None:
+            line["vs_baseline_of"] = {"value": PUBLISHED[args.workload][0], "unit": "tok/s",
+                                      "source": PUBLISHED[args.workload][1]}
         print(json.dumps(line))
         return
 
@@ -849,7 +867,7 @@ def main():
     line = {
         "metric": "decode tok/s (batch 1)", "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": vs_published(args, tok_s),
         "dtype": {0: "f32", 2: "q4_0 x q8 (int8 dot, f32 accumulate)", 8: "q8_0 x q8"}[cfg.wtype],
         "data": "synthetic",
         "config": decode_config(args, cfg, ws, tp),
@@ -874,6 +892,9 @@ def main():
         line["parity"] = r["parity"]
     if not args.no_cpu_baseline and ws == 1:
         line["cpu_baseline"] = cpu_reference(cfg, "reference")
+    if line["vs_baseline"] is not None:
+        line["vs_baseline_of"] = {"value": PUBLISHED[args.workload][0], "unit": "tok/s",
+                                  "source": PUBLISHED[args.workload][1]}
     print(json.dumps(line))
     if dist:
         dist.destroy_process_group()

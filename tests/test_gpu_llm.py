@@ -154,6 +154,29 @@ def test_random_init_model_runs_and_is_deterministic(llm):
     assert np.array_equal(outs[0], outs[1])
 
 
+def test_step_into_buffer_or_the_models_own_copy(llm):
+    """cats_gpu_llama2_transformer with a host buffer fills it; with NULL it
+    returns the model's own page-locked copy (the same pointer every step,
+    overwritten by the next one), as the reference returns its state's
+    logits.  Both forms give the same logits on twin models."""
+    cfg = llm.LlmConfig(dim=512, hidden=1376, n_layers=2, n_heads=8, n_kv_heads=2, vocab=4096, seq_len=64,
+                        wtype=Q4_0)
+    a, b = llm.GpuLLM(cfg), llm.GpuLLM(cfg)
+    a.init_random(99)
+    b.init_random(99)
+    buf = np.zeros(cfg.vocab, np.float32)
+    views = []
+    for pos, tok in enumerate([3, 17, 400, 9]):
+        v = a.step(tok, pos)
+        got = b.step(tok, pos, out=buf)
+        assert got is buf
+        assert np.array_equal(v, buf), pos
+        views.append(v)
+    assert all(v is views[0] for v in views)   # one view of the model's own array
+    a.close()
+    b.close()
+
+
 def _synth_weights(llm, cfg, seed):
     """Download the device generator's tensors for an oracle run."""
     class W:

@@ -55,11 +55,18 @@ def _absent_peer_rank(rank, world, port, out, done):
     from catseye_b200.llm import tp_share_id
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    try:
+        # the rendezvous waits as long as the slowest process takes to start;
+        # the handshake runs on a group of its own with a short timeout
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=3))
+    except Exception as e:
+        out.put(("setup failed: " + repr(e), 0.0))
+        os._exit(0)
     if rank == 0:
         t0 = time.monotonic()
         try:
-            tp_share_id(make_id=lambda: bytes(128))
+            tp_share_id(group=group, make_id=lambda: bytes(128))
             out.put(("returned", time.monotonic() - t0))
         except Exception as e:   # the group's timeout: the handshake gives up
             out.put((type(e).__name__, time.monotonic() - t0))
@@ -82,6 +89,7 @@ def test_handshake_gives_up_when_a_peer_never_arrives():
         done.set()
         for p in procs:
             p.join(timeout=60)
+    assert not how.startswith("setup failed"), how
     assert how != "returned", "the handshake completed without its peer"
     assert waited < 60, waited
 

@@ -384,10 +384,15 @@ constexpr uint32_t QT_RAW_BYTES = QT_CODE_BYTES + QT_SCALE_BYTES;
 
 // Stages of the TMA-fed kernel: fp16 operand stages (weight rows and the
 // stage's activation rows) and raw weight stages.  Wide tiles (prefill) run
-// one CTA per SM with deep rings; tiles of up to 64 tokens (batched decode)
-// are sized so two CTAs share an SM (<= 113 KB each).
-__host__ __device__ constexpr int qt_stages(int bn) { return bn >= 128 ? qg_stages(bn) : 3; }
-__host__ __device__ constexpr int qt_raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : bn >= 32 ? 2 : 3; }
+// one CTA per SM with deep rings; tiles of 32 and 64 tokens are sized so two
+// CTAs share an SM (<= 113 KB each), 16-token tiles so three do (~74 KB
+// each).  A CTA's K slice is paced by its own chain (producers, then the one
+// MMA thread, then the commit's return), so more CTAs per SM beat deeper
+// rings: same-box A/B of the batch-16 step, 2 + 2 stages at three CTAs per
+// SM against 3 + 3 at two, 3526 -> 3772 tok/s (w1/w3 49.2 -> 40.0 us);
+// eight stages at one CTA per SM was slower than either.
+__host__ __device__ constexpr int qt_stages(int bn) { return bn >= 128 ? qg_stages(bn) : bn == 16 ? 2 : 3; }
+__host__ __device__ constexpr int qt_raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 2; }
 
 struct QgemmTmaArgs {
     CUtensorMap codes, scales;             // full segments

@@ -62,7 +62,7 @@ def _absent_peer_rank(rank, world, port, out, done):
         group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=3))
     except Exception as e:
         out.put(("setup failed: " + repr(e), 0.0))
-        os._exit(0)
+        _flush_exit(out)
     if rank == 0:
         t0 = time.monotonic()
         try:
@@ -72,7 +72,14 @@ def _absent_peer_rank(rank, world, port, out, done):
             out.put((type(e).__name__, time.monotonic() - t0))
     else:
         done.wait(120)   # alive but silent until rank 0 has its answer
-    os._exit(0)          # no collective teardown with a peer that never answered
+    _flush_exit(out)     # no collective teardown with a peer that never answered
+
+
+def _flush_exit(out):
+    """Exit at once, after the queue's feeder thread has written what was put."""
+    out.close()
+    out.join_thread()
+    os._exit(0)
 
 
 def test_handshake_gives_up_when_a_peer_never_arrives():

@@ -365,8 +365,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
 // ---------------------------------------------------------------------------
 // Q4_0 weights through the tensor-memory-access engine.  The producers above
 // fetch weight words with ordinary loads, which cap near 8 GB/s per SM (the
-// few bytes one SM keeps in flight at the loaded latency); at small T that is
-// the bound.  Here a warp of its own (the TMA warp) brings 4 K slices of a
+// few bytes one SM keeps in flight at the loaded latency).  Here a warp of
+// its own (the TMA warp) brings 4 K slices of a
 // 128-row tile at a time straight from the matvec's tile layout into a ring
 // of raw stages: the codes with one 4-D tensor-map copy (128 bytes of each
 // row's segment x 16 rows x 1 segment x 8 tiles, 128-byte swizzled so the
@@ -374,7 +374,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
 // bytes x 16 x 1 x 8).  A weight whose last segment is short has a second
 // pair of maps for that segment; coordinates past its end read zeros.  The
 // producers dequantize from shared memory as before; the MMA warp and the
-// epilogue are unchanged.
+// epilogue are unchanged.  With the weights off the producers' path, a K
+// slice is paced by the CTA's own chain (the producers' dequantization, the
+// one MMA thread's issue, the commit's return to the producers: ~0.5 us at
+// 16 and at 512 tokens, against 0.28 us of tensor work for a 128 x 256 x 64
+// slice), which the stage counts below trade against CTAs per SM.
 constexpr int QT_THREADS = QG_PROD + 64;      // + the MMA warp + the TMA warp
 constexpr int QT_TMA_WARP = QG_MMA_WARP + 1;
 constexpr int QT_GROUP = 4;                    // K slices per raw stage

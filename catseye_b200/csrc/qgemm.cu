@@ -132,27 +132,33 @@ __device__ __forceinline__ __half2 u2h(uint32_t v) { return *reinterpret_cast<__
 //  an fma with 1/16 (exact); the word shifted by 8 gives the odd elements.
 //  Q8_0: the int8 codes of bytes (4i, 4i+2) and (4i+1, 4i+3) of each plane
 //  with the sign bit flipped are code + 128, exact as 1024 + that.
+// One Q4_0 code word (4 bytes: elements 4i..4i+3 in the low nibbles and
+// 16+4i.. in the high ones) to its 16-byte chunk of fp16 values in the x16
+// element order: the masked nibbles OR-ed into the exponent of 1024 are
+// 1024 + q (or 1024 + 16q, scaled back exactly by 1/16), so (q - 8) d is one
+// rounding of exact operands.
+__device__ __forceinline__ uint4 q4_word_fp16(uint32_t w, __half2 d2)
+{
+    const __half2 lo_bias = __float2half2_rn(1032.f);      // 1024 + the code offset 8
+    const __half2 sixteenth = __float2half2_rn(0.0625f);
+    const __half2 hi_bias = __float2half2_rn(-72.f);       // -(64 + 8)
+    const uint32_t w8 = w >> 8;
+    const uint32_t l02 = (w & 0x000F000Fu) | 0x64006400u, l13 = (w8 & 0x000F000Fu) | 0x64006400u;
+    const uint32_t g02 = (w & 0x00F000F0u) | 0x64006400u, g13 = (w8 & 0x00F000F0u) | 0x64006400u;
+    return make_uint4(h2u(__hmul2(__hsub2(u2h(l02), lo_bias), d2)), h2u(__hmul2(__hsub2(u2h(l13), lo_bias), d2)),
+                      h2u(__hmul2(__hfma2(u2h(g02), sixteenth, hi_bias), d2)),
+                      h2u(__hmul2(__hfma2(u2h(g13), sixteenth, hi_bias), d2)));
+}
+
 template <int WT>
 __device__ __forceinline__ void dequant_store(const RawBlk &raw, uint8_t *tile, const uint32_t (&off)[4])
 {
     const uint16_t sb = (uint16_t)(raw.sc & 0xffff);
     const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
     if (WT == W_Q4_0) {
-        const __half2 lo_bias = __float2half2_rn(1032.f);      // 1024 + the code offset 8
-        const __half2 sixteenth = __float2half2_rn(0.0625f);
-        const __half2 hi_bias = __float2half2_rn(-72.f);       // -(64 + 8)
         const uint32_t wv[4] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t w = wv[i], w8 = w >> 8;
-            const uint32_t l02 = (w & 0x000F000Fu) | 0x64006400u, l13 = (w8 & 0x000F000Fu) | 0x64006400u;
-            const uint32_t g02 = (w & 0x00F000F0u) | 0x64006400u, g13 = (w8 & 0x00F000F0u) | 0x64006400u;
-            const uint4 o = make_uint4(h2u(__hmul2(__hsub2(u2h(l02), lo_bias), d2)),
-                                       h2u(__hmul2(__hsub2(u2h(l13), lo_bias), d2)),
-                                       h2u(__hmul2(__hfma2(u2h(g02), sixteenth, hi_bias), d2)),
-                                       h2u(__hmul2(__hfma2(u2h(g13), sixteenth, hi_bias), d2)));
-            *reinterpret_cast<uint4 *>(tile + off[i]) = o;
-        }
+        for (int i = 0; i < 4; i++) *reinterpret_cast<uint4 *>(tile + off[i]) = q4_word_fp16(wv[i], d2);
     } else {
         const __half2 bias = __float2half2_rn(1152.f);          // 1024 + 128
         const uint32_t lo[4] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w};
@@ -379,8 +385,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
 // one MMA thread's issue, the commit's return to the producers: ~0.5 us at
 // 16 and at 512 tokens, against 0.28 us of tensor work for a 128 x 256 x 64
 // slice), which the stage counts below trade against CTAs per SM.
-constexpr int QT_THREADS = QG_PROD + 64;      // + the MMA warp + the TMA warp
-constexpr int QT_TMA_WARP = QG_MMA_WARP + 1;
+// Producer warps: 16 for the wide tiles (one CTA per SM; each thread takes
+// half a block per K slice, which halves the producers' link of a slice's
+// chain), 8 for the narrow ones (one block per thread; two or three CTAs per
+// SM, whose registers leave no room for more).  Then the MMA warp, then the
+// TMA warp.
+__host__ __device__ constexpr int qt_prod_warps(int bn) { return bn >= 128 ? 16 : 8; }
+__host__ __device__ constexpr int qt_threads(int bn) { return qt_prod_warps(bn) * 32 + 64; }
 constexpr int QT_GROUP = 4;                    // K slices per raw stage
 constexpr uint32_t QT_CODE_BYTES = QG_M * 128;   // 128 rows x 4 slices x 32 bytes
 constexpr uint32_t QT_SCALE_BYTES = QG_M * 16;   // 128 rows x 4 slices x 2 blocks x 2 bytes
@@ -421,8 +432,10 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
 }
 
 template <int BN>
-__global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_constant__ QgemmTmaArgs a)
+__global__ void __launch_bounds__(qt_threads(BN), 1) k_qgemm_tma(const __grid_constant__ QgemmTmaArgs a)
 {
+    constexpr int NPW = qt_prod_warps(BN);          // producer warps
+    constexpr int MMA_WARP = NPW, TMA_WARP = NPW + 1;
     constexpr int ST = qt_stages(BN);
     constexpr int RS = qt_raw_stages(BN);
     constexpr uint32_t B_BYTES = BN * 128;
@@ -453,19 +466,19 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; s++) {
-            mbar_init(&full[s], QG_PROD / 32);
+            mbar_init(&full[s], NPW);
             mbar_init(&empty[s], 1);
         }
         for (int s = 0; s < RS; s++) {
             mbar_init(&rfull[s], 1);
-            mbar_init(&rempty[s], QG_PROD / 32);   // every producer warp, after its last read of the stage
+            mbar_init(&rempty[s], NPW);   // every producer warp, after its last read of the stage
         }
         mbar_init(done, 1);
         *abort_s = 0;
         for (int s = 0; s < ST; s++) commits[s] = 0;
         fence_barrier_init();
     }
-    if (warp == QG_MMA_WARP) {
+    if (warp == MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TCOLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -476,7 +489,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 0) stamp(a.trace_slices, 0);
 
-    if (warp == QT_TMA_WARP) {
+    if (warp == TMA_WARP) {
         // ---------------- raw weight stages through the TMA engine
         if (lane == 0) {
             int issued = 0;
@@ -499,7 +512,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
             for (int g = max(0, issued - RS); g < issued; g++)
                 mbar_wait_bounded(&rfull[g % RS], (uint32_t)(g / RS) & 1u, nullptr, 0);
         }
-    } else if (warp == QG_MMA_WARP) {
+    } else if (warp == MMA_WARP) {
         if (lane == 0) {
             const uint32_t idesc = umma_idesc(0, QG_M, BN);
             for (int kb = 0; kb < nk; kb++) {
@@ -529,11 +542,16 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
                          ::"r"(smem_u32(done)) : "memory");
         }
     } else {
-        // ---------------- producers: thread p dequantizes block p & 1 of row p >> 1 from the raw stage
-        const int p = threadIdx.x, r = p >> 1, h = p & 1;
-        uint32_t off[4];
+        // ---------------- producers: from the raw stage, thread p dequantizes
+        // block h of row r (8 warps), or half qh of it (16 warps: code words
+        // 2 qh and 2 qh + 1, the chunks they fill)
+        constexpr int NW = NPW == 16 ? 2 : 4;   // code words per thread
+        const int p = threadIdx.x;
+        const int r = NPW == 16 ? p >> 2 : p >> 1, h = NPW == 16 ? (p >> 1) & 1 : p & 1;
+        const int qh = NPW == 16 ? p & 1 : 0;
+        uint32_t off[NW];
 #pragma unroll
-        for (int i = 0; i < 4; i++) off[i] = sw128(r, 4 * h + i);
+        for (int i = 0; i < NW; i++) off[i] = sw128(r, 4 * h + NW * qh + i);
         int s = 0;
         uint32_t ph = 0;
         for (int kb = 0; kb < nk; kb++) {
@@ -548,18 +566,27 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
                 if (kb < a.trace_slices) stamp(kb, 1);
             }
             const uint8_t *rb = rawst + rs * QT_RAW_BYTES;
-            RawBlk blk;
             // the codes of this slice's block: 16-byte chunk 2 k4 + h of row r, 128-byte swizzled by the copy
-            blk.w[0] = *reinterpret_cast<const uint4 *>(rb + r * 128 + (((2 * k4 + h) ^ (r & 7)) << 4));
-            blk.sc = *reinterpret_cast<const unsigned short *>(rb + QT_CODE_BYTES + r * 16 + k4 * 4 + h * 2);
-            dequant_store<W_Q4_0>(blk, sa, off);
+            const uint8_t *cw = rb + r * 128 + (((2 * k4 + h) ^ (r & 7)) << 4);
+            const unsigned short sb = *reinterpret_cast<const unsigned short *>(rb + QT_CODE_BYTES + r * 16 + k4 * 4 + h * 2);
+            const __half2 d2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
+            if constexpr (NW == 4) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(cw);
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) *reinterpret_cast<uint4 *>(sa + off[i]) = q4_word_fp16(wv[i], d2);
+            } else {
+                const uint2 w = *reinterpret_cast<const uint2 *>(cw + 8 * qh);
+                *reinterpret_cast<uint4 *>(sa + off[0]) = q4_word_fp16(w.x, d2);
+                *reinterpret_cast<uint4 *>(sa + off[1]) = q4_word_fp16(w.y, d2);
+            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
                 if (p == 0) mbar_arrive_expect_tx(&full[s], B_BYTES);
                 else mbar_arrive(&full[s]);
                 if (k4 == QT_GROUP - 1 || kb == nk - 1) mbar_arrive(&rempty[rs]);   // the warp is done with it
-                if (kb < a.trace_slices) stamp(kb, 4 + warp);
+                if (kb < a.trace_slices && warp < 8) stamp(kb, 4 + warp);
             }
             if (++s == ST) { s = 0; ph ^= 1u; }
         }
@@ -572,13 +599,16 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
         if (p == 0) stamp(a.trace_slices, 1);
         tc_fence_after();
         if (ok && !*abort_s && nk > 0) {
-            const int q = warp & 3, half = warp >> 2;
+            // warp w reads TMEM lanes 32 (w & 3) .. + 31 (its quarter of the
+            // rows) over part w >> 2 of the columns
+            constexpr int PARTS = NPW / 4, PCOLS = BN / PARTS;
+            const int q = warp & 3, part = warp >> 2;
             const int orow = m0 + q * 32 + lane;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
             float *out = a.splits > 1 ? a.ws + (size_t)z * a.T * a.d : a.y;
             const bool acc = a.splits == 1 && a.accumulate;
 #pragma unroll 1
-            for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 8) {
+            for (int c0 = part * PCOLS; c0 < (part + 1) * PCOLS; c0 += 8) {
                 uint32_t v[8];
                 asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
@@ -601,7 +631,7 @@ __global__ void __launch_bounds__(QT_THREADS, 1) k_qgemm_tma(const __grid_consta
     if (threadIdx.x == 0) stamp(a.trace_slices, 2);
     tc_fence_before();
     __syncthreads();
-    if (warp == QG_MMA_WARP) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
     }
@@ -865,7 +895,7 @@ static cudaError_t prepare_tma_t(int *per_sm)
     const size_t smem = qgemm_tma_smem_bytes(BN);
     cudaError_t e = cudaFuncSetAttribute(k_qgemm_tma<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_qgemm_tma<BN>, QT_THREADS, smem);
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_qgemm_tma<BN>, qt_threads(BN), smem);
 }
 
 static cudaError_t prepare_tma_bn(int bn, int *per_sm)
@@ -908,7 +938,7 @@ static cudaError_t launch_tma_t(const QgemmTmaArgs &a, cudaStream_t st)
 {
     resident_tma(BN);   // raises the kernel's shared-memory limit once per device
     dim3 grid(cdiv(a.T, BN), cdiv(a.d, QG_M), a.splits);
-    k_qgemm_tma<BN><<<grid, QT_THREADS, qgemm_tma_smem_bytes(BN), st>>>(a);
+    k_qgemm_tma<BN><<<grid, qt_threads(BN), qgemm_tma_smem_bytes(BN), st>>>(a);
     return cudaGetLastError();
 }
 
